@@ -1,0 +1,392 @@
+// extract.cu — threshold → event-stream extraction, replica expansion and the
+// event gather / scatter.  Semantics follow the reference extension
+// csrc/extract/extract_events_cuda.cu (count_base_kernel :192-208,
+// fill_base_kernel :226-312, build_logical_cu_kernel :449-467,
+// expand_events_direct_kernel :482-509, gather/scatter :629-662); the design
+// is our own:
+//   pass 1  one warp per base channel reads the row once (coalesced 128 B
+//           loads, 32 in flight per lane), ballots 32 positions at a time and
+//           writes a 1-bit-per-position mask plus the channel count;
+//   pass 2  one CTA scans the counts into cu_seqlens and the max;
+//   pass 3  one warp per channel turns mask words into (ch, t, k) with a warp
+//           prefix sum for positions and a warp max-scan for the previous t.
+// The row is read once (the reference reads it twice) and the fill pass reads
+// L/8 bytes of mask instead of the L*sizeof(T) input row.
+#include "common.cuh"
+
+namespace bcm {
+namespace {
+
+constexpr int kCountWarps = 4;   // warps per CTA in the count pass
+constexpr int kFillWarps = 4;
+
+// ---- pass 1: threshold + bitmask + count ---------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kCountWarps * 32)
+threshold_mask_kernel(const T* __restrict__ x, int64_t n_rows, int L, int n_words,
+                      float thr, uint32_t* __restrict__ mask,
+                      int32_t* __restrict__ counts) {
+    const int lane = lane_id();
+    const int64_t row = (int64_t)blockIdx.x * kCountWarps + (threadIdx.x >> 5);
+    if (row >= n_rows) return;
+    const T* xr = x + row * (int64_t)L;
+    uint32_t* mr = mask + row * (int64_t)n_words;
+    int cnt = 0;
+    for (int w0 = 0; w0 < n_words; w0 += 32) {
+        // 32 words = 1024 positions per iteration; lane j keeps word w0 + j.
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int t = (w0 + j) * 32 + lane;
+            v[j] = (t < L) ? to_f32<T>(xr[t]) : -INFINITY;
+        }
+        uint32_t mine = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            // NaN > thr is false, like the reference's float compare.
+            const uint32_t b = __ballot_sync(kFull, v[j] > thr);
+            if (lane == j) mine = b;
+        }
+        if (w0 + lane < n_words) {
+            mr[w0 + lane] = mine;
+            cnt += __popc(mine);
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) cnt += __shfl_xor_sync(kFull, cnt, off);
+    if (lane == 0) counts[row] = cnt;
+}
+
+// ---- pass 2: exclusive scan of counts into cu_seqlens + max ----------------
+constexpr int kScanThreads = 1024;
+
+__global__ void __launch_bounds__(kScanThreads)
+counts_scan_kernel(const int32_t* __restrict__ counts, int64_t n,
+                   int32_t* __restrict__ cu, int32_t* __restrict__ max_out) {
+    __shared__ int s_warp_sum[32];
+    __shared__ int s_warp_max[32];
+    const int tid = threadIdx.x;
+    const int64_t per = (n + kScanThreads - 1) / kScanThreads;
+    const int64_t beg = min((int64_t)tid * per, n);
+    const int64_t end = min(beg + per, n);
+    int local = 0, lmax = 0;
+    for (int64_t i = beg; i < end; ++i) {
+        const int c = counts[i];
+        local += c;
+        lmax = max(lmax, c);
+    }
+    // block exclusive scan of `local`
+    int incl = warp_inclusive_sum(local);
+    int wmax = lmax;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) wmax = max(wmax, __shfl_xor_sync(kFull, wmax, off));
+    const int warp = tid >> 5, lane = tid & 31;
+    if (lane == 31) s_warp_sum[warp] = incl;
+    if (lane == 0) s_warp_max[warp] = wmax;
+    __syncthreads();
+    if (warp == 0) {
+        int s = s_warp_sum[lane];
+        int m = s_warp_max[lane];
+        int si = warp_inclusive_sum(s);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) m = max(m, __shfl_xor_sync(kFull, m, off));
+        s_warp_sum[lane] = si - s;  // exclusive
+        if (lane == 0) *max_out = m;
+    }
+    __syncthreads();
+    int run = s_warp_sum[warp] + incl - local;  // exclusive prefix for this thread
+    if (tid == 0) cu[0] = 0;
+    for (int64_t i = beg; i < end; ++i) {
+        run += counts[i];
+        cu[i + 1] = run;
+    }
+}
+
+// ---- pass 3: mask words → (ch, t, k) ---------------------------------------
+__global__ void __launch_bounds__(kFillWarps * 32)
+mask_fill_kernel(const uint32_t* __restrict__ mask, const int32_t* __restrict__ cu,
+                 int64_t n_rows, int L, int n_words,
+                 int32_t* __restrict__ ch_ids, int32_t* __restrict__ t_steps,
+                 int32_t* __restrict__ k_flat) {
+    const int lane = lane_id();
+    const int64_t row = (int64_t)blockIdx.x * kFillWarps + (threadIdx.x >> 5);
+    if (row >= n_rows) return;
+    const uint32_t* mr = mask + row * (int64_t)n_words;
+    int pos = cu[row];       // next output slot (warp-uniform)
+    int carry_t = -1;        // t of the last event before this 1024-block
+    for (int w0 = 0; w0 < n_words; w0 += 32) {
+        const int w = w0 + lane;
+        const uint32_t word = (w < n_words) ? mr[w] : 0u;
+        const int c = __popc(word);
+        const int incl = warp_inclusive_sum(c);
+        const int total = __shfl_sync(kFull, incl, 31);
+        const int last_here = word ? (w * 32 + 31 - __clz(word)) : -1;
+        const int last_incl = warp_inclusive_max(last_here);
+        int prev = __shfl_up_sync(kFull, last_incl, 1);
+        if (lane == 0) prev = -1;
+        prev = max(prev, carry_t);
+        int p = pos + incl - c;
+        uint32_t bits = word;
+        while (bits) {
+            const int b = __ffs(bits) - 1;
+            bits &= bits - 1;
+            const int t = w * 32 + b;
+            ch_ids[p] = (int32_t)row;
+            t_steps[p] = t;
+            k_flat[p] = (prev < 0) ? (t + 1) : (t - prev);
+            prev = t;
+            ++p;
+        }
+        pos += total;
+        carry_t = max(carry_t, __shfl_sync(kFull, last_incl, 31));
+    }
+}
+
+// ---- expansion ---------------------------------------------------------------
+__global__ void build_logical_cu_kernel(const int32_t* __restrict__ base_cu, int64_t n_base,
+                                        int expand, int32_t* __restrict__ cu,
+                                        int32_t* __restrict__ max_out) {
+    const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int cnt = 0;
+    if (c < n_base) {
+        const int s = base_cu[c];
+        cnt = base_cu[c + 1] - s;
+        for (int r = 0; r < expand; ++r) cu[c * expand + r] = s * expand + r * cnt;
+    } else if (c == n_base) {
+        cu[n_base * expand] = base_cu[n_base] * expand;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) cnt = max(cnt, __shfl_xor_sync(kFull, cnt, off));
+    if (lane_id() == 0 && cnt > 0) atomicMax(max_out, cnt);
+}
+
+__global__ void expand_events_kernel(const int32_t* __restrict__ bch, const int32_t* __restrict__ bt,
+                                     const int32_t* __restrict__ bk, const int32_t* __restrict__ base_cu,
+                                     int64_t n_base_events, int64_t n_base, int expand,
+                                     int32_t* __restrict__ ch, int32_t* __restrict__ t,
+                                     int32_t* __restrict__ k) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_base_events; i += stride) {
+        const int c = bch[i];
+        if (c < 0 || c >= n_base) continue;  // malformed stream: skip, never fault
+        const int tv = bt[i], kv = bk[i];
+        const int s = base_cu[c];
+        const int cnt = base_cu[c + 1] - s;
+        const int64_t local = i - s;
+        if (local < 0 || local >= cnt) continue;  // stream inconsistent with cu_seqlens
+        for (int r = 0; r < expand; ++r) {
+            const int64_t o = (int64_t)s * expand + (int64_t)r * cnt + local;
+            ch[o] = c * expand + r;
+            t[o] = tv;
+            k[o] = kv;
+        }
+    }
+}
+
+// ---- gather / scatter -----------------------------------------------------
+template <typename T>
+__global__ void gather_kernel(const T* __restrict__ x, int64_t n_ch, int L,
+                              const int32_t* __restrict__ ch, const int32_t* __restrict__ ts,
+                              int64_t n_events, T* __restrict__ out) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_events; e += stride) {
+        const int c = ch[e], t = ts[e];
+        T v = from_f32<T>(0.f);
+        if (c >= 0 && c < n_ch && t >= 0 && t < L) v = x[(int64_t)c * L + t];
+        out[e] = v;
+    }
+}
+
+template <typename T>
+__global__ void scatter_kernel(const T* __restrict__ g, const int32_t* __restrict__ ch,
+                               const int32_t* __restrict__ ts, int64_t n_events,
+                               int64_t n_ch, int L, T* __restrict__ dx) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_events; e += stride) {
+        const int c = ch[e], t = ts[e];
+        if (c >= 0 && c < n_ch && t >= 0 && t < L) dx[(int64_t)c * L + t] = g[e];
+    }
+}
+
+inline int grid_for(int64_t n, int threads) {
+    const int64_t want = (n + threads - 1) / threads;
+    const int64_t cap = (int64_t)sm_count() * 16;
+    return (int)std::max<int64_t>(1, std::min(want, cap));
+}
+
+}  // namespace
+}  // namespace bcm
+
+using namespace bcm;
+
+extern "C" size_t bcm_extract_workspace_bytes(int64_t n_base_channels, int64_t seqlen) {
+    if (n_base_channels < 0 || seqlen < 0) return 0;
+    const int64_t words = (seqlen + 31) / 32;
+    return align_up((size_t)(n_base_channels * words * sizeof(uint32_t)), 256);
+}
+
+extern "C" bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype dtype,
+                                             int64_t n_base_channels, int64_t seqlen,
+                                             float threshold, int32_t* counts,
+                                             int32_t* cu_seqlens, int32_t* max_seqlen,
+                                             void* workspace, size_t workspace_bytes,
+                                             int64_t* n_events_host, cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(dtype_ok64(dtype), "extract_base_events: unsupported dtype %d", (int)dtype);
+    BCM_REQUIRE(n_base_channels >= 0 && seqlen >= 0, "extract_base_events: negative size");
+    BCM_REQUIRE(seqlen < (1ll << 31) && n_base_channels * seqlen < (1ll << 31) * 64,
+                "extract_base_events: sizes exceed int32 event indexing");
+    BCM_REQUIRE(cu_seqlens && max_seqlen && n_events_host, "extract_base_events: null output");
+    const size_t need = bcm_extract_workspace_bytes(n_base_channels, seqlen);
+    if (workspace_bytes < need || (need > 0 && !workspace)) {
+        set_error("extract_base_events: workspace of %zu bytes < required %zu",
+                  workspace_bytes, need);
+        return BCM_ERR_WORKSPACE;
+    }
+    BCM_CUDA_TRY(cudaMemsetAsync(max_seqlen, 0, sizeof(int32_t), stream));
+    if (n_base_channels == 0) {
+        BCM_CUDA_TRY(cudaMemsetAsync(cu_seqlens, 0, sizeof(int32_t), stream));
+        BCM_CUDA_TRY(cudaStreamSynchronize(stream));
+        *n_events_host = 0;
+        return BCM_OK;
+    }
+    BCM_REQUIRE(base_input && counts, "extract_base_events: null pointer");
+    const int L = (int)seqlen;
+    const int n_words = (L + 31) / 32;
+    uint32_t* mask = static_cast<uint32_t*>(workspace);
+    if (L == 0) {
+        BCM_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * n_base_channels, stream));
+    } else {
+        const int grid = ceil_div(n_base_channels, kCountWarps);
+        bcm_status st = dispatch_dtype64(dtype, [&](auto tag) -> bcm_status {
+            using T = decltype(tag);
+            threshold_mask_kernel<T><<<grid, kCountWarps * 32, 0, stream>>>(
+                static_cast<const T*>(base_input), n_base_channels, L, n_words, threshold,
+                mask, counts);
+            BCM_LAUNCH_CHECK();
+            return BCM_OK;
+        });
+        if (st != BCM_OK) return st;
+    }
+    counts_scan_kernel<<<1, kScanThreads, 0, stream>>>(counts, n_base_channels, cu_seqlens,
+                                                       max_seqlen);
+    BCM_LAUNCH_CHECK();
+    int32_t e_host = 0;
+    BCM_CUDA_TRY(cudaMemcpyAsync(&e_host, cu_seqlens + n_base_channels, sizeof(int32_t),
+                                 cudaMemcpyDeviceToHost, stream));
+    BCM_CUDA_TRY(cudaStreamSynchronize(stream));
+    *n_events_host = e_host;
+    return BCM_OK;
+}
+
+extern "C" bcm_status bcm_extract_base_fill(int64_t n_base_channels, int64_t seqlen,
+                                            const int32_t* cu_seqlens, const void* workspace,
+                                            size_t workspace_bytes, int32_t* ch_ids,
+                                            int32_t* t_steps, int32_t* k_flat,
+                                            cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(n_base_channels >= 0 && seqlen >= 0, "extract_base_events: negative size");
+    if (n_base_channels == 0 || seqlen == 0) return BCM_OK;
+    const size_t need = bcm_extract_workspace_bytes(n_base_channels, seqlen);
+    if (workspace_bytes < need || !workspace) {
+        set_error("extract_base_events: workspace of %zu bytes < required %zu",
+                  workspace_bytes, need);
+        return BCM_ERR_WORKSPACE;
+    }
+    BCM_REQUIRE(cu_seqlens && ch_ids && t_steps && k_flat, "extract_base_events: null pointer");
+    const int L = (int)seqlen;
+    const int n_words = (L + 31) / 32;
+    const int grid = ceil_div(n_base_channels, kFillWarps);
+    mask_fill_kernel<<<grid, kFillWarps * 32, 0, stream>>>(
+        static_cast<const uint32_t*>(workspace), cu_seqlens, n_base_channels, L, n_words,
+        ch_ids, t_steps, k_flat);
+    BCM_LAUNCH_CHECK();
+    return BCM_OK;
+}
+
+extern "C" bcm_status bcm_expand_base_events(const int32_t* base_ch_ids,
+                                             const int32_t* base_t_steps,
+                                             const int32_t* base_k_flat,
+                                             const int32_t* base_cu_seqlens,
+                                             int64_t n_base_events, int64_t n_base_channels,
+                                             int64_t expand, int32_t* ch_ids,
+                                             int32_t* t_steps, int32_t* k_flat,
+                                             int32_t* cu_seqlens, int32_t* max_seqlen,
+                                             cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(n_base_events >= 0 && n_base_channels >= 0, "expand_base_events: negative size");
+    BCM_REQUIRE(expand >= 1, "expand_base_events: expand must be >= 1");
+    BCM_REQUIRE(n_base_events * expand < (1ll << 31) && n_base_channels * expand < (1ll << 31),
+                "expand_base_events: sizes exceed int32 indexing");
+    BCM_REQUIRE(cu_seqlens && max_seqlen, "expand_base_events: null output");
+    BCM_CUDA_TRY(cudaMemsetAsync(max_seqlen, 0, sizeof(int32_t), stream));
+    if (n_base_events == 0) {
+        // Reference returns zero cu_seqlens and a zero max when nothing fires.
+        BCM_CUDA_TRY(cudaMemsetAsync(cu_seqlens, 0,
+                                     sizeof(int32_t) * (n_base_channels * expand + 1), stream));
+        return BCM_OK;
+    }
+    BCM_REQUIRE(base_ch_ids && base_t_steps && base_k_flat && base_cu_seqlens && ch_ids &&
+                    t_steps && k_flat,
+                "expand_base_events: null pointer");
+    {
+        const int threads = 256;
+        const int grid = ceil_div(n_base_channels + 1, threads);
+        build_logical_cu_kernel<<<grid, threads, 0, stream>>>(base_cu_seqlens, n_base_channels,
+                                                              (int)expand, cu_seqlens, max_seqlen);
+        BCM_LAUNCH_CHECK();
+    }
+    {
+        const int threads = 256;
+        expand_events_kernel<<<grid_for(n_base_events, threads), threads, 0, stream>>>(
+            base_ch_ids, base_t_steps, base_k_flat, base_cu_seqlens, n_base_events,
+            n_base_channels, (int)expand, ch_ids, t_steps, k_flat);
+        BCM_LAUNCH_CHECK();
+    }
+    return BCM_OK;
+}
+
+extern "C" bcm_status bcm_gather_events_fwd(const void* x, bcm_dtype dtype, int64_t n_channels,
+                                            int64_t seqlen, const int32_t* channel_ids,
+                                            const int32_t* time_steps, int64_t n_events,
+                                            void* out, cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(dtype_ok64(dtype), "gather_events_fwd: unsupported dtype %d", (int)dtype);
+    BCM_REQUIRE(n_events >= 0 && n_channels >= 0 && seqlen >= 0, "gather_events_fwd: negative size");
+    if (n_events == 0) return BCM_OK;
+    BCM_REQUIRE(x && channel_ids && time_steps && out, "gather_events_fwd: null pointer");
+    const int threads = 256;
+    return dispatch_dtype64(dtype, [&](auto tag) -> bcm_status {
+        using T = decltype(tag);
+        gather_kernel<T><<<grid_for(n_events, threads), threads, 0, stream>>>(
+            static_cast<const T*>(x), n_channels, (int)seqlen, channel_ids, time_steps, n_events,
+            static_cast<T*>(out));
+        BCM_LAUNCH_CHECK();
+        return BCM_OK;
+    });
+}
+
+extern "C" bcm_status bcm_gather_events_bwd(const void* grad, bcm_dtype dtype,
+                                            const int32_t* channel_ids,
+                                            const int32_t* time_steps, int64_t n_events,
+                                            int64_t n_channels, int64_t seqlen, void* dx,
+                                            cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(dtype_ok64(dtype), "gather_events_bwd: unsupported dtype %d", (int)dtype);
+    BCM_REQUIRE(n_events >= 0 && n_channels >= 0 && seqlen >= 0, "gather_events_bwd: negative size");
+    const size_t bytes = (size_t)n_channels * (size_t)seqlen * dtype_size(dtype);
+    if (bytes == 0) return BCM_OK;
+    BCM_REQUIRE(dx, "gather_events_bwd: null dx");
+    BCM_CUDA_TRY(cudaMemsetAsync(dx, 0, bytes, stream));
+    if (n_events == 0) return BCM_OK;
+    BCM_REQUIRE(grad && channel_ids && time_steps, "gather_events_bwd: null pointer");
+    const int threads = 256;
+    return dispatch_dtype64(dtype, [&](auto tag) -> bcm_status {
+        using T = decltype(tag);
+        scatter_kernel<T><<<grid_for(n_events, threads), threads, 0, stream>>>(
+            static_cast<const T*>(grad), channel_ids, time_steps, n_events, n_channels,
+            (int)seqlen, static_cast<T*>(dx));
+        BCM_LAUNCH_CHECK();
+        return BCM_OK;
+    });
+}

@@ -1,0 +1,104 @@
+// scan_common.cuh — layout and helpers shared by the flat-channel scan kernels.
+//
+// Thread mapping (both directions): a CTA of kScanThreads threads covers
+// kScanThreads / LPC logical channels; the LPC consecutive lanes of a channel
+// ("group") each own G of the channel's states, so LPC * G >= dstate.  Events
+// of a channel are walked sequentially (a register recurrence per state,
+// fully independent across states), so there is no block-wide scan and no
+// barrier in the inner loop; the per-event sum over states is a shuffle
+// reduction inside the group.  Parallelism comes from channels x state groups.
+#pragma once
+
+#include "common.cuh"
+
+namespace bcm {
+
+constexpr int kScanThreads = 128;
+constexpr int kChunkX = 2048;   // events per saved chunk state (x layout)
+constexpr int kCkpt = 8;        // events per backward recompute tile
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Arguments shared by the scan kernels (device-visible copy of the C ABI args).
+struct ScanArgs {
+    int n_channels, dim, dstate, n_chunks, n_events;
+    int bc_mode, b_variable, c_variable, tile_cs, n_tiles;
+    const void* u; const int32_t* k; const int32_t* cu;
+    const float* dt_idle; const float* dt_active;
+    const float* A; int64_t A_sd, A_sn;
+    const float* B; const float* C;      // depthwise: effective W_B/W_C [dim, N]
+    const float* D; const void* z; const int32_t* tile_off;
+    void* out; float* x; void* out_z;
+    const void* dout; const void* out_fwd;
+    void* du; float* dB_ev; float* dC_ev;  // per-event dB/dC (flat variable / tiled)
+    void* dz;
+    float* ws_ckpt;   // backward: recompute checkpoints
+    float* ws_part;   // backward: per-channel parameter-gradient partials
+    int part_stride;  // floats per channel in ws_part
+};
+
+// exp2 of an argument already clamped to [-126, 126]: the hardware
+// approximation is exact enough there and needs no subnormal path.
+__device__ __forceinline__ float ex2_clamped(float e) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(e));
+    return r;
+}
+
+__device__ __forceinline__ float decay_fast(float delta, float A2) {
+    return ex2_clamped(fmaxf(fminf(delta * A2, 126.0f), -126.0f));
+}
+
+// delta of an event with gap k: dt_idle*(k-1) + dt_active (one rounding, as
+// the reference's contracted expression).
+__device__ __forceinline__ float event_delta(float dt_idle, float dt_active, int k) {
+    return fmaf(dt_idle, (float)(k - 1), dt_active);
+}
+
+// Sum over the LPC lanes of a group (groups are aligned to LPC lanes).
+template <int LPC>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int off = LPC / 2; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off);
+    return v;
+}
+
+template <int LPC>
+__device__ __forceinline__ int group_max_warp(int v) {
+    // max over the whole warp (all groups), used for warp-uniform trip counts
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = max(v, __shfl_xor_sync(kFull, v, off));
+    return v;
+}
+
+__device__ __forceinline__ float silu(float z) { return z / (1.0f + expf(-z)); }
+
+// Reference event-chunk size for the tiled B/C layout: the forward kernel's
+// kNThreads*kNItems picked from max_seqlen
+// (selective_scan_fwd_kernel.cuh:771-785).
+inline int ref_chunk_size(int64_t max_seqlen) {
+    if (max_seqlen <= 128) return 128;
+    if (max_seqlen <= 256) return 256;
+    if (max_seqlen <= 512) return 512;
+    if (max_seqlen <= 1024) return 1024;
+    return 2048;
+}
+
+inline int n_chunks_for(int64_t max_seqlen) {
+    int64_t n = (max_seqlen + kChunkX - 1) / kChunkX;
+    return (int)(n < 1 ? 1 : n);
+}
+
+// Lanes per channel and states per lane for dstate N.
+inline void pick_layout(int N, int& G, int& LPC) {
+    if (N <= 128) {
+        G = 4;
+        int l = (N + 3) / 4;
+        LPC = 1;
+        while (LPC < l) LPC <<= 1;
+    } else {
+        G = 8;
+        LPC = 32;
+    }
+}
+
+}  // namespace bcm

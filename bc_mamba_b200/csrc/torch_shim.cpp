@@ -1,0 +1,543 @@
+// torch_shim.cpp — host side of the drop-in boundary.
+//
+// Mirrors the reference's pybind11 bindings argument for argument, with the
+// same validation messages and return layouts:
+//   selective_scan_cuda.fwd_flat_ch / bwd_flat_ch
+//       (csrc/selective_scan/selective_scan.cpp:674-1197)
+//   extract_events_cuda.extract_base_events / expand_base_events /
+//       gather_events_fwd / gather_events_bwd / extract_events
+//       (csrc/extract/extract_events_cuda.cu:117-179, 324-798)
+//   restore_dense_cuda_nodecay.restore_dense_fwd / restore_dense_bwd
+//       (csrc/r_nodecay/restore_dense.cpp:41-226)
+// Every device computation goes through the C ABI of libbcm_b200.so
+// (include/bcm_b200.h); this file only validates, allocates with the ATen
+// caching allocator and turns status codes into RuntimeError.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <vector>
+
+#include "bcm_b200.h"
+
+#define CHECK_SHAPE(x, ...) \
+    TORCH_CHECK(x.sizes() == torch::IntArrayRef({__VA_ARGS__}), #x " must have shape (" #__VA_ARGS__ ")")
+
+namespace {
+
+using at::Tensor;
+using c10::optional;
+
+void check_status(bcm_status st, const char* what) {
+    if (st != BCM_OK) {
+        TORCH_CHECK(false, what, ": ", bcm_last_error(), " (status ", (int)st, ")");
+    }
+}
+
+bcm_dtype to_bcm(at::ScalarType t, const char* what) {
+    switch (t) {
+        case at::ScalarType::Float: return BCM_F32;
+        case at::ScalarType::Half: return BCM_F16;
+        case at::ScalarType::BFloat16: return BCM_BF16;
+        case at::ScalarType::Double: return BCM_F64;
+        default: break;
+    }
+    TORCH_CHECK(false, what, " not implemented for type '", toString(t), "'");
+    return BCM_F32;
+}
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+Tensor workspace(int64_t bytes, const at::Device& dev) {
+    return torch::empty({std::max<int64_t>(bytes, 1)},
+                        torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+}
+
+// ---------------------------------------------------------------- extract ----
+std::vector<Tensor> extract_base_events_fwd(Tensor base_input, double threshold) {
+    TORCH_CHECK(base_input.is_cuda(), "base_input must be CUDA");
+    TORCH_CHECK(base_input.is_contiguous(), "base_input must be contiguous");
+    TORCH_CHECK(base_input.dim() == 3, "base_input must be 3-D [B, d_model, L]");
+    const bcm_dtype dt = to_bcm(base_input.scalar_type(), "count_base_kernel");
+    c10::cuda::CUDAGuard guard(base_input.device());
+    const int64_t B = base_input.size(0), d_model = base_input.size(1), L = base_input.size(2);
+    const int64_t NCb = B * d_model;
+    const float thr = (float)threshold;
+    auto opt_i = torch::TensorOptions().dtype(torch::kInt32).device(base_input.device());
+    auto counts = torch::empty({NCb}, opt_i);
+    auto cu = torch::empty({NCb + 1}, opt_i);
+    auto mx = torch::empty({}, opt_i);
+    auto ws = workspace((int64_t)bcm_extract_workspace_bytes(NCb, L), base_input.device());
+    int64_t E = 0;
+    check_status(bcm_extract_base_count(base_input.data_ptr(), dt, NCb, L, thr,
+                                        counts.data_ptr<int32_t>(), cu.data_ptr<int32_t>(),
+                                        mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), &E,
+                                        cur_stream()),
+                 "extract_base_events");
+    if (E == 0) {
+        auto ei = torch::zeros({0}, opt_i);
+        auto ms = torch::zeros({1}, opt_i);
+        return {ei, ei, ei, cu, counts, ms};
+    }
+    auto ch = torch::empty({E}, opt_i);
+    auto ts = torch::empty({E}, opt_i);
+    auto kf = torch::empty({E}, opt_i);
+    check_status(bcm_extract_base_fill(NCb, L, cu.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(),
+                                       ch.data_ptr<int32_t>(), ts.data_ptr<int32_t>(),
+                                       kf.data_ptr<int32_t>(), cur_stream()),
+                 "extract_base_events");
+    return {ch, ts, kf, cu, counts, mx};
+}
+
+std::vector<Tensor> expand_base_events_fwd(Tensor base_ch_ids, Tensor base_t_steps,
+                                           Tensor base_k_flat, Tensor base_cu_seqlens,
+                                           int64_t B, int64_t d_model, int64_t expand) {
+    TORCH_CHECK(base_ch_ids.is_cuda(), "base_ch_ids must be CUDA");
+    TORCH_CHECK(base_ch_ids.is_contiguous(), "base_ch_ids must be contiguous");
+    c10::cuda::CUDAGuard guard(base_ch_ids.device());
+    const int64_t NCb = B * d_model;
+    const int64_t NCi = B * d_model * expand;
+    const int64_t Eb = base_ch_ids.size(0);
+    auto opt_i = torch::TensorOptions().dtype(torch::kInt32).device(base_ch_ids.device());
+    if (Eb == 0) {
+        auto cu = torch::zeros({NCi + 1}, opt_i);
+        auto ms = torch::zeros({1}, opt_i);
+        auto ei = torch::zeros({0}, opt_i);
+        return {ei, ei, ei, cu, ms};
+    }
+    TORCH_CHECK(base_t_steps.is_contiguous() && base_k_flat.is_contiguous() &&
+                    base_cu_seqlens.is_contiguous(),
+                "expand_base_events: inputs must be contiguous");
+    TORCH_CHECK(base_cu_seqlens.numel() >= NCb + 1,
+                "expand_base_events: base_cu_seqlens must have B*d_model+1 entries");
+    const int64_t E = Eb * expand;
+    auto ch = torch::empty({E}, opt_i);
+    auto ts = torch::empty({E}, opt_i);
+    auto kf = torch::empty({E}, opt_i);
+    auto cu = torch::empty({NCi + 1}, opt_i);
+    auto mx = torch::empty({}, opt_i);
+    check_status(bcm_expand_base_events(base_ch_ids.data_ptr<int32_t>(),
+                                        base_t_steps.data_ptr<int32_t>(),
+                                        base_k_flat.data_ptr<int32_t>(),
+                                        base_cu_seqlens.data_ptr<int32_t>(), Eb, NCb, expand,
+                                        ch.data_ptr<int32_t>(), ts.data_ptr<int32_t>(),
+                                        kf.data_ptr<int32_t>(), cu.data_ptr<int32_t>(),
+                                        mx.data_ptr<int32_t>(), cur_stream()),
+                 "expand_base_events");
+    return {ch, ts, kf, cu, mx};
+}
+
+std::vector<Tensor> gather_events_fwd(Tensor x, Tensor channel_ids, Tensor time_steps) {
+    TORCH_CHECK(x.is_cuda(), "gather_events_fwd: x must be a CUDA tensor");
+    TORCH_CHECK(x.is_contiguous(), "gather_events_fwd: x must be contiguous");
+    TORCH_CHECK(channel_ids.scalar_type() == torch::kInt32, "gather_events_fwd: channel_ids must be int32");
+    TORCH_CHECK(time_steps.scalar_type() == torch::kInt32, "gather_events_fwd: time_steps must be int32");
+    TORCH_CHECK(x.dim() == 3, "gather_events_fwd: x must be 3-D [B, D, L]");
+    c10::cuda::CUDAGuard guard(x.device());
+    const int64_t L = x.size(2);
+    const int64_t E = channel_ids.size(0);
+    auto out = torch::empty({E}, x.options());
+    if (E == 0) return {out};
+    auto ch = channel_ids.contiguous();
+    auto ts = time_steps.contiguous();
+    check_status(bcm_gather_events_fwd(x.data_ptr(), to_bcm(x.scalar_type(), "gather_events_fwd"),
+                                       x.size(0) * x.size(1), L, ch.data_ptr<int32_t>(),
+                                       ts.data_ptr<int32_t>(), E, out.data_ptr(), cur_stream()),
+                 "gather_events_fwd");
+    return {out};
+}
+
+std::vector<Tensor> gather_events_bwd(Tensor grad_x, Tensor channel_ids, Tensor time_steps,
+                                      int64_t NC, int64_t L) {
+    TORCH_CHECK(grad_x.is_cuda(), "gather_events_bwd: grad tensor must be CUDA");
+    TORCH_CHECK(channel_ids.scalar_type() == torch::kInt32, "gather_events_bwd: channel_ids must be int32");
+    TORCH_CHECK(time_steps.scalar_type() == torch::kInt32, "gather_events_bwd: time_steps must be int32");
+    c10::cuda::CUDAGuard guard(grad_x.device());
+    auto g = grad_x.contiguous();
+    auto dx = torch::empty({NC, L}, g.options());
+    auto ch = channel_ids.contiguous();
+    auto ts = time_steps.contiguous();
+    check_status(bcm_gather_events_bwd(g.data_ptr(), to_bcm(g.scalar_type(), "gather_events_bwd"),
+                                       ch.data_ptr<int32_t>(), ts.data_ptr<int32_t>(), g.size(0),
+                                       NC, L, dx.data_ptr(), cur_stream()),
+                 "gather_events_bwd");
+    return {dx};
+}
+
+// Legacy bool-mask extraction (extract_events_cuda.cu:117-179): the same event
+// stream as extract_base_events on mask > 0.5, plus head_flags.
+std::vector<Tensor> extract_events_fwd(Tensor mask) {
+    TORCH_CHECK(mask.is_cuda(), "mask must be a CUDA tensor");
+    TORCH_CHECK(mask.is_contiguous(), "mask must be contiguous");
+    TORCH_CHECK(mask.dtype() == torch::kBool, "mask must be bool");
+    c10::cuda::CUDAGuard guard(mask.device());
+    auto r = extract_base_events_fwd(mask.to(torch::kHalf), 0.5);
+    auto ch = r[0], ts = r[1], kf = r[2], cu = r[3], counts = r[4];
+    auto opt_i = torch::TensorOptions().dtype(torch::kInt32).device(mask.device());
+    if (ch.numel() == 0) {
+        auto ei = torch::zeros({0}, opt_i);
+        return {ei, ei, ei, cu, torch::zeros({1}, opt_i), ei};
+    }
+    auto hflags = torch::zeros({ch.numel()}, opt_i);
+    auto starts = cu.slice(0, 0, cu.numel() - 1).masked_select(counts > 0).to(torch::kLong);
+    hflags.index_fill_(0, starts, 1);
+    return {ch, ts, kf, cu, r[5], hflags};
+}
+
+// ------------------------------------------------------------------- scan ----
+struct ScanPrep {
+    bcm_flat_ch_args a{};
+    Tensor u, k, cu, dti, dta, A, B, C, D, z, toff, pwB, pwC;
+    bool depthwise = false, tiled = false, has_z = false, has_pw = false;
+};
+
+void prep_scan(ScanPrep& P, const char* fn, const Tensor& u_flat, const Tensor& k_flat,
+               const Tensor& cu_seqlens, int64_t max_seqlen, const Tensor& dt_idle,
+               const Tensor& dt_active, const Tensor& A, const Tensor& B, const Tensor& C,
+               const optional<Tensor>& D_, const optional<Tensor>& z_,
+               const optional<Tensor>& tile_offsets_, bool is_depthwise_bc,
+               const optional<Tensor>& pw_B_, const optional<Tensor>& pw_C_, bool bwd) {
+    const auto input_type = u_flat.scalar_type();
+    TORCH_CHECK(input_type == at::ScalarType::Float || input_type == at::ScalarType::Half ||
+                    input_type == at::ScalarType::BFloat16,
+                fn, ": u_flat must be fp16/bf16/fp32");
+    TORCH_CHECK(A.scalar_type() == at::ScalarType::Float, fn, ": A must be float32");
+    TORCH_CHECK(B.scalar_type() == at::ScalarType::Float, fn, ": B must be float32");
+    TORCH_CHECK(C.scalar_type() == at::ScalarType::Float, fn, ": C must be float32");
+    TORCH_CHECK(u_flat.is_cuda() && k_flat.is_cuda() && cu_seqlens.is_cuda() && dt_idle.is_cuda() &&
+                    dt_active.is_cuda() && A.is_cuda() && B.is_cuda() && C.is_cuda(),
+                fn, ": all tensors must be CUDA tensors");
+    TORCH_CHECK(u_flat.is_contiguous() && k_flat.is_contiguous() && cu_seqlens.is_contiguous(),
+                fn, ": u_flat/k_flat/cu_seqlens must be contiguous");
+    TORCH_CHECK(u_flat.dim() == 1, fn, ": u_flat must be 1-D");
+    TORCH_CHECK(k_flat.dim() == 1, fn, ": k_flat must be 1-D");
+    TORCH_CHECK(cu_seqlens.dim() == 1, fn, ": cu_seqlens must be 1-D");
+    TORCH_CHECK(k_flat.scalar_type() == at::ScalarType::Int, fn, ": k_flat must be int32");
+    TORCH_CHECK(cu_seqlens.scalar_type() == at::ScalarType::Int, fn, ": cu_seqlens must be int32");
+    const int64_t E = u_flat.size(0);
+    TORCH_CHECK(k_flat.size(0) == E, fn, ": k_flat must match u_flat shape");
+    TORCH_CHECK(cu_seqlens.size(0) >= 2, fn, ": cu_seqlens must have at least 2 elements");
+    const int64_t NC = cu_seqlens.size(0) - 1;
+    TORCH_CHECK(dt_idle.scalar_type() == at::ScalarType::Float &&
+                    dt_active.scalar_type() == at::ScalarType::Float,
+                fn, ": dt_idle/dt_active must be float32");
+    TORCH_CHECK(dt_idle.dim() == 1 && dt_active.dim() == 1, fn, ": dt_idle/dt_active must be 1-D");
+    TORCH_CHECK(A.dim() == 2, fn, ": A must be 2-D (dim, dstate)");
+    const int64_t dim = A.size(0), dstate = A.size(1);
+    TORCH_CHECK(dstate <= 256, fn, ": dstate must be <= 256");
+    CHECK_SHAPE(dt_idle, dim);
+    CHECK_SHAPE(dt_active, dim);
+    P.tiled = tile_offsets_.has_value() && tile_offsets_.value().defined();
+    P.depthwise = is_depthwise_bc && !P.tiled;
+    if (P.depthwise) {
+        TORCH_CHECK(B.dim() == 2 && C.dim() == 2, fn, " (depthwise): W_B/W_C must be 2-D [dim, dstate]");
+        TORCH_CHECK(B.size(0) == dim && B.size(1) == dstate, fn, " (depthwise): W_B must be [dim, dstate]");
+        TORCH_CHECK(C.size(0) == dim && C.size(1) == dstate, fn, " (depthwise): W_C must be [dim, dstate]");
+        TORCH_CHECK(B.is_contiguous() && C.is_contiguous(), fn, " (depthwise): W_B/W_C must be contiguous");
+    } else if (P.tiled) {
+        TORCH_CHECK(B.dim() == 3 && C.dim() == 3, fn,
+                    ": tiled B/C must be 3-D [N_tiles, dstate, tile_chunk_size]");
+        TORCH_CHECK(B.size(1) == dstate && C.size(1) == dstate, fn, ": tiled B/C dim-1 must equal dstate");
+        TORCH_CHECK(B.is_contiguous() && C.is_contiguous(), fn, ": tiled B/C must be contiguous");
+    } else if (!bwd) {
+        TORCH_CHECK(B.dim() == 2 && C.dim() == 2, fn, ": B/C must be 2-D (dstate, E) [transposed layout]");
+        CHECK_SHAPE(B, dstate, E);
+        CHECK_SHAPE(C, dstate, E);
+        TORCH_CHECK(B.stride(1) == 1 && C.stride(1) == 1, fn,
+                    ": B/C must have contiguous last dimension (stride(1) == 1)");
+    } else {
+        TORCH_CHECK(B.dim() == 2 && C.dim() == 2, fn, ": B/C must be 2-D [dstate, E] or [dstate, dim]");
+        TORCH_CHECK(B.stride(1) == 1 && C.stride(1) == 1, fn, ": B/C must have contiguous last dimension");
+    }
+    if (D_.has_value()) {
+        TORCH_CHECK(D_.value().scalar_type() == at::ScalarType::Float, fn, ": D must be float32");
+        TORCH_CHECK(D_.value().is_cuda() && D_.value().is_contiguous());
+        CHECK_SHAPE(D_.value(), dim);
+    }
+    P.has_z = z_.has_value();
+    if (P.has_z) {
+        const Tensor& z = z_.value();
+        TORCH_CHECK(z.scalar_type() == input_type, fn, ": z must have same dtype as u_flat");
+        TORCH_CHECK(z.is_cuda() && z.is_contiguous());
+        TORCH_CHECK(z.dim() == 1 && z.size(0) == E, fn, ": z must have shape (E,)");
+    }
+    TORCH_CHECK(max_seqlen >= 0, fn, ": max_seqlen must be non-negative");
+    P.has_pw = P.depthwise && pw_B_.has_value() && pw_B_.value().defined();
+    if (P.has_pw) {
+        TORCH_CHECK(pw_C_.has_value() && pw_C_.value().defined(), fn, ": pw_C must accompany pw_B");
+        const Tensor& pwB = pw_B_.value();
+        const Tensor& pwC = pw_C_.value();
+        TORCH_CHECK(pwB.scalar_type() == at::ScalarType::Float && pwC.scalar_type() == at::ScalarType::Float,
+                    fn, ": pw_B/pw_C must be float32");
+        TORCH_CHECK(pwB.is_cuda() && pwC.is_cuda() && pwB.is_contiguous() && pwC.is_contiguous(), fn,
+                    ": pw_B/pw_C must be CUDA and contiguous");
+        TORCH_CHECK(pwB.dim() == 2 && pwB.size(0) == dim && pwB.size(1) == dim, fn, ": pw_B must be [dim, dim]");
+        TORCH_CHECK(pwC.dim() == 2 && pwC.size(0) == dim && pwC.size(1) == dim, fn, ": pw_C must be [dim, dim]");
+        P.pwB = pwB;
+        P.pwC = pwC;
+    }
+    P.u = u_flat; P.k = k_flat; P.cu = cu_seqlens;
+    P.dti = dt_idle.contiguous(); P.dta = dt_active.contiguous();
+    P.A = A;
+    P.B = B.contiguous(); P.C = C.contiguous();
+    if (D_.has_value()) P.D = D_.value();
+    if (P.has_z) P.z = z_.value();
+    if (P.tiled) P.toff = tile_offsets_.value().to(torch::kInt32).contiguous();
+
+    bcm_flat_ch_args& a = P.a;
+    a.n_events = E;
+    a.n_channels = NC;
+    a.dim = dim;
+    a.dstate = dstate;
+    a.max_seqlen = max_seqlen;
+    a.dtype = to_bcm(input_type, fn);
+    a.bc_mode = P.depthwise ? BCM_BC_DEPTHWISE : (P.tiled ? BCM_BC_TILED : BCM_BC_FLAT);
+    a.b_variable = P.B.dim() == 2 ? (P.B.size(1) == E) : 1;
+    a.c_variable = P.C.dim() == 2 ? (P.C.size(1) == E) : 1;
+    a.u = P.u.data_ptr();
+    a.k = P.k.data_ptr<int32_t>();
+    a.cu_seqlens = P.cu.data_ptr<int32_t>();
+    a.dt_idle = P.dti.data_ptr<float>();
+    a.dt_active = P.dta.data_ptr<float>();
+    a.A = P.A.data_ptr<float>();
+    a.A_stride_d = P.A.stride(0);
+    a.A_stride_n = P.A.stride(1);
+    a.B = P.B.data_ptr<float>();
+    a.C = P.C.data_ptr<float>();
+    a.D = P.D.defined() ? P.D.data_ptr<float>() : nullptr;
+    a.z = P.has_z ? P.z.data_ptr() : nullptr;
+    a.tile_offsets = P.tiled ? P.toff.data_ptr<int32_t>() : nullptr;
+    a.n_tiles = P.tiled ? std::min(P.B.size(0), P.C.size(0)) : 0;
+    a.pw_B = P.has_pw ? P.pwB.data_ptr<float>() : nullptr;
+    a.pw_C = P.has_pw ? P.pwC.data_ptr<float>() : nullptr;
+}
+
+std::vector<Tensor> selective_scan_fwd_flat_ch(
+    const Tensor& u_flat, const Tensor& k_flat, const Tensor& cu_seqlens, const int64_t max_seqlen,
+    const Tensor& dt_idle, const Tensor& dt_active, const Tensor& A, const Tensor& B,
+    const Tensor& C, const optional<Tensor>& D_, const optional<Tensor>& z_,
+    const optional<Tensor>& tile_offsets_, const int64_t tile_chunk_size, const bool is_depthwise_bc,
+    const optional<Tensor>& pw_B_, const optional<Tensor>& pw_C_) {
+    (void)tile_chunk_size;  // the kernel derives the tile stride from max_seqlen, as the reference
+    ScanPrep P;
+    prep_scan(P, "selective_scan_fwd_flat_ch", u_flat, k_flat, cu_seqlens, max_seqlen, dt_idle,
+              dt_active, A, B, C, D_, z_, tile_offsets_, is_depthwise_bc, pw_B_, pw_C_, false);
+    c10::cuda::CUDAGuard guard(u_flat.device());
+    int64_t n_chunks = (max_seqlen + 2047) / 2048;
+    if (n_chunks == 0) n_chunks = 1;
+    auto out = torch::empty_like(u_flat);
+    auto x = torch::zeros({P.a.n_channels, n_chunks, P.a.dstate * 2},
+                          u_flat.options().dtype(torch::kFloat32));
+    Tensor out_z;
+    if (P.has_z) out_z = torch::empty_like(u_flat);
+    bcm_flat_ch_args& a = P.a;
+    a.out = out.data_ptr();
+    a.x = x.data_ptr<float>();
+    a.out_z = P.has_z ? out_z.data_ptr() : nullptr;
+    Tensor ws = workspace((int64_t)bcm_flat_ch_fwd_workspace_bytes(&a), u_flat.device());
+    a.workspace = ws.data_ptr();
+    a.workspace_bytes = ws.numel();
+    check_status(bcm_flat_ch_fwd(&a, cur_stream()), "selective_scan_fwd_flat_ch");
+    std::vector<Tensor> result = {out, x};
+    if (P.has_z) result.push_back(out_z);
+    return result;
+}
+
+std::vector<Tensor> selective_scan_bwd_flat_ch(
+    const Tensor& u_flat, const Tensor& k_flat, const Tensor& cu_seqlens, const int64_t max_seqlen,
+    const Tensor& dt_idle, const Tensor& dt_active, const Tensor& A, const Tensor& B,
+    const Tensor& C, const Tensor& dout_flat, const Tensor& x, const optional<Tensor>& D_,
+    const optional<Tensor>& z_, const optional<Tensor>& out_, const optional<Tensor>& tile_offsets_,
+    const int64_t tile_chunk_size, const bool is_depthwise_bc, const optional<Tensor>& pw_B_,
+    const optional<Tensor>& pw_C_) {
+    (void)tile_chunk_size;
+    const char* fn = "selective_scan_bwd_flat_ch";
+    TORCH_CHECK(dout_flat.scalar_type() == u_flat.scalar_type(), fn, ": dout_flat must match u_flat dtype");
+    TORCH_CHECK(dout_flat.is_cuda() && x.is_cuda(), fn, ": all tensors must be CUDA tensors");
+    TORCH_CHECK(dout_flat.is_contiguous(), fn, ": u_flat/k_flat/cu_seqlens/dout_flat must be contiguous");
+    TORCH_CHECK(dout_flat.dim() == 1, fn, ": u_flat/k_flat/cu_seqlens/dout_flat must be 1-D");
+    ScanPrep P;
+    prep_scan(P, fn, u_flat, k_flat, cu_seqlens, max_seqlen, dt_idle, dt_active, A, B, C, D_, z_,
+              tile_offsets_, is_depthwise_bc, pw_B_, pw_C_, true);
+    TORCH_CHECK(dout_flat.size(0) == u_flat.size(0), fn, ": dout_flat must match u_flat shape");
+    c10::cuda::CUDAGuard guard(u_flat.device());
+    bcm_flat_ch_args& a = P.a;
+    TORCH_CHECK(x.scalar_type() == at::ScalarType::Float, fn, ": x must be float32");
+    TORCH_CHECK(x.is_contiguous(), fn, ": x must be contiguous");
+    TORCH_CHECK(x.dim() == 3 && x.size(0) == a.n_channels && x.size(2) == a.dstate * 2, fn,
+                ": x must have shape (n_channels, n_chunks, dstate*2)");
+    int64_t n_chunks = (max_seqlen + 2047) / 2048;
+    if (n_chunks == 0) n_chunks = 1;
+    TORCH_CHECK(x.size(1) == n_chunks, fn, ": x.size(1) must equal n_chunks = (max_seqlen + 2047) / 2048");
+    Tensor out_fwd, dz;
+    if (P.has_z) {
+        TORCH_CHECK(out_.has_value(), fn,
+                    ": out (forward ungated output) must be provided when z is provided");
+        out_fwd = out_.value();
+        TORCH_CHECK(out_fwd.scalar_type() == u_flat.scalar_type(), fn, ": z/out must match u_flat dtype");
+        TORCH_CHECK(out_fwd.is_cuda() && out_fwd.is_contiguous());
+        TORCH_CHECK(out_fwd.size(0) == u_flat.size(0), fn, ": z/out must have shape (E,)");
+        dz = torch::zeros_like(u_flat);
+    }
+    auto du = torch::empty_like(u_flat);
+    auto dA = torch::empty_like(A, at::MemoryFormat::Contiguous);
+    Tensor dB, dC;
+    if (P.depthwise) {
+        dB = torch::empty_like(P.B);
+        dC = torch::empty_like(P.C);
+    } else {
+        dB = torch::zeros_like(P.B);
+        dC = torch::zeros_like(P.C);
+    }
+    auto ddt_idle = torch::empty_like(dt_idle);
+    auto ddt_active = torch::empty_like(dt_active);
+    Tensor dD, dpwB, dpwC;
+    if (D_.has_value()) dD = torch::empty_like(D_.value());
+    if (P.has_pw) {
+        dpwB = torch::empty_like(P.pwB);
+        dpwC = torch::empty_like(P.pwC);
+    }
+    a.x = x.data_ptr<float>();
+    a.dout = dout_flat.data_ptr();
+    a.out_fwd = P.has_z ? out_fwd.data_ptr() : nullptr;
+    a.du = du.data_ptr();
+    a.dA = dA.data_ptr<float>();
+    a.dB = dB.data_ptr<float>();
+    a.dC = dC.data_ptr<float>();
+    a.ddt_idle = ddt_idle.data_ptr<float>();
+    a.ddt_active = ddt_active.data_ptr<float>();
+    a.dD = dD.defined() ? dD.data_ptr<float>() : nullptr;
+    a.dz = P.has_z ? dz.data_ptr() : nullptr;
+    a.dpw_B = P.has_pw ? dpwB.data_ptr<float>() : nullptr;
+    a.dpw_C = P.has_pw ? dpwC.data_ptr<float>() : nullptr;
+    Tensor ws = workspace((int64_t)bcm_flat_ch_bwd_workspace_bytes(&a), u_flat.device());
+    a.workspace = ws.data_ptr();
+    a.workspace_bytes = ws.numel();
+    check_status(bcm_flat_ch_bwd(&a, cur_stream()), fn);
+    std::vector<Tensor> result = {du, dA, dB, dC, ddt_idle, ddt_active};
+    if (D_.has_value()) result.push_back(dD);
+    if (P.has_z) result.push_back(dz);
+    if (P.has_pw) {
+        result.push_back(dpwB);
+        result.push_back(dpwC);
+    }
+    return result;
+}
+
+std::vector<Tensor> dense_scan_unavailable(py::args, py::kwargs) {
+    TORCH_CHECK(false,
+                "selective_scan_cuda.fwd/bwd (dense Mamba scan) is not part of this build; "
+                "the event path uses fwd_flat_ch/bwd_flat_ch");
+    return {};
+}
+
+// ---------------------------------------------------------------- restore ----
+Tensor restore_dense_fwd(const Tensor& y_flat, const Tensor& time_steps, const Tensor& cu_seqlens,
+                         int64_t dim, int64_t seqlen, const optional<at::ScalarType> out_dtype_opt) {
+    auto input_type = y_flat.scalar_type();
+    TORCH_CHECK(input_type == at::ScalarType::Float || input_type == at::ScalarType::Half ||
+                    input_type == at::ScalarType::BFloat16,
+                "restore_dense_fwd: y_flat must be fp32, fp16, or bf16");
+    TORCH_CHECK(time_steps.scalar_type() == at::ScalarType::Int,
+                "restore_dense_fwd: time_steps must be int32 (torch.int32)");
+    TORCH_CHECK(cu_seqlens.scalar_type() == at::ScalarType::Int,
+                "restore_dense_fwd: cu_seqlens must be int32 (torch.int32)");
+    TORCH_CHECK(y_flat.is_cuda() && time_steps.is_cuda() && cu_seqlens.is_cuda(),
+                "restore_dense_fwd: all tensors must be on CUDA");
+    TORCH_CHECK(y_flat.is_contiguous() && time_steps.is_contiguous() && cu_seqlens.is_contiguous(),
+                "restore_dense_fwd: all tensors must be contiguous");
+    TORCH_CHECK(y_flat.dim() == 1, "restore_dense_fwd: y_flat must be 1-D");
+    TORCH_CHECK(time_steps.sizes() == y_flat.sizes(), "restore_dense_fwd: time_steps shape must equal y_flat shape");
+    TORCH_CHECK(cu_seqlens.dim() == 1, "restore_dense_fwd: cu_seqlens must be 1-D");
+    TORCH_CHECK(dim >= 1, "restore_dense_fwd: dim must be >= 1");
+    TORCH_CHECK(seqlen >= 1, "restore_dense_fwd: seqlen must be >= 1");
+    const int64_t E = y_flat.size(0);
+    const int64_t NC = cu_seqlens.size(0) - 1;
+    TORCH_CHECK(NC >= 1, "restore_dense_fwd: cu_seqlens must have at least 2 elements");
+    TORCH_CHECK(NC % dim == 0, "restore_dense_fwd: n_channels (B*D) must be divisible by dim");
+    auto out_type = out_dtype_opt.value_or(input_type);
+    TORCH_CHECK(out_type == at::ScalarType::Float || out_type == at::ScalarType::Half ||
+                    out_type == at::ScalarType::BFloat16,
+                "restore_dense_fwd: out_dtype must be fp32, fp16, or bf16");
+    if (input_type == at::ScalarType::Half)
+        TORCH_CHECK(out_type == at::ScalarType::Half, "restore_dense_fwd: fp16 input only supports fp16 output");
+    if (input_type == at::ScalarType::BFloat16)
+        TORCH_CHECK(out_type == at::ScalarType::BFloat16, "restore_dense_fwd: bf16 input only supports bf16 output");
+    c10::cuda::CUDAGuard guard(y_flat.device());
+    const int64_t B = NC / dim;
+    auto out = torch::empty({B, seqlen, dim}, y_flat.options().dtype(out_type));
+    check_status(bcm_restore_dense_fwd(y_flat.data_ptr(), to_bcm(input_type, "restore_dense_fwd"),
+                                       time_steps.data_ptr<int32_t>(), cu_seqlens.data_ptr<int32_t>(),
+                                       E, NC, dim, seqlen, out.data_ptr(),
+                                       to_bcm(out_type, "restore_dense_fwd"), cur_stream()),
+                 "restore_dense_fwd");
+    return out;
+}
+
+Tensor restore_dense_bwd(const Tensor& dout, const Tensor& time_steps, const Tensor& cu_seqlens,
+                         int64_t dim, int64_t seqlen) {
+    auto input_type = dout.scalar_type();
+    TORCH_CHECK(input_type == at::ScalarType::Float || input_type == at::ScalarType::Half ||
+                    input_type == at::ScalarType::BFloat16,
+                "restore_dense_bwd: dout must be fp32/fp16/bf16");
+    TORCH_CHECK(time_steps.scalar_type() == at::ScalarType::Int, "restore_dense_bwd: time_steps must be int32");
+    TORCH_CHECK(cu_seqlens.scalar_type() == at::ScalarType::Int, "restore_dense_bwd: cu_seqlens must be int32");
+    TORCH_CHECK(dout.is_cuda() && time_steps.is_cuda() && cu_seqlens.is_cuda(),
+                "restore_dense_bwd: all tensors must be on CUDA");
+    TORCH_CHECK(dout.is_contiguous() && time_steps.is_contiguous() && cu_seqlens.is_contiguous(),
+                "restore_dense_bwd: all tensors must be contiguous");
+    TORCH_CHECK(dim >= 1, "restore_dense_bwd: dim must be >= 1");
+    TORCH_CHECK(seqlen >= 1, "restore_dense_bwd: seqlen must be >= 1");
+    const int64_t NC = cu_seqlens.size(0) - 1;
+    const int64_t E = time_steps.size(0);
+    TORCH_CHECK(dout.dim() == 3, "restore_dense_bwd: dout must be 3-D (B, L, D)");
+    TORCH_CHECK(dout.size(1) == seqlen, "restore_dense_bwd: dout.size(1) must equal seqlen");
+    TORCH_CHECK(dout.size(2) == dim, "restore_dense_bwd: dout.size(2) must equal dim (D)");
+    TORCH_CHECK(dout.size(0) * dim == NC, "restore_dense_bwd: dout.size(0)*dim must equal n_channels");
+    c10::cuda::CUDAGuard guard(dout.device());
+    auto dy = torch::empty({E}, dout.options().dtype(at::ScalarType::Float));
+    if (E == 0) return dy;
+    check_status(bcm_restore_dense_bwd(dout.data_ptr(), to_bcm(input_type, "restore_dense_bwd"),
+                                       time_steps.data_ptr<int32_t>(), cu_seqlens.data_ptr<int32_t>(),
+                                       E, NC, dim, seqlen, dy.data_ptr<float>(), cur_stream()),
+                 "restore_dense_bwd");
+    return dy;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    m.attr("abi_version") = bcm_abi_version();
+    // selective_scan_cuda
+    m.def("fwd", &dense_scan_unavailable, "dense Mamba selective scan (not built)");
+    m.def("bwd", &dense_scan_unavailable, "dense Mamba selective scan (not built)");
+    m.def("fwd_flat_ch", &selective_scan_fwd_flat_ch, py::arg("u_flat"), py::arg("k_flat"),
+          py::arg("cu_seqlens"), py::arg("max_seqlen"), py::arg("dt_idle"), py::arg("dt_active"),
+          py::arg("A"), py::arg("B"), py::arg("C"), py::arg("D") = py::none(),
+          py::arg("z") = py::none(), py::arg("tile_offsets") = py::none(),
+          py::arg("tile_chunk_size") = 0, py::arg("is_depthwise_bc") = false,
+          py::arg("pw_B") = py::none(), py::arg("pw_C") = py::none(),
+          "Selective scan forward (flat per-channel, jagged layout)");
+    m.def("bwd_flat_ch", &selective_scan_bwd_flat_ch, py::arg("u_flat"), py::arg("k_flat"),
+          py::arg("cu_seqlens"), py::arg("max_seqlen"), py::arg("dt_idle"), py::arg("dt_active"),
+          py::arg("A"), py::arg("B"), py::arg("C"), py::arg("dout_flat"), py::arg("x"),
+          py::arg("D") = py::none(), py::arg("z") = py::none(), py::arg("out") = py::none(),
+          py::arg("tile_offsets") = py::none(), py::arg("tile_chunk_size") = 0,
+          py::arg("is_depthwise_bc") = false, py::arg("pw_B") = py::none(),
+          py::arg("pw_C") = py::none(), "Selective scan backward (flat per-channel, jagged layout)");
+    // extract_events_cuda
+    m.def("extract_events", &extract_events_fwd, "bool mask -> (ch_ids, t_steps, k_flat, cu_seqlens, max_seqlen, head_flags)");
+    m.def("extract_base_events", &extract_base_events_fwd,
+          "float base_input + threshold -> (base_ch_ids, base_t_steps, base_k_flat, base_cu_seqlens, base_counts, base_max_seqlen)");
+    m.def("expand_base_events", &expand_base_events_fwd,
+          "expand the base event stream by `expand` (repeat_interleave order)");
+    m.def("gather_events_fwd", &gather_events_fwd, "gather x[B,D,L] at (channel_ids, time_steps)");
+    m.def("gather_events_bwd", &gather_events_bwd, "scatter-store backward of gather_events_fwd");
+    // restore_dense_cuda_nodecay
+    m.def("restore_dense_fwd", &restore_dense_fwd, py::arg("y_flat"), py::arg("time_steps"),
+          py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"), py::arg("out_dtype") = py::none(),
+          "Zero-order-hold restore (B, L, D) from flat events");
+    m.def("restore_dense_bwd", &restore_dense_bwd, py::arg("dout"), py::arg("time_steps"),
+          py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"),
+          "Backward of restore_dense_fwd; returns dy_flat (float32)");
+}

@@ -1,0 +1,198 @@
+"""Autograd boundary of the event pipeline, identical in signature to the
+reference's Python layer so callers switch without edits:
+
+* ``SelectiveScanFlatChFn`` / ``selective_scan_flat_ch_fn``
+  (spike_mamba/selective_scan_interface.py:1015-1237)
+* ``RestoreDenseFn`` / ``restore_dense_fn``  (spike_mamba/e_model.py:123-161)
+* ``GatherEventsFn`` / ``gather_events``       (spike_mamba/e_model.py:167-193)
+* ``extract_events_1d``                        (spike_mamba/e_model.py:361-409)
+
+All device work goes through the native shim (``bc_mamba_b200._native``);
+there is no Python or CPU fallback.  ``install_shim()`` puts the drop-in
+modules ``selective_scan_cuda``, ``extract_events_cuda`` and
+``restore_dense_cuda_nodecay`` on ``sys.path`` so the reference's own
+``e_model.py`` / ``lra_impl.py`` import them unchanged.
+"""
+from __future__ import annotations
+
+import contextlib
+import sys
+from pathlib import Path
+
+import torch
+
+from ._native import load_ops
+
+SHIM_DIR = Path(__file__).resolve().parent / "shim"
+
+
+def install_shim() -> None:
+    """Make ``import selective_scan_cuda`` (and the other two) resolve here."""
+    p = str(SHIM_DIR)
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+@contextlib.contextmanager
+def cuda_stage(name: str):
+    """NVTX range named like the reference's profiling stages
+    (spike_mamba/runtime_breakdown.py:12-15)."""
+    if torch.cuda.is_available():
+        torch.cuda.nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        yield
+
+
+class SelectiveScanFlatChFn(torch.autograd.Function):
+    """Flat per-channel selective scan over event streams.
+
+    Forward inputs (positional): u_flat, k_flat, cu_seqlens, dt_idle,
+    dt_active, A, B, C, D, z, max_seqlen, tile_offsets, tile_chunk_size,
+    is_depthwise_bc, pw_B, pw_C.  Returns (out, x) where x holds the chunk
+    boundary states (non-differentiable); out is gated by silu(z) if z given.
+    """
+
+    @staticmethod
+    def forward(ctx, u_flat, k_flat, cu_seqlens, dt_idle, dt_active, A, B, C, D, z,
+                max_seqlen, tile_offsets, tile_chunk_size, is_depthwise_bc, pw_B, pw_C):
+        ops = load_ops()
+        u_flat = u_flat.contiguous()
+        k_flat = k_flat.contiguous()
+        cu_seqlens = cu_seqlens.contiguous()
+        dt_idle = dt_idle.contiguous()
+        dt_active = dt_active.contiguous()
+        A, B, C = A.contiguous(), B.contiguous(), C.contiguous()
+        D = D.contiguous() if D is not None else None
+        z = z.contiguous() if z is not None else None
+        tile_offsets = tile_offsets.contiguous() if tile_offsets is not None else None
+        pw_B = pw_B.contiguous() if pw_B is not None else None
+        pw_C = pw_C.contiguous() if pw_C is not None else None
+        with cuda_stage("sparse_scan_forward"):
+            res = ops.fwd_flat_ch(u_flat, k_flat, cu_seqlens, max_seqlen, dt_idle, dt_active,
+                                  A, B, C, D, z, tile_offsets, tile_chunk_size,
+                                  is_depthwise_bc, pw_B, pw_C)
+        out, x = res[0], res[1]
+        ctx.has_D = D is not None
+        ctx.has_z = z is not None
+        ctx.has_tiles = tile_offsets is not None
+        ctx.has_pw = pw_B is not None
+        ctx.max_seqlen = max_seqlen
+        ctx.tile_chunk_size = tile_chunk_size
+        ctx.is_depthwise_bc = is_depthwise_bc
+        saved = [u_flat, k_flat, cu_seqlens, dt_idle, dt_active, A, B, C, x]
+        if ctx.has_D:
+            saved.append(D)
+        if ctx.has_z:
+            saved += [z, out]
+        if ctx.has_tiles:
+            saved.append(tile_offsets)
+        if ctx.has_pw:
+            saved += [pw_B, pw_C]
+        ctx.save_for_backward(*saved)
+        ctx.mark_non_differentiable(x)
+        return (res[2] if ctx.has_z else out), x
+
+    @staticmethod
+    def backward(ctx, dout, _dx):
+        ops = load_ops()
+        if dout.stride(-1) != 1:
+            dout = dout.contiguous()
+        it = iter(ctx.saved_tensors)
+        u_flat, k_flat, cu_seqlens, dt_idle, dt_active, A, B, C, x = (next(it) for _ in range(9))
+        D = next(it) if ctx.has_D else None
+        z, out = (next(it), next(it)) if ctx.has_z else (None, None)
+        tile_offsets = next(it) if ctx.has_tiles else None
+        pw_B, pw_C = (next(it), next(it)) if ctx.has_pw else (None, None)
+        with cuda_stage("sparse_scan_backward"):
+            res = ops.bwd_flat_ch(u_flat, k_flat, cu_seqlens, ctx.max_seqlen, dt_idle, dt_active,
+                                  A, B, C, dout, x, D, z, out, tile_offsets,
+                                  ctx.tile_chunk_size, ctx.is_depthwise_bc, pw_B, pw_C)
+        du, dA, dB, dC, ddt_idle, ddt_active = res[:6]
+        rest = iter(res[6:])
+        dD = next(rest) if ctx.has_D else None
+        dz = next(rest) if ctx.has_z else None
+        dpw_B, dpw_C = (next(rest), next(rest)) if ctx.has_pw else (None, None)
+        return (du, None, None, ddt_idle, ddt_active, dA, dB, dC, dD, dz,
+                None, None, None, None, dpw_B, dpw_C)
+
+
+def selective_scan_flat_ch_fn(u_flat, k_flat, cu_seqlens, max_seqlen, dt_idle, dt_active, A, B, C,
+                              D=None, z=None, tile_offsets=None, tile_chunk_size=0,
+                              is_depthwise_bc=False, pw_B=None, pw_C=None):
+    """Autograd-enabled flat per-channel selective scan; returns (out, x)."""
+    return SelectiveScanFlatChFn.apply(u_flat, k_flat, cu_seqlens, dt_idle, dt_active, A, B, C,
+                                       D, z, max_seqlen, tile_offsets, tile_chunk_size,
+                                       is_depthwise_bc, pw_B, pw_C)
+
+
+class RestoreDenseFn(torch.autograd.Function):
+    """Zero-order-hold restore: (E,) event values -> (B, L, D) dense."""
+
+    @staticmethod
+    def forward(ctx, y_flat, time_steps_i32, cu_seqlens, dim: int, seqlen: int):
+        with cuda_stage("dense_restoration_forward"):
+            out = load_ops().restore_dense_fwd(y_flat, time_steps_i32, cu_seqlens, dim, seqlen)
+        ctx.save_for_backward(time_steps_i32, cu_seqlens)
+        ctx.dim = dim
+        ctx.seqlen = seqlen
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        time_steps_i32, cu_seqlens = ctx.saved_tensors
+        with cuda_stage("restore_backward"):
+            dy = load_ops().restore_dense_bwd(dout.contiguous(), time_steps_i32, cu_seqlens,
+                                              ctx.dim, ctx.seqlen)
+        return dy, None, None, None, None
+
+
+def restore_dense_fn(y_flat, time_steps_i32, cu_seqlens, dim: int, seqlen: int):
+    return RestoreDenseFn.apply(y_flat, time_steps_i32, cu_seqlens, dim, seqlen)
+
+
+class GatherEventsFn(torch.autograd.Function):
+    """u_flat[e] = x_conv[b, d, t] at (channel_ids[e] = b*D + d, time_steps[e])."""
+
+    @staticmethod
+    def forward(ctx, x_conv, channel_ids_i32, time_steps_i32):
+        x_c = x_conv.contiguous()
+        with cuda_stage("active_gather_forward"):
+            out_x = load_ops().gather_events_fwd(x_c, channel_ids_i32, time_steps_i32)[0]
+        ctx.save_for_backward(channel_ids_i32, time_steps_i32)
+        ctx.shape = x_c.shape
+        return out_x
+
+    @staticmethod
+    def backward(ctx, grad_x):
+        channel_ids_i32, time_steps_i32 = ctx.saved_tensors
+        B, D, L = ctx.shape
+        with cuda_stage("gather_scatter_backward"):
+            dx = load_ops().gather_events_bwd(grad_x.contiguous(), channel_ids_i32,
+                                              time_steps_i32, B * D, L)[0]
+        return dx.view(B, D, L), None, None
+
+
+def gather_events(x_conv, channel_ids_i32, time_steps_i32):
+    return GatherEventsFn.apply(x_conv, channel_ids_i32, time_steps_i32)
+
+
+def extract_events_1d(hidden_states, x_conv, threshold: float, expand: int):
+    """Threshold (B, L, d_model) spikes into the expanded event stream and
+    gather x_conv (B, D, L) at the events, like Mamba.extract_events_1d.
+
+    Returns (channel_ids, time_steps, k_flat, cu_seqlens, max_seqlen, x_conv_flat).
+    """
+    ops = load_ops()
+    B, L, d_model = hidden_states.shape
+    base_input = hidden_states.transpose(1, 2).contiguous()
+    with cuda_stage("routing_index_extraction"):
+        bch, bt, bk, bcu, _counts, _bmax = ops.extract_base_events(base_input, threshold)
+    with cuda_stage("active_token_packing"):
+        ch, ts, kf, cu, mx = ops.expand_base_events(bch, bt, bk, bcu, B, d_model, expand)
+        max_seqlen = int(mx.item())
+    x_flat = gather_events(x_conv, ch, ts)
+    return ch, ts, kf, cu, max_seqlen, x_flat

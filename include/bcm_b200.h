@@ -1,0 +1,239 @@
+/*
+ * bcm_b200.h — C ABI of the B200 (sm_100a) event-scan pipeline.
+ *
+ * One shared library (libbcm_b200.so) exports every entry point below with
+ * plain pointers, sizes and a cudaStream_t.  No torch types cross this line.
+ * Each entry point replaces one binding of the reference's pybind11
+ * extensions; the reference location it replaces is cited beside it.  The
+ * caller owns and allocates every buffer (outputs and workspaces); the library
+ * allocates nothing, keeps no state between calls, and is re-entrant.
+ *
+ * Conventions
+ *   - Every function returns a bcm_status.  BCM_OK (0) means success; any
+ *     other value leaves a thread-local message readable with bcm_last_error().
+ *   - Device pointers must belong to the current CUDA device; kernels are
+ *     launched on `stream` (0 = legacy default stream).
+ *   - Index tensors are int32.  Event streams are channel-major: the events of
+ *     logical channel c occupy [cu_seqlens[c], cu_seqlens[c+1]) in ascending t.
+ *   - Workspaces are opaque device scratch of at least the size the matching
+ *     *_workspace_bytes() query returns; they need no initialisation.
+ */
+#ifndef BCM_B200_H_
+#define BCM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BCM_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define BCM_API __attribute__((visibility("default")))
+#else
+#define BCM_API
+#endif
+
+typedef enum bcm_status {
+    BCM_OK = 0,
+    BCM_ERR_INVALID_ARGUMENT = 1, /* shape/dtype/size/pointer contract violated   */
+    BCM_ERR_CUDA = 2,             /* a CUDA runtime call or launch failed          */
+    BCM_ERR_WORKSPACE = 3,        /* workspace missing or smaller than required    */
+    BCM_ERR_UNSUPPORTED = 4       /* valid request this build does not implement   */
+} bcm_status;
+
+/* Element type of the floating-point event / dense tensors.  BCM_F64 is
+ * accepted only by the extraction input and the gather entry points (the
+ * reference dispatches those on double as well). */
+typedef enum bcm_dtype {
+    BCM_F32 = 0,
+    BCM_F16 = 1,
+    BCM_BF16 = 2,
+    BCM_F64 = 3
+} bcm_dtype;
+
+/* Thread-local description of the last failure on this thread ("" if none). */
+BCM_API const char* bcm_last_error(void);
+BCM_API int bcm_abi_version(void);
+
+/* ------------------------------------------------------------------------- *
+ * Event extraction.
+ * Replaces extract_events_cuda.extract_base_events
+ *   (reference csrc/extract/extract_events_cuda.cu:324-418).
+ * Split in two calls because the output length E_base is data dependent:
+ *   1. bcm_extract_base_count thresholds base_input[NCb, L] (strictly
+ *      float(x) > threshold), writes counts[NCb], cu_seqlens[NCb+1],
+ *      max_seqlen[1] (device, int32) and a bitmask into the workspace, then
+ *      copies E_base to *n_events_host (this synchronises `stream`).
+ *   2. bcm_extract_base_fill writes ch_ids/t_steps/k_flat[E_base] from the
+ *      workspace bitmask (k = t - t_prev, first event of a channel k = t + 1).
+ * ------------------------------------------------------------------------- */
+BCM_API size_t bcm_extract_workspace_bytes(int64_t n_base_channels, int64_t seqlen);
+
+BCM_API bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype dtype,
+                                  int64_t n_base_channels, int64_t seqlen,
+                                  float threshold,
+                                  int32_t* counts, int32_t* cu_seqlens,
+                                  int32_t* max_seqlen,
+                                  void* workspace, size_t workspace_bytes,
+                                  int64_t* n_events_host, cudaStream_t stream);
+
+BCM_API bcm_status bcm_extract_base_fill(int64_t n_base_channels, int64_t seqlen,
+                                 const int32_t* cu_seqlens,
+                                 const void* workspace, size_t workspace_bytes,
+                                 int32_t* ch_ids, int32_t* t_steps,
+                                 int32_t* k_flat, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Expansion of the base stream into `expand` logical replicas per channel
+ * (repeat_interleave order: logical channel = base channel * expand + r).
+ * Replaces extract_events_cuda.expand_base_events
+ *   (reference csrc/extract/extract_events_cuda.cu:529-603).
+ * Outputs: ch_ids/t_steps/k_flat[E_base*expand], cu_seqlens[NCb*expand+1],
+ * max_seqlen[1] = max per-channel count.
+ * ------------------------------------------------------------------------- */
+BCM_API bcm_status bcm_expand_base_events(const int32_t* base_ch_ids,
+                                  const int32_t* base_t_steps,
+                                  const int32_t* base_k_flat,
+                                  const int32_t* base_cu_seqlens,
+                                  int64_t n_base_events, int64_t n_base_channels,
+                                  int64_t expand,
+                                  int32_t* ch_ids, int32_t* t_steps,
+                                  int32_t* k_flat, int32_t* cu_seqlens,
+                                  int32_t* max_seqlen, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Event gather of x[NC, L] at (channel_ids, time_steps) and its transpose.
+ * Replaces extract_events_cuda.gather_events_fwd / gather_events_bwd
+ *   (reference csrc/extract/extract_events_cuda.cu:670-708, 717-754).
+ * bcm_gather_events_bwd writes all of dx[NC, L]: zeros, then grad at events.
+ * ------------------------------------------------------------------------- */
+BCM_API bcm_status bcm_gather_events_fwd(const void* x, bcm_dtype dtype,
+                                 int64_t n_channels, int64_t seqlen,
+                                 const int32_t* channel_ids,
+                                 const int32_t* time_steps, int64_t n_events,
+                                 void* out, cudaStream_t stream);
+
+BCM_API bcm_status bcm_gather_events_bwd(const void* grad, bcm_dtype dtype,
+                                 const int32_t* channel_ids,
+                                 const int32_t* time_steps, int64_t n_events,
+                                 int64_t n_channels, int64_t seqlen,
+                                 void* dx, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Flat per-channel sparse selective scan with inter-spike decay.
+ * Replaces selective_scan_cuda.fwd_flat_ch / bwd_flat_ch
+ *   (reference csrc/selective_scan/selective_scan.cpp:674-884, 890-1153).
+ *
+ * Per logical channel c (feature d = c % dim) and event i of that channel:
+ *   delta_i = dt_idle[d]*(k_i - 1) + dt_active[d]
+ *   a_i,s   = exp2(clamp(delta_i*A[d,s]*log2(e), -126, 126))
+ *   h_i,s   = a_i,s*h_{i-1},s + delta_i*u_i*B_i,s          (h_{-1} = 0)
+ *   y_i     = D[d]*u_i + sum_s h_i,s*C_i,s ; out_z = y*silu(z) when z given
+ * B/C modes (bc_mode):
+ *   BCM_BC_DEPTHWISE : B_i,s = u_i*W_B[d,s], C_i,s = u_i*W_C[d,s]; B,C [dim,N];
+ *                      optional pw_B/pw_C [dim,dim] mix W first
+ *                      (W_eff[d,s] = sum_d' pw[d,d']*W[d',s]).
+ *   BCM_BC_FLAT      : B and C independently either per event [N, E]
+ *                      (b_variable / c_variable = 1) or per feature [N, dim].
+ *   BCM_BC_TILED     : B,C [n_tiles, N, chunk] addressed through
+ *                      tile_offsets[c] + event/chunk, chunk chosen from
+ *                      max_seqlen (128/256/512/1024/2048).
+ * x[c, j, 2s] / x[c, j, 2s+1] = (prod of a, h) of state s after the last event
+ * of 2048-event chunk j of channel c; x has n_chunks = max(1, ceil(max_seqlen /
+ * 2048)) chunks per channel and must be zeroed by the caller.
+ * ------------------------------------------------------------------------- */
+enum {
+    BCM_BC_DEPTHWISE = 0,
+    BCM_BC_FLAT = 1,
+    BCM_BC_TILED = 2
+};
+
+typedef struct bcm_flat_ch_args {
+    /* sizes */
+    int64_t n_events;     /* E                                   */
+    int64_t n_channels;   /* NC = len(cu_seqlens) - 1            */
+    int64_t dim;          /* D (features; channel c uses c % D)  */
+    int64_t dstate;       /* N, 1..256                           */
+    int64_t max_seqlen;   /* max events of one channel           */
+    bcm_dtype dtype;      /* u / out / z / dout / du / dz        */
+    int32_t bc_mode;      /* BCM_BC_*                            */
+    int32_t b_variable;   /* BCM_BC_FLAT: B is [N,E] (1) or [N,dim] (0) */
+    int32_t c_variable;   /* BCM_BC_FLAT: C is [N,E] (1) or [N,dim] (0) */
+    /* forward inputs (A is [dim, N] with the given strides, in elements) */
+    const void* u;
+    const int32_t* k;
+    const int32_t* cu_seqlens;
+    const float* dt_idle;
+    const float* dt_active;
+    const float* A;
+    int64_t A_stride_d;
+    int64_t A_stride_n;
+    const float* B;
+    const float* C;
+    const float* D;             /* nullable */
+    const void* z;              /* nullable */
+    const int32_t* tile_offsets;/* BCM_BC_TILED only */
+    int64_t n_tiles;            /* BCM_BC_TILED: leading size of B/C (bounds check) */
+    const float* pw_B;          /* nullable, depthwise only */
+    const float* pw_C;
+    /* forward outputs */
+    void* out;                  /* [E] ungated output                 */
+    float* x;                   /* [NC, n_chunks, 2N], pre-zeroed     */
+    void* out_z;                /* [E] gated output when z != NULL    */
+    /* backward inputs / outputs (ignored by the forward) */
+    const void* dout;           /* [E] gradient of the primary output */
+    const void* out_fwd;        /* [E] ungated forward output, needed with z */
+    void* du;                   /* [E]                                */
+    float* dA;                  /* [dim, N] contiguous                */
+    float* dB;                  /* depthwise: dW_B [dim,N]; else same shape as B */
+    float* dC;
+    float* ddt_idle;            /* [dim] */
+    float* ddt_active;          /* [dim] */
+    float* dD;                  /* [dim] or NULL */
+    void* dz;                   /* [E] or NULL   */
+    float* dpw_B;               /* [dim,dim] or NULL */
+    float* dpw_C;
+    /* scratch */
+    void* workspace;
+    size_t workspace_bytes;
+} bcm_flat_ch_args;
+
+BCM_API size_t bcm_flat_ch_fwd_workspace_bytes(const bcm_flat_ch_args* args);
+BCM_API size_t bcm_flat_ch_bwd_workspace_bytes(const bcm_flat_ch_args* args);
+BCM_API bcm_status bcm_flat_ch_fwd(const bcm_flat_ch_args* args, cudaStream_t stream);
+BCM_API bcm_status bcm_flat_ch_bwd(const bcm_flat_ch_args* args, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Causal zero-order-hold restore to the dense (B, L, D) layout and its
+ * backward (segment sums of dout over each event's hold interval, fp32 out).
+ * Replaces restore_dense_cuda_nodecay.restore_dense_fwd / restore_dense_bwd
+ *   (reference csrc/r_nodecay/restore_dense.cpp:41-123, 131-201; kernels
+ *   restore_dense_fwd_kernel.cuh:38-112, restore_dense_bwd_kernel.cuh:42-113).
+ * Event selection follows the reference search exactly: at most the first
+ * 4095 events of a channel are addressable (index capped at 4094).
+ * out (fwd) and dy (bwd) are written in full; no pre-zeroing needed.
+ * ------------------------------------------------------------------------- */
+BCM_API bcm_status bcm_restore_dense_fwd(const void* y_flat, bcm_dtype y_dtype,
+                                 const int32_t* time_steps,
+                                 const int32_t* cu_seqlens,
+                                 int64_t n_events, int64_t n_channels,
+                                 int64_t dim, int64_t seqlen,
+                                 void* out, bcm_dtype out_dtype,
+                                 cudaStream_t stream);
+
+BCM_API bcm_status bcm_restore_dense_bwd(const void* dout, bcm_dtype dtype,
+                                 const int32_t* time_steps,
+                                 const int32_t* cu_seqlens,
+                                 int64_t n_events, int64_t n_channels,
+                                 int64_t dim, int64_t seqlen,
+                                 float* dy, cudaStream_t stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* BCM_B200_H_ */
