@@ -8,8 +8,9 @@
 //           loads, 32 in flight per lane), ballots 32 positions at a time and
 //           writes a 1-bit-per-position mask plus the channel count;
 //   pass 2  one CTA scans the counts into cu_seqlens and the max;
-//   pass 3  one warp per channel turns mask words into (ch, t, k) with a warp
-//           prefix sum for positions and a warp max-scan for the previous t.
+//   pass 3  one warp per channel turns mask words into (ch, t, k): a warp
+//           prefix sum places each word's events in a shared-memory list that
+//           is then written out with coalesced stores.
 // The row is read once (the reference reads it twice) and the fill pass reads
 // L/8 bytes of mask instead of the L*sizeof(T) input row.
 #include "common.cuh"
@@ -103,42 +104,50 @@ counts_scan_kernel(const int32_t* __restrict__ counts, int64_t n,
 }
 
 // ---- pass 3: mask words → (ch, t, k) ---------------------------------------
+// One warp per channel, 1024 positions (32 words) per step: each lane expands
+// its word's set bits into a shared-memory list at its warp-prefix offset,
+// then the warp writes (ch, t, k) for the whole list with coalesced stores;
+// k = t - t_prev reads the neighbouring list entry (first of the channel:
+// t + 1, reference fill_base_kernel :294-299).
 __global__ void __launch_bounds__(kFillWarps * 32)
 mask_fill_kernel(const uint32_t* __restrict__ mask, const int32_t* __restrict__ cu,
                  int64_t n_rows, int L, int n_words,
                  int32_t* __restrict__ ch_ids, int32_t* __restrict__ t_steps,
                  int32_t* __restrict__ k_flat) {
+    __shared__ int s_t[kFillWarps][1024 + 1];
     const int lane = lane_id();
-    const int64_t row = (int64_t)blockIdx.x * kFillWarps + (threadIdx.x >> 5);
+    const int w_in = threadIdx.x >> 5;
+    const int64_t row = (int64_t)blockIdx.x * kFillWarps + w_in;
     if (row >= n_rows) return;
+    int* st = s_t[w_in] + 1;             // st[-1] holds the previous block's last t
     const uint32_t* mr = mask + row * (int64_t)n_words;
-    int pos = cu[row];       // next output slot (warp-uniform)
-    int carry_t = -1;        // t of the last event before this 1024-block
+    int pos = cu[row];
+    if (lane == 0) st[-1] = -1;
     for (int w0 = 0; w0 < n_words; w0 += 32) {
         const int w = w0 + lane;
         const uint32_t word = (w < n_words) ? mr[w] : 0u;
         const int c = __popc(word);
         const int incl = warp_inclusive_sum(c);
         const int total = __shfl_sync(kFull, incl, 31);
-        const int last_here = word ? (w * 32 + 31 - __clz(word)) : -1;
-        const int last_incl = warp_inclusive_max(last_here);
-        int prev = __shfl_up_sync(kFull, last_incl, 1);
-        if (lane == 0) prev = -1;
-        prev = max(prev, carry_t);
-        int p = pos + incl - c;
+        int o = incl - c;
         uint32_t bits = word;
         while (bits) {
             const int b = __ffs(bits) - 1;
             bits &= bits - 1;
-            const int t = w * 32 + b;
-            ch_ids[p] = (int32_t)row;
-            t_steps[p] = t;
-            k_flat[p] = (prev < 0) ? (t + 1) : (t - prev);
-            prev = t;
-            ++p;
+            st[o++] = w * 32 + b;
         }
+        __syncwarp();
+        for (int i = lane; i < total; i += 32) {
+            const int t = st[i];
+            const int prev = st[i - 1];
+            ch_ids[pos + i] = (int32_t)row;
+            t_steps[pos + i] = t;
+            k_flat[pos + i] = (prev < 0) ? (t + 1) : (t - prev);
+        }
+        __syncwarp();
+        if (lane == 0 && total > 0) st[-1] = st[total - 1];
+        __syncwarp();
         pos += total;
-        carry_t = max(carry_t, __shfl_sync(kFull, last_incl, 31));
     }
 }
 

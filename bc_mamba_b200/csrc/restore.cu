@@ -9,25 +9,34 @@
 // L.  dy[e] = sum of dout over [t_e, t_{e+1}) (L for the last addressable
 // event), 0 for unaddressable events, always fp32.
 //
-// Design (ours): a CTA owns one batch row b, 32 consecutive features d and a
-// range of positions.  It walks that range in windows of kTT positions.  For
-// each window, every channel's events are loaded 32 at a time by a warp
-// (coalesced) and each lane fills / sums its event's hold interval in a
-// shared-memory tile [kTT][33]; the tile is exchanged with HBM row by row so
-// every global access is a contiguous 32-feature row of (B, L, D).  This
-// replaces the reference's per-(t,d) binary search and its strided stores, and
-// the backward's fp32 atomics with a deterministic ordered sum: the CTA that
-// owns an event's start keeps reading past its range until the event ends.
+// Design (ours).  A CTA owns one batch row b, 32 consecutive features and a
+// range of positions, walked in windows of kTT = 128 positions:
+//   1. staging: each warp loads the window's events of 8 channels (32 events
+//      per coalesced load) and builds a 128-bit event mask per channel with
+//      warp OR-reductions (plus, forward, the event values in order);
+//   2. sweep: warp w takes positions [32w, 32w+32) of the window, lane c takes
+//      channel c, and walks them in order from its mask word: the forward
+//      writes the held value into a shared tile [128][32], the backward adds
+//      tile values and closes a segment at each set bit;
+//   3. the tile moves to or from HBM as 16-byte pieces of contiguous
+//      32-feature rows of (B, L, D).
+// No global load sits in the inner loop and every shared access is conflict
+// free.  The backward combines the four sub-window partials of each channel
+// in order and the CTA owning an event's start keeps reading past its range
+// until the event ends, so each dy is summed in one fixed order (the
+// reference uses fp32 atomics).
 #include "common.cuh"
 
 namespace bcm {
 namespace {
 
 constexpr int kDB = 32;       // features per CTA
-constexpr int kTT = 64;       // positions per window
-constexpr int kWarpsR = 4;    // warps per CTA (8 channels per warp)
+constexpr int kTT = 128;      // positions per window
+constexpr int kWarpsR = 4;    // warps per CTA; warp w sweeps positions [32w, 32w+32)
 constexpr int kChPerWarp = kDB / kWarpsR;
 constexpr int kCap = 4095;    // addressable events per channel (reference search limit)
+constexpr int kMW = kTT / 32; // mask words per channel and window
+constexpr int kMP = kMW + 1;  // padded mask pitch (conflict-free column reads)
 
 __device__ __forceinline__ int lower_bound_i32(const int32_t* a, int n, int key) {
     int lo = 0, hi = n;
@@ -38,80 +47,181 @@ __device__ __forceinline__ int lower_bound_i32(const int32_t* a, int n, int key)
     return lo;
 }
 
+template <typename T>
+__device__ __forceinline__ bool rows_vectorizable(int D, int d0, const void* p) {
+    constexpr int EPV = 16 / sizeof(T);
+    return (D % EPV == 0) && (d0 + kDB <= D) && (reinterpret_cast<uintptr_t>(p) % 16 == 0);
+}
+
+template <typename T>
+__device__ __forceinline__ void tile_store(const float (*tile)[kDB], T* out, int b, int L, int D,
+                                           int d0, int t0, int rows, bool vec) {
+    constexpr int EPV = 16 / sizeof(T);
+    constexpr int VPR = kDB / EPV;
+    if (vec) {
+        for (int idx = threadIdx.x; idx < rows * VPR; idx += kWarpsR * 32) {
+            const int r = idx / VPR, v = idx % VPR;
+            alignas(16) T pack[EPV];
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) pack[e] = from_f32<T>(tile[r][v * EPV + e]);
+            *reinterpret_cast<uint4*>(out + ((int64_t)b * L + t0 + r) * D + d0 + v * EPV) =
+                *reinterpret_cast<const uint4*>(pack);
+        }
+    } else {
+        for (int idx = threadIdx.x; idx < rows * kDB; idx += kWarpsR * 32) {
+            const int r = idx / kDB, c = idx % kDB;
+            if (d0 + c < D) out[((int64_t)b * L + t0 + r) * D + d0 + c] = from_f32<T>(tile[r][c]);
+        }
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void tile_load(float (*tile)[kDB], const T* src, int b, int L, int D, int d0,
+                                          int t0, int rows, bool vec) {
+    constexpr int EPV = 16 / sizeof(T);
+    constexpr int VPR = kDB / EPV;
+    if (vec) {
+        for (int idx = threadIdx.x; idx < kTT * VPR; idx += kWarpsR * 32) {
+            const int r = idx / VPR, v = idx % VPR;
+            alignas(16) T pack[EPV];
+            if (r < rows) {
+                *reinterpret_cast<uint4*>(pack) =
+                    *reinterpret_cast<const uint4*>(src + ((int64_t)b * L + t0 + r) * D + d0 + v * EPV);
+#pragma unroll
+                for (int e = 0; e < EPV; ++e) tile[r][v * EPV + e] = to_f32<T>(pack[e]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < EPV; ++e) tile[r][v * EPV + e] = 0.f;
+            }
+        }
+    } else {
+        for (int idx = threadIdx.x; idx < kTT * kDB; idx += kWarpsR * 32) {
+            const int r = idx / kDB, c = idx % kDB;
+            tile[r][c] = (r < rows && d0 + c < D)
+                             ? to_f32<T>(src[((int64_t)b * L + t0 + r) * D + d0 + c]) : 0.f;
+        }
+    }
+}
+
+// Staging of one channel's events in [t0, wend) starting at local index p:
+// sets the channel's mask words, optionally stores the values in order, and
+// returns the number of events taken (warp-uniform).  Events are loaded 32 at
+// a time with one coalesced load per array.
+template <typename Tin, bool VALUES>
+__device__ __forceinline__ int stage_channel(const int32_t* ts, const Tin* y, int beg, int n, int p,
+                                             int t0, int wend, uint32_t* mask, float* vals,
+                                             int lane, float& last_val) {
+    uint32_t m[kMW];
+#pragma unroll
+    for (int w = 0; w < kMW; ++w) m[w] = 0u;
+    int taken = 0;
+    while (true) {
+        const int j = p + taken + lane;
+        const int t = (j < n) ? ts[beg + j] : INT_MAX;
+        const bool valid = t >= t0 && t < wend && taken + lane < kTT;
+        const int cnt = __popc(__ballot_sync(kFull, valid));
+        const int rel = valid ? t - t0 : -1;
+#pragma unroll
+        for (int w = 0; w < kMW; ++w)
+            m[w] |= __reduce_or_sync(kFull, (valid && (rel >> 5) == w) ? (1u << (rel & 31)) : 0u);
+        if (VALUES) {
+            const float v = valid ? to_f32<Tin>(y[beg + j]) : 0.f;
+            if (valid) vals[taken + lane] = v;
+            if (cnt > 0) last_val = __shfl_sync(kFull, v, cnt - 1);
+        }
+        taken += cnt;
+        if (cnt < 32) break;
+    }
+    if (lane < kMW) {
+#pragma unroll
+        for (int w = 0; w < kMW; ++w)
+            if (lane == w) mask[w] = m[w];
+    }
+    return taken;
+}
+
 template <typename Tin, typename Tout>
 __global__ void __launch_bounds__(kWarpsR * 32)
 restore_fwd_kernel(const Tin* __restrict__ y, const int32_t* __restrict__ ts,
                    const int32_t* __restrict__ cu, int D, int L, int part_len,
                    int n_dblk, Tout* __restrict__ out) {
-    __shared__ float tile[kTT][kDB + 1];
-    __shared__ int s_ptr[kDB];     // next event (local index) with t >= window start
-    __shared__ int s_n[kDB];       // addressable events
-    __shared__ int s_beg[kDB];     // global index of the channel's first event
-    __shared__ float s_carry[kDB]; // value held at the window start
-
+    __shared__ __align__(16) float tile[kTT][kDB];
+    __shared__ float s_val[kDB][kTT + 1];    // event values of the window, in order
+    __shared__ uint32_t s_mask[kDB][kMP];
+    __shared__ float s_carry[kDB];           // value held at the window start
+    __shared__ int s_p[kDB];
     const int dblk = blockIdx.x % n_dblk;
     const int part = blockIdx.x / n_dblk;
     const int b = blockIdx.y;
     const int d0 = dblk * kDB;
     const int t_beg = part * part_len;
     const int t_end = min(L, t_beg + part_len);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool vec = rows_vectorizable<Tout>(D, d0, out);
 
-    if (tid < kDB) {
-        const int d = d0 + tid;
-        int beg = 0, n = 0, p = 0;
-        float carry = 0.f;
+    int c_beg[kChPerWarp], c_n[kChPerWarp];
+#pragma unroll
+    for (int ci = 0; ci < kChPerWarp; ++ci) {
+        const int d = d0 + warp * kChPerWarp + ci;
+        c_beg[ci] = 0; c_n[ci] = 0;
         if (d < D) {
             const int ch = b * D + d;
-            beg = cu[ch];
-            n = min(cu[ch + 1] - beg, kCap);
-            p = lower_bound_i32(ts + beg, n, t_beg);
-            if (p > 0) carry = to_f32<Tin>(y[beg + p - 1]);
+            c_beg[ci] = cu[ch];
+            c_n[ci] = min(cu[ch + 1] - c_beg[ci], kCap);
         }
-        s_ptr[tid] = p; s_n[tid] = n; s_beg[tid] = beg; s_carry[tid] = carry;
     }
-    __syncthreads();
+    if (lane < kChPerWarp) {
+        int beg = 0, n = 0;
+#pragma unroll
+        for (int ci = 0; ci < kChPerWarp; ++ci)
+            if (ci == lane) { beg = c_beg[ci]; n = c_n[ci]; }
+        const int p = lower_bound_i32(ts + beg, n, t_beg);
+        s_p[warp * kChPerWarp + lane] = p;
+        s_carry[warp * kChPerWarp + lane] = (p > 0) ? to_f32<Tin>(y[beg + p - 1]) : 0.f;
+    }
+    __syncwarp();
 
     for (int t0 = t_beg; t0 < t_end; t0 += kTT) {
         const int wend = min(t0 + kTT, t_end);
+        // 1. staging
+        float carry_new[kChPerWarp];
+        int p_new[kChPerWarp];
+#pragma unroll
         for (int ci = 0; ci < kChPerWarp; ++ci) {
             const int c = warp * kChPerWarp + ci;
-            if (d0 + c >= D) break;
-            const int n = s_n[c], beg = s_beg[c];
-            int p = s_ptr[c];
-            float carry = s_carry[c];
-            int fill_from = t0;
-            while (true) {
-                const int j = p + lane;
-                const int tj = (j < n) ? ts[beg + j] : INT_MAX;
-                const bool valid = tj < wend;
-                const unsigned vm = __ballot_sync(kFull, valid);
-                const int cnt = __popc(vm);
-                const int first_t = cnt ? __shfl_sync(kFull, tj, 0) : wend;
-                // hold the carried value up to the first event of this batch
-                for (int t = max(fill_from, t0) + lane; t < first_t; t += 32) tile[t - t0][c] = carry;
-                if (cnt == 0) break;
-                const float yj = valid ? to_f32<Tin>(y[beg + j]) : 0.f;
-                int tn = __shfl_down_sync(kFull, tj, 1);
-                if (lane == 31) tn = (p + 32 < n) ? ts[beg + p + 32] : INT_MAX;
-                const int seg_end = min(tn, wend);
-                if (valid)
-                    for (int t = max(tj, t0); t < seg_end; ++t) tile[t - t0][c] = yj;
-                carry = __shfl_sync(kFull, yj, cnt - 1);
-                const int last_end = __shfl_sync(kFull, seg_end, cnt - 1);
-                p += cnt;
-                fill_from = last_end;
-                if (cnt < 32 || last_end >= wend) break;
-            }
-            if (lane == 0) { s_ptr[c] = p; s_carry[c] = carry; }
+            const int p = s_p[c];
+            float last = s_carry[c];
+            const int taken = stage_channel<Tin, true>(ts, y, c_beg[ci], c_n[ci], p, t0, wend, s_mask[c],
+                                                       s_val[c], lane, last);
+            carry_new[ci] = last;
+            p_new[ci] = p + taken;
         }
         __syncthreads();
-        const int rows = wend - t0;
-        for (int idx = tid; idx < rows * kDB; idx += kWarpsR * 32) {
-            const int r = idx / kDB, c = idx % kDB;
-            if (d0 + c < D)
-                out[((int64_t)b * L + t0 + r) * D + d0 + c] = from_f32<Tout>(tile[r][c]);
+        // 2. sweep: lane = channel, this warp's 32 positions
+        {
+            const int c = lane;
+            uint32_t before = 0;
+#pragma unroll
+            for (int w = 0; w < kMW; ++w)
+                if (w < warp) before += __popc(s_mask[c][w]);
+            const uint32_t mw = s_mask[c][warp];
+            int e = (int)before;
+            float cur = e > 0 ? s_val[c][e - 1] : s_carry[c];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                if ((mw >> i) & 1u) cur = s_val[c][e++];
+                tile[warp * 32 + i][c] = cur;
+            }
         }
+        __syncthreads();
+        // advance the channel state (each warp updates its own 8 channels)
+        if (lane < kChPerWarp) {
+#pragma unroll
+            for (int ci = 0; ci < kChPerWarp; ++ci)
+                if (ci == lane) { s_p[warp * kChPerWarp + ci] = p_new[ci]; s_carry[warp * kChPerWarp + ci] = carry_new[ci]; }
+        }
+        // 3. tile -> rows of (B, L, D)
+        tile_store<Tout>(tile, out, b, L, D, d0, t0, wend - t0, vec);
         __syncthreads();
     }
 }
@@ -121,130 +231,129 @@ __global__ void __launch_bounds__(kWarpsR * 32)
 restore_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ ts,
                    const int32_t* __restrict__ cu, int D, int L, int part_len,
                    int n_dblk, float* __restrict__ dy) {
-    // Per channel: p = next event (local index) whose start is not processed,
-    // open = event whose hold interval is running (-1: none of ours), acc = its
-    // partial sum.  Events starting in [t_beg, t_own_end) are owned here; the
-    // CTA keeps reading past t_own_end until each owned interval has ended.
-    __shared__ float tile[kTT][kDB + 1];
-    __shared__ int s_ptr[kDB];
-    __shared__ int s_n[kDB];
-    __shared__ int s_beg[kDB];
-    __shared__ int s_open[kDB];
-    __shared__ float s_acc[kDB];
-    __shared__ int s_any_open;
-
+    __shared__ __align__(16) float tile[kTT][kDB];
+    __shared__ uint32_t s_mask[kDB][kMP];
+    __shared__ float s_head[kWarpsR][kDB], s_tail[kWarpsR][kDB];
+    __shared__ int s_cnt[kWarpsR][kDB];
+    __shared__ int s_p[kDB];
+    __shared__ int s_any;
     const int dblk = blockIdx.x % n_dblk;
     const int part = blockIdx.x / n_dblk;
     const int b = blockIdx.y;
     const int d0 = dblk * kDB;
     const int t_beg = part * part_len;
     const int t_own_end = min(L, t_beg + part_len);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool vec = rows_vectorizable<T>(D, d0, dout);
 
-    if (tid < kDB) {
-        const int d = d0 + tid;
-        int beg = 0, n = 0, p = 0;
+    int c_beg[kChPerWarp], c_n[kChPerWarp];
+#pragma unroll
+    for (int ci = 0; ci < kChPerWarp; ++ci) {
+        const int d = d0 + warp * kChPerWarp + ci;
+        c_beg[ci] = 0; c_n[ci] = 0;
         if (d < D) {
             const int ch = b * D + d;
-            beg = cu[ch];
-            const int n_all = cu[ch + 1] - beg;
-            n = min(n_all, kCap);
-            p = lower_bound_i32(ts + beg, n, t_beg);
+            c_beg[ci] = cu[ch];
+            const int n_all = cu[ch + 1] - c_beg[ci];
+            c_n[ci] = min(n_all, kCap);
             if (part == 0)  // events past the search cap receive no gradient
-                for (int j = kCap; j < n_all; ++j) dy[beg + j] = 0.f;
+                for (int j = kCap + lane; j < n_all; j += 32) dy[c_beg[ci] + j] = 0.f;
         }
-        s_ptr[tid] = p; s_n[tid] = n; s_beg[tid] = beg;
-        s_open[tid] = -1;
-        s_acc[tid] = 0.f;
     }
+    if (lane < kChPerWarp) {
+        int beg = 0, n = 0;
+#pragma unroll
+        for (int ci = 0; ci < kChPerWarp; ++ci)
+            if (ci == lane) { beg = c_beg[ci]; n = c_n[ci]; }
+        s_p[warp * kChPerWarp + lane] = lower_bound_i32(ts + beg, n, t_beg);
+    }
+    // interval bookkeeping of channel `lane` (threads of warp 0 only):
+    // open = global index of the event whose interval is running (ours), -1 none
+    int open = -1;
+    float open_acc = 0.f;
+    int p_next[kChPerWarp];
+    const int my_d = d0 + lane;
+    const int my_beg = (warp == 0 && my_d < D) ? cu[b * D + my_d] : 0;
     __syncthreads();
 
     for (int t0 = t_beg; t0 < L; t0 += kTT) {
         const bool owning = t0 < t_own_end;
-        const int wend = min(t0 + kTT, owning ? t_own_end : L);
         if (!owning) {
-            if (tid == 0) {
-                int any = 0;
-                for (int c = 0; c < kDB; ++c) any |= (s_open[c] >= 0);
-                s_any_open = any;
-            }
+            if (threadIdx.x == 0) s_any = 0;
             __syncthreads();
-            if (!s_any_open) break;
+            if (warp == 0 && open >= 0) s_any = 1;
+            __syncthreads();
+            if (!s_any) break;
         }
-        const int rows = wend - t0;
-        for (int idx = tid; idx < rows * kDB; idx += kWarpsR * 32) {
-            const int r = idx / kDB, c = idx % kDB;
-            tile[r][c] = (d0 + c < D) ? to_f32<T>(dout[((int64_t)b * L + t0 + r) * D + d0 + c]) : 0.f;
+        const int wend = min(t0 + kTT, L);
+        // 1. tile + staging (event masks only).  Each warp first publishes the
+        //    advanced pointers of its own channels from the previous window (the
+        //    previous combine read the old values).
+        tile_load<T>(tile, dout, b, L, D, d0, t0, wend - t0, vec);
+        if (t0 != t_beg && lane < kChPerWarp) {
+#pragma unroll
+            for (int ci = 0; ci < kChPerWarp; ++ci)
+                if (ci == lane) s_p[warp * kChPerWarp + ci] = p_next[ci];
         }
-        __syncthreads();
+        __syncwarp();
+#pragma unroll
         for (int ci = 0; ci < kChPerWarp; ++ci) {
             const int c = warp * kChPerWarp + ci;
-            if (d0 + c >= D) break;
-            const int n = s_n[c], beg = s_beg[c];
-            int p = s_ptr[c];
-            int open = s_open[c];
-            float acc = s_acc[c];
-            if (!owning) {
-                if (open >= 0) {
-                    const int tn = (open + 1 < n) ? ts[beg + open + 1] : INT_MAX;
-                    const int stop = min(tn, wend);
-                    float s = 0.f;
-                    for (int t = t0 + lane; t < stop; t += 32) s += tile[t - t0][c];
+            float dummy = 0.f;
+            const int p = s_p[c];
+            p_next[ci] = p + stage_channel<T, false>(ts, nullptr, c_beg[ci], c_n[ci], p, t0, wend,
+                                                     s_mask[c], nullptr, lane, dummy);
+        }
+        __syncthreads();
+        // 2. sweep: lane = channel, positions [32w, 32w+32) of the window
+        {
+            const int c = lane;
+            uint32_t before = 0;
 #pragma unroll
-                    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(kFull, s, off);
-                    acc += s;
-                    if (tn <= wend) {
-                        if (lane == 0) dy[beg + open] = acc;
-                        open = -1;
-                        acc = 0.f;
-                    }
+            for (int w = 0; w < kMW; ++w)
+                if (w < warp) before += __popc(s_mask[c][w]);
+            const uint32_t mw = s_mask[c][warp];
+            const int cbeg = (d0 + c < D) ? cu[b * D + d0 + c] : 0;
+            const int ebase = cbeg + s_p[c] + (int)before;   // global index of this piece's first event
+            float acc = 0.f, head = 0.f;
+            int e = 0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                if ((mw >> i) & 1u) {
+                    if (e == 0) head = acc;
+                    else if (owning) dy[ebase + e - 1] = acc;   // interval inside the piece
+                    acc = 0.f;
+                    ++e;
                 }
-            } else {
-                int from = t0;
-                while (true) {
-                    const int j = p + lane;
-                    const int tj = (j < n) ? ts[beg + j] : INT_MAX;
-                    const bool valid = tj < wend;
-                    const int cnt = __popc(__ballot_sync(kFull, valid));
-                    const int first_t = cnt ? __shfl_sync(kFull, tj, 0) : wend;
-                    // [from, first_t) still belongs to the open interval
-                    float s = 0.f;
-                    for (int t = max(from, t0) + lane; t < first_t; t += 32) s += tile[t - t0][c];
+                acc += tile[warp * 32 + i][c];
+            }
+            if (e == 0) head = acc;
+            s_head[warp][c] = head;
+            s_tail[warp][c] = acc;
+            s_cnt[warp][c] = e;
+        }
+        __syncthreads();
+        // 3. ordered combine of the four pieces (warp 0, lane = channel)
+        if (warp == 0 && my_d < D) {
+            const int c = lane;
+            int ebase = my_beg + s_p[c];
 #pragma unroll
-                    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(kFull, s, off);
-                    acc += s;
-                    if (cnt == 0) break;
-                    if (open >= 0 && lane == 0) dy[beg + open] = acc;  // next event ended it
-                    // each valid lane owns [tj, tn)
-                    int tn = __shfl_down_sync(kFull, tj, 1);
-                    if (lane == 31) tn = (p + 32 < n) ? ts[beg + p + 32] : INT_MAX;
-                    const int seg_end = min(tn, wend);
-                    float v = 0.f;
-                    if (valid)
-                        for (int t = max(tj, t0); t < seg_end; ++t) v += tile[t - t0][c];
-                    if (valid && tn <= wend) dy[beg + j] = v;
-                    const int tn_last = __shfl_sync(kFull, tn, cnt - 1);
-                    const float v_last = __shfl_sync(kFull, v, cnt - 1);
-                    p += cnt;
-                    if (tn_last <= wend) {
-                        open = -1;
-                        acc = 0.f;
-                        from = tn_last;
-                        if (cnt < 32 || tn_last >= wend) break;
-                    } else {
-                        open = p - 1;
-                        acc = v_last;
-                        break;
-                    }
+            for (int w = 0; w < kWarpsR; ++w) {
+                const int cnt = s_cnt[w][c];
+                if (cnt > 0) {
+                    if (open >= 0) dy[open] = open_acc + s_head[w][c];
+                    ebase += cnt;
+                    open = owning ? ebase - 1 : -1;
+                    open_acc = s_tail[w][c];
+                } else {
+                    open_acc += s_head[w][c];
                 }
             }
-            if (lane == 0) { s_ptr[c] = p; s_open[c] = open; s_acc[c] = acc; }
         }
         __syncthreads();
     }
     // intervals still open at L end there
-    if (tid < kDB && d0 + tid < D && s_open[tid] >= 0)
-        dy[s_beg[tid] + s_open[tid]] = s_acc[tid];
+    if (warp == 0 && my_d < D && open >= 0) dy[open] = open_acc;
 }
 
 }  // namespace
@@ -253,12 +362,12 @@ restore_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ ts,
 using namespace bcm;
 
 static int restore_part_len(int64_t n_blocks_2d, int64_t L) {
-    // Enough CTAs to cover the SMs several times, windows of kTT positions.
-    const int64_t target = (int64_t)sm_count() * 8;
+    // Enough CTAs to cover the SMs several times; whole windows per part.
+    const int64_t target = (int64_t)sm_count() * 12;
     int64_t parts = std::max<int64_t>(1, target / std::max<int64_t>(1, n_blocks_2d));
     int64_t len = (L + parts - 1) / parts;
-    len = std::max<int64_t>(kTT * 4, (len + kTT - 1) / kTT * kTT);
-    return (int)std::min<int64_t>(len, std::max<int64_t>(L, 1));
+    len = std::max<int64_t>(kTT * 2, (len + kTT - 1) / kTT * kTT);
+    return (int)std::min<int64_t>(len, std::max<int64_t>((L + kTT - 1) / kTT * kTT, kTT));
 }
 
 extern "C" bcm_status bcm_restore_dense_fwd(const void* y_flat, bcm_dtype y_dtype,
@@ -273,7 +382,7 @@ extern "C" bcm_status bcm_restore_dense_fwd(const void* y_flat, bcm_dtype y_dtyp
     BCM_REQUIRE(dim >= 1 && seqlen >= 1 && n_channels >= 1 && n_events >= 0,
                 "restore_dense_fwd: bad sizes");
     BCM_REQUIRE(n_channels % dim == 0, "restore_dense_fwd: n_channels must be divisible by dim");
-    BCM_REQUIRE(seqlen < (1ll << 31) - 64, "restore_dense_fwd: seqlen too large");
+    BCM_REQUIRE(seqlen < (1ll << 31) - 2 * kTT, "restore_dense_fwd: seqlen too large");
     BCM_REQUIRE(out && cu_seqlens && (n_events == 0 || (y_flat && time_steps)),
                 "restore_dense_fwd: null pointer");
     const int64_t B = n_channels / dim;
@@ -309,6 +418,7 @@ extern "C" bcm_status bcm_restore_dense_bwd(const void* dout, bcm_dtype dtype,
     BCM_REQUIRE(dim >= 1 && seqlen >= 1 && n_channels >= 0 && n_events >= 0,
                 "restore_dense_bwd: bad sizes");
     BCM_REQUIRE(n_channels % dim == 0, "restore_dense_bwd: n_channels must be divisible by dim");
+    BCM_REQUIRE(seqlen < (1ll << 31) - 2 * kTT, "restore_dense_bwd: seqlen too large");
     if (n_events == 0 || n_channels == 0) return BCM_OK;
     BCM_REQUIRE(dout && time_steps && cu_seqlens && dy, "restore_dense_bwd: null pointer");
     const int64_t B = n_channels / dim;

@@ -181,6 +181,11 @@ dw_bwd_kernel(ScanArgs a) {
                 if (HAS_Z && ok) dg = gate_bwd<T>(a, beg + jb + i, dg, q == 0);
                 dv[i] = dg;
             }
+            // tile-local partial sums, folded into the totals after the tile
+            // (pairwise summation keeps long channels accurate in fp32)
+            float tSA[G], tSB[G], tQE[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) tSA[g] = tSB[g] = tQE[g] = 0.f;
             // forward recompute of the tile
             float eti[kCkpt][G], deci[kCkpt][G], teta[kCkpt];
 #pragma unroll
@@ -197,7 +202,7 @@ dw_bwd_kernel(ScanArgs a) {
                     eti[i][g] = et[g];
                     deci[i][g] = dec;
                     te = fmaf(cc[g], et[g], te);
-                    QE[g] = fmaf(qv, et[g], QE[g]);
+                    tQE[g] = fmaf(qv, et[g], tQE[g]);
                 }
                 teta[i] = te;
             }
@@ -216,9 +221,9 @@ dw_bwd_kernel(ScanArgs a) {
                         gam[g] = fmaf(anx[g], gam[g], qv);
                         const float e = eti[i][g] - w;
                         const float pr = gam[g] * e;
-                        SA[g] = fmaf(pr, delta, SA[g]);
+                        tSA[g] = fmaf(pr, delta, tSA[g]);
                         ta = fmaf(ccA[g], pr, ta);
-                        SB[g] = fmaf(gam[g], w, SB[g]);
+                        tSB[g] = fmaf(gam[g], w, tSB[g]);
                         tg = fmaf(cc[g], gam[g], tg);
                         anx[g] = deci[i][g];
                     }
@@ -232,7 +237,10 @@ dw_bwd_kernel(ScanArgs a) {
                 tgam[i] = group_sum<LPC>(tgam[i]);
                 tdA[i] = group_sum<LPC>(tdA[i]);
             }
+#pragma unroll
+            for (int g = 0; g < G; ++g) { SA[g] += tSA[g]; SB[g] += tSB[g]; QE[g] += tQE[g]; }
             if (q == 0) {
+                float t_ddi = 0.f, t_dda = 0.f, t_dD = 0.f;
 #pragma unroll
                 for (int i = 0; i < kCkpt; ++i) {
                     if (i < cnt) {
@@ -240,11 +248,14 @@ dw_bwd_kernel(ScanArgs a) {
                         const float duv = fmaf(Dv, dv[i], fmaf(2.f * uv[i] * delta, tgam[i], dv[i] * teta[i]));
                         du[jb + i] = from_f32<T>(duv);
                         const float ddel = fmaf(uv[i] * uv[i], tgam[i], tdA[i]);
-                        s_ddi = fmaf(ddel, (float)(kv[i] - 1), s_ddi);
-                        s_dda += ddel;
-                        s_dD = fmaf(dv[i], uv[i], s_dD);
+                        t_ddi = fmaf(ddel, (float)(kv[i] - 1), t_ddi);
+                        t_dda += ddel;
+                        t_dD = fmaf(dv[i], uv[i], t_dD);
                     }
                 }
+                s_ddi += t_ddi;
+                s_dda += t_dda;
+                s_dD += t_dD;
             }
         }
     }
@@ -374,6 +385,9 @@ gen_bwd_kernel(ScanArgs a) {
                 if (HAS_Z && ok) dg = gate_bwd<T>(a, beg + jb + i, dg, q == 0);
                 dv[i] = dg;
             }
+            float tSA[G], tSB[G], tSC[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) tSA[g] = tSB[g] = tSC[g] = 0.f;
             float hi[kCkpt][G], deci[kCkpt][G];
 #pragma unroll
             for (int i = 0; i < kCkpt; ++i) {
@@ -413,11 +427,11 @@ gen_bwd_kernel(ScanArgs a) {
                         const float gB = gg[g] * Bv;
                         t1 = fmaf(gB, delta, t1);                       // du via B*delta*u
                         t2 = fmaf(gB, uv[i], fmaf(gg[g] * Ar[g], e, t2)); // ddelta
-                        SA[g] = fmaf(gg[g] * delta, e, SA[g]);
+                        tSA[g] = fmaf(gg[g] * delta, e, tSA[g]);
                         const float dBv = gg[g] * delta * uv[i];
                         const float dCv = dv[i] * hi[i][g];
-                        if (a.b_variable) { if (bi >= 0) a.dB_ev[bi] = dBv; } else SB[g] += dBv;
-                        if (a.c_variable) { if (ci >= 0) a.dC_ev[ci] = dCv; } else SC[g] += dCv;
+                        if (a.b_variable) { if (bi >= 0) a.dB_ev[bi] = dBv; } else tSB[g] += dBv;
+                        if (a.c_variable) { if (ci >= 0) a.dC_ev[ci] = dCv; } else tSC[g] += dCv;
                         anx[g] = deci[i][g];
                     }
                 }
@@ -429,16 +443,22 @@ gen_bwd_kernel(ScanArgs a) {
                 tdu[i] = group_sum<LPC>(tdu[i]);
                 tdd[i] = group_sum<LPC>(tdd[i]);
             }
+#pragma unroll
+            for (int g = 0; g < G; ++g) { SA[g] += tSA[g]; SB[g] += tSB[g]; SC[g] += tSC[g]; }
             if (q == 0) {
+                float t_ddi = 0.f, t_dda = 0.f, t_dD = 0.f;
 #pragma unroll
                 for (int i = 0; i < kCkpt; ++i) {
                     if (i < cnt) {
                         du[jb + i] = from_f32<T>(fmaf(Dv, dv[i], tdu[i]));
-                        s_ddi = fmaf(tdd[i], (float)(kv[i] - 1), s_ddi);
-                        s_dda += tdd[i];
-                        s_dD = fmaf(dv[i], uv[i], s_dD);
+                        t_ddi = fmaf(tdd[i], (float)(kv[i] - 1), t_ddi);
+                        t_dda += tdd[i];
+                        t_dD = fmaf(dv[i], uv[i], t_dD);
                     }
                 }
+                s_ddi += t_ddi;
+                s_dda += t_dda;
+                s_dD += t_dD;
             }
         }
     }
@@ -550,6 +570,8 @@ BwdLayout bwd_layout(const bcm_flat_ch_args* p) {
     int G, LPC;
     pick_layout((int)p->dstate, G, LPC);
     L.NP = G * LPC;
+    if (p->bc_mode == BCM_BC_DEPTHWISE && dw_fast_supported((int)p->dstate))
+        L.NP = dw_fast_np((int)p->dstate);
     L.part_stride = (3 * L.NP + 3 + 3) / 4 * 4;
     const size_t slots = (size_t)(p->n_events >> 3) + (size_t)p->n_channels + 1;
     L.ckpt_off = 0;
@@ -607,7 +629,10 @@ extern "C" bcm_status bcm_flat_ch_bwd(const bcm_flat_ch_args* p, cudaStream_t st
         a.C = WC_eff;
     }
     // every channel writes its partial row, so no clearing is needed
-    if (p->n_events > 0) {
+    if (p->n_events > 0 && dw && dw_fast_supported(a.dstate)) {
+        st = dw_fast_launch(a, p->dtype, true, stream);
+        if (st != BCM_OK) return st;
+    } else if (p->n_events > 0) {
         st = dispatch_dtype(p->dtype, [&](auto tag) -> bcm_status {
             using T = decltype(tag);
             return launch_bwd<T>(a, dw, p->z != nullptr, stream);

@@ -36,16 +36,11 @@ struct ScanArgs {
     int part_stride;  // floats per channel in ws_part
 };
 
-// exp2 of an argument already clamped to [-126, 126]: the hardware
-// approximation is exact enough there and needs no subnormal path.
-__device__ __forceinline__ float ex2_clamped(float e) {
-    float r;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(e));
-    return r;
-}
-
+// Decay factor exp2(clamp(delta*A2, -126, 126)) with the accurate exp2f
+// (as the reference): with long-memory states (a close to 1) a biased
+// approximation would compound over ~1/(1-a) events.
 __device__ __forceinline__ float decay_fast(float delta, float A2) {
-    return ex2_clamped(fmaxf(fminf(delta * A2, 126.0f), -126.0f));
+    return exp2f(fmaxf(fminf(delta * A2, 126.0f), -126.0f));
 }
 
 // delta of an event with gap k: dt_idle*(k-1) + dt_active (one rounding, as
@@ -100,5 +95,10 @@ inline void pick_layout(int N, int& G, int& LPC) {
         LPC = 32;
     }
 }
+
+// Depthwise fast path (scan_dw.cu), used for dstate <= 64.
+bool dw_fast_supported(int dstate);
+int dw_fast_np(int dstate);
+bcm_status dw_fast_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t st);
 
 }  // namespace bcm

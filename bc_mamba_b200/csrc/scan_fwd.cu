@@ -331,6 +331,7 @@ extern "C" bcm_status bcm_flat_ch_fwd(const bcm_flat_ch_args* p, cudaStream_t st
     if (p->n_events == 0) return BCM_OK;
     const bool dw = p->bc_mode == BCM_BC_DEPTHWISE;
     const bool has_z = p->z != nullptr;
+    if (dw && dw_fast_supported(a.dstate)) return dw_fast_launch(a, p->dtype, false, stream);
     return dispatch_dtype(p->dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);
         return launch_fwd<T>(a, dw, has_z, stream);

@@ -180,6 +180,24 @@ def gather_events(x_conv, channel_ids_i32, time_steps_i32):
     return GatherEventsFn.apply(x_conv, channel_ids_i32, time_steps_i32)
 
 
+def extract_events_base(base_input, x_conv, threshold: float, expand: int):
+    """Extraction from the (B, d_model, L) layout extract_base_events takes
+    (what Mamba.extract_events_1d builds by transposing hidden_states), then
+    expansion and the gather of x_conv (B, D, L).
+
+    Returns (channel_ids, time_steps, k_flat, cu_seqlens, max_seqlen, x_conv_flat).
+    """
+    ops = load_ops()
+    B, d_model, L = base_input.shape
+    with cuda_stage("routing_index_extraction"):
+        bch, bt, bk, bcu, _counts, _bmax = ops.extract_base_events(base_input, threshold)
+    with cuda_stage("active_token_packing"):
+        ch, ts, kf, cu, mx = ops.expand_base_events(bch, bt, bk, bcu, B, d_model, expand)
+        max_seqlen = int(mx.item())
+    x_flat = gather_events(x_conv, ch, ts)
+    return ch, ts, kf, cu, max_seqlen, x_flat
+
+
 def extract_events_1d(hidden_states, x_conv, threshold: float, expand: int):
     """Threshold (B, L, d_model) spikes into the expanded event stream and
     gather x_conv (B, D, L) at the events, like Mamba.extract_events_1d.

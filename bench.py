@@ -62,13 +62,20 @@ class ClockSampler:
         self._t = None
 
     def start(self):
+        """Start sampling and wait for the first sample (nvidia-smi start-up
+        must not overlap the timed region)."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0:
+                time.sleep(0.05)
+            time.sleep(0.2)
+            self.skip = len(self.lines)
         except Exception:
             self.proc = None
         return self
@@ -87,7 +94,7 @@ class ClockSampler:
             self.proc.kill()
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[getattr(self, "skip", 0):]:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -140,7 +147,7 @@ def run_ours(args):
     ops = load_ops()
     inp = make_inputs(cfg, device=dev, rank=rank)
     thr = inp["threshold"]
-    hs = inp["v"].transpose(1, 2).contiguous()          # spikes as (B, L, d_model)
+    hs = inp["v"].contiguous()   # membrane in the (B, d_model, L) layout extract_base_events takes
     names = ["dt_idle", "dt_active", "A", "W_B", "W_C", "D"]
     params = {n: inp[n].clone().requires_grad_(True) for n in names}
     bucket = dp.GradBucket([params[n] for n in names]) if world > 1 else None
@@ -148,7 +155,7 @@ def run_ours(args):
 
     def step(hs_, u_, dout_):
         u = u_.requires_grad_(True) if not u_.requires_grad else u_
-        ch, ts, kf, cu, mx, u_flat = itf.extract_events_1d(hs_, u, thr, cfg.expand)
+        ch, ts, kf, cu, mx, u_flat = itf.extract_events_base(hs_, u, thr, cfg.expand)
         y, _x = itf.selective_scan_flat_ch_fn(u_flat, kf, cu, mx, params["dt_idle"], params["dt_active"],
                                               params["A"], params["W_B"], params["W_C"], params["D"], None,
                                               is_depthwise_bc=True)
@@ -279,7 +286,7 @@ def time_ops(ops, itf, cfg, hs, u_dev, inp, params, thr, flush, reps=5):
     p = params
     res = {k: 0.0 for k in ["extract", "expand", "gather_fwd", "scan_fwd", "restore_fwd", "restore_bwd",
                             "scan_bwd", "gather_bwd"]}
-    base = hs.transpose(1, 2).contiguous()
+    base = hs
 
     def timed(key, fn):
         flush.zero_()
@@ -402,7 +409,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c1")

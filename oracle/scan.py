@@ -90,7 +90,7 @@ def _bc_pad(P: _Pad, W, mode, var, u_pad, toff, cs, N):
 
 
 def _prepare(u, k, cu, max_seqlen, dt_idle, dt_active, A, B, C, tile_offsets, is_depthwise_bc,
-             pw_B, pw_C):
+             pw_B, pw_C, fp32_decay=False):
     u = np.asarray(u)
     E = u.size
     A = np.asarray(A, np.float64)
@@ -112,7 +112,19 @@ def _prepare(u, k, cu, max_seqlen, dt_idle, dt_active, A, B, C, tile_offsets, is
     delta = dti * (k_pad - 1.0) + dta
     delta[~P.mask] = 0.0
     Ad = A[P.d]  # (NC, N)
-    a = np.exp2(np.clip(delta[:, :, None] * Ad[:, None, :] * LOG2E, -126.0, 126.0))
+    if fp32_decay:
+        # The decays exactly as the reference kernel forms them in fp32
+        # (selective_scan_fwd_kernel.cuh:545, :559, :650-651): delta by one fused
+        # multiply-add, A*log2e rounded to fp32, their product rounded, clamped,
+        # exp2 rounded to fp32.  With near-uniform gaps and long memory (a ~ 1)
+        # every event reuses the same rounded decay, so its rounding compounds
+        # over ~1/(1-a) events; this mode reproduces that arithmetic.
+        delta = delta.astype(np.float32).astype(np.float64)
+        A2 = (Ad * LOG2E).astype(np.float32).astype(np.float64)
+        x = (delta[:, :, None] * A2[:, None, :]).astype(np.float32).astype(np.float64)
+        a = np.exp2(np.clip(x, -126.0, 126.0)).astype(np.float32).astype(np.float64)
+    else:
+        a = np.exp2(np.clip(delta[:, :, None] * Ad[:, None, :] * LOG2E, -126.0, 126.0))
     a[~P.mask] = 1.0
     Bp = _bc_pad(P, B, mode, b_var, u_pad, tile_offsets, cs, N)
     Cp = _bc_pad(P, C, mode, c_var, u_pad, tile_offsets, cs, N)
@@ -132,10 +144,10 @@ def _forward(S):
 
 
 def scan_fwd(u, k, cu, max_seqlen, dt_idle, dt_active, A, B, C, D=None, z=None,
-             tile_offsets=None, is_depthwise_bc=False, pw_B=None, pw_C=None):
+             tile_offsets=None, is_depthwise_bc=False, pw_B=None, pw_C=None, fp32_decay=False):
     """Returns (out[E], x[NC, n_chunks, 2N], out_z or None), float64."""
     S = _prepare(u, k, cu, max_seqlen, dt_idle, dt_active, A, B, C, tile_offsets,
-                 is_depthwise_bc, pw_B, pw_C)
+                 is_depthwise_bc, pw_B, pw_C, fp32_decay)
     P, N = S["P"], S["N"]
     hs = _forward(S)
     y = (hs * S["Cp"]).sum(-1)
@@ -161,11 +173,11 @@ def scan_fwd(u, k, cu, max_seqlen, dt_idle, dt_active, A, B, C, D=None, z=None,
 
 
 def scan_bwd(u, k, cu, max_seqlen, dt_idle, dt_active, A, B, C, dout, D=None, z=None, out=None,
-             tile_offsets=None, is_depthwise_bc=False, pw_B=None, pw_C=None):
+             tile_offsets=None, is_depthwise_bc=False, pw_B=None, pw_C=None, fp32_decay=False):
     """Gradients in the reference's return order:
     [du, dA, dB (or dW_B), dC (or dW_C), ddt_idle, ddt_active, (dD), (dz), (dpw_B, dpw_C)]."""
     S = _prepare(u, k, cu, max_seqlen, dt_idle, dt_active, A, B, C, tile_offsets,
-                 is_depthwise_bc, pw_B, pw_C)
+                 is_depthwise_bc, pw_B, pw_C, fp32_decay)
     P, N, dim, E = S["P"], S["N"], S["dim"], S["E"]
     mode = S["mode"]
     hs = _forward(S)
