@@ -25,6 +25,7 @@ ABI_SYMBOLS = (
     "bcm_extract_base_fill",
     "bcm_expand_base_events",
     "bcm_gather_events_fwd",
+    "bcm_gather_bwd_workspace_bytes",
     "bcm_gather_events_bwd",
     "bcm_flat_ch_fwd_workspace_bytes",
     "bcm_flat_ch_bwd_workspace_bytes",

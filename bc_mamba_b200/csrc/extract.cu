@@ -206,10 +206,94 @@ __global__ void gather_kernel(const T* __restrict__ x, int64_t n_ch, int L,
     }
 }
 
+// ---- gather backward --------------------------------------------------------
+// Pass A: row boundaries of a channel-sorted stream (row_start[r] = first event
+// of row r, row_start[NC] = E) and an order check: channel_ids must be
+// non-decreasing and inside [0, NC); otherwise *flag = 1.
+__global__ void row_bounds_kernel(const int32_t* __restrict__ ch, int64_t n_events, int64_t n_ch,
+                                  int32_t* __restrict__ row_start, int32_t* __restrict__ flag) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e <= n_events; e += stride) {
+        const int64_t c = (e < n_events) ? (int64_t)ch[e] : n_ch;
+        const int64_t prev = (e > 0) ? (int64_t)ch[e - 1] : -1;
+        if ((e < n_events && (c < 0 || c >= n_ch)) || c < prev || prev >= n_ch) {
+            *flag = 1;
+            continue;
+        }
+        for (int64_t r = prev + 1; r <= c; ++r) row_start[r] = (int32_t)e;
+    }
+}
+
+// Pass B: one warp per row writes the whole row of dx (zeros and the event
+// values) in chunks of 32*V positions with vector stores; the row's events are
+// staged 32 at a time into a shared chunk buffer.  Rows whose times are not
+// strictly increasing inside [0, L) raise *flag.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(128)
+dense_rows_kernel(const T* __restrict__ g, const int32_t* __restrict__ ts,
+                  const int32_t* __restrict__ row_start, const int32_t* __restrict__ flag,
+                  int64_t n_ch, int L, T* __restrict__ dx, int32_t* __restrict__ flag_out) {
+    constexpr int V = 16 / sizeof(T);
+    constexpr int CH = 32 * V;             // positions per chunk
+    __shared__ __align__(16) T s_chunk[4][CH];
+    if (*flag) return;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t r = (int64_t)blockIdx.x * 4 + w;
+    if (r >= n_ch) return;
+    T* row = dx + r * (int64_t)L;
+    T* buf = s_chunk[w];
+    int e = row_start[r];
+    const int e_end = row_start[r + 1];
+    int prev_t = -1;
+    for (int c0 = 0; c0 < L; c0 += CH) {
+        const int cend = min(c0 + CH, L);
+#pragma unroll
+        for (int v = 0; v < V; ++v) buf[lane * V + v] = from_f32<T>(0.f);
+        __syncwarp();
+        while (e < e_end) {
+            const int j = e + lane;
+            const int t = (j < e_end) ? ts[j] : INT_MAX;
+            const bool in = t < cend;
+            const unsigned m = __ballot_sync(kFull, in);
+            const int cnt = __popc(m);
+            // order check: strictly increasing times inside [0, L)
+            int tp = __shfl_up_sync(kFull, t, 1);
+            if (lane == 0) tp = prev_t;
+            if (in && (t <= tp || t < c0)) atomicExch(flag_out, 1);
+            if (in) buf[t - c0 < 0 ? 0 : t - c0] = g[j];
+            if (cnt > 0) prev_t = __shfl_sync(kFull, t, cnt - 1);
+            e += cnt;
+            if (cnt < 32) break;
+        }
+        __syncwarp();
+        if (VEC) {
+            const int pos = c0 + lane * V;
+            if (pos < cend)
+                *reinterpret_cast<uint4*>(row + pos) = *reinterpret_cast<const uint4*>(buf + lane * V);
+        } else {
+            for (int p = lane; p < cend - c0; p += 32) row[c0 + p] = buf[p];
+        }
+        __syncwarp();
+    }
+    if (lane == 0 && e != e_end) atomicExch(flag_out, 1);  // events at t >= L
+}
+
+// Fallback for any other event order (runs only when *flag is set):
+// zero-fill, then scatter in stream order (reference
+// extract_events_cuda.cu:649-662, 731).
 template <typename T>
-__global__ void scatter_kernel(const T* __restrict__ g, const int32_t* __restrict__ ch,
-                               const int32_t* __restrict__ ts, int64_t n_events,
-                               int64_t n_ch, int L, T* __restrict__ dx) {
+__global__ void fallback_zero_kernel(const int32_t* __restrict__ flag, T* __restrict__ dx, int64_t n) {
+    if (!*flag) return;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        dx[i] = from_f32<T>(0.f);
+}
+
+template <typename T>
+__global__ void fallback_scatter_kernel(const int32_t* __restrict__ flag, const T* __restrict__ g,
+                                        const int32_t* __restrict__ ch, const int32_t* __restrict__ ts,
+                                        int64_t n_events, int64_t n_ch, int L, T* __restrict__ dx) {
+    if (!*flag) return;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_events; e += stride) {
         const int c = ch[e], t = ts[e];
@@ -375,25 +459,62 @@ extern "C" bcm_status bcm_gather_events_fwd(const void* x, bcm_dtype dtype, int6
     });
 }
 
+extern "C" size_t bcm_gather_bwd_workspace_bytes(int64_t n_channels) {
+    if (n_channels < 0) return 0;
+    return align_up((size_t)(n_channels + 1 + 64) * sizeof(int32_t), 256);
+}
+
 extern "C" bcm_status bcm_gather_events_bwd(const void* grad, bcm_dtype dtype,
                                             const int32_t* channel_ids,
                                             const int32_t* time_steps, int64_t n_events,
                                             int64_t n_channels, int64_t seqlen, void* dx,
+                                            void* workspace, size_t workspace_bytes,
                                             cudaStream_t stream) {
     clear_error();
     BCM_REQUIRE(dtype_ok64(dtype), "gather_events_bwd: unsupported dtype %d", (int)dtype);
     BCM_REQUIRE(n_events >= 0 && n_channels >= 0 && seqlen >= 0, "gather_events_bwd: negative size");
+    BCM_REQUIRE(n_events < (1ll << 31) && seqlen < (1ll << 31), "gather_events_bwd: sizes exceed int32");
     const size_t bytes = (size_t)n_channels * (size_t)seqlen * dtype_size(dtype);
     if (bytes == 0) return BCM_OK;
     BCM_REQUIRE(dx, "gather_events_bwd: null dx");
-    BCM_CUDA_TRY(cudaMemsetAsync(dx, 0, bytes, stream));
-    if (n_events == 0) return BCM_OK;
+    if (n_events == 0) {
+        BCM_CUDA_TRY(cudaMemsetAsync(dx, 0, bytes, stream));
+        return BCM_OK;
+    }
     BCM_REQUIRE(grad && channel_ids && time_steps, "gather_events_bwd: null pointer");
+    const size_t need = bcm_gather_bwd_workspace_bytes(n_channels);
+    if (!workspace || workspace_bytes < need) {
+        set_error("gather_events_bwd: workspace of %zu bytes < required %zu", workspace_bytes, need);
+        return BCM_ERR_WORKSPACE;
+    }
+    // workspace: [flag][pad to 256 B][row_start[NC + 1]]
+    int32_t* flag = static_cast<int32_t*>(workspace);
+    int32_t* row_start = flag + 64;
+    BCM_CUDA_TRY(cudaMemsetAsync(flag, 0, sizeof(int32_t), stream));
     const int threads = 256;
+    row_bounds_kernel<<<grid_for(n_events + 1, threads), threads, 0, stream>>>(
+        channel_ids, n_events, n_channels, row_start, flag);
+    BCM_LAUNCH_CHECK();
     return dispatch_dtype64(dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);
-        scatter_kernel<T><<<grid_for(n_events, threads), threads, 0, stream>>>(
-            static_cast<const T*>(grad), channel_ids, time_steps, n_events, n_channels,
+        constexpr int V = 16 / sizeof(T);
+        const bool vec = (seqlen % V == 0) && (reinterpret_cast<uintptr_t>(dx) % 16 == 0);
+        const int rows_grid = ceil_div(n_channels, 4);
+        if (vec)
+            dense_rows_kernel<T, true><<<rows_grid, 128, 0, stream>>>(
+                static_cast<const T*>(grad), time_steps, row_start, flag, n_channels, (int)seqlen,
+                static_cast<T*>(dx), flag);
+        else
+            dense_rows_kernel<T, false><<<rows_grid, 128, 0, stream>>>(
+                static_cast<const T*>(grad), time_steps, row_start, flag, n_channels, (int)seqlen,
+                static_cast<T*>(dx), flag);
+        BCM_LAUNCH_CHECK();
+        const int fb_grid = sm_count() * 2;
+        fallback_zero_kernel<T><<<fb_grid, threads, 0, stream>>>(flag, static_cast<T*>(dx),
+                                                                 (int64_t)n_channels * seqlen);
+        BCM_LAUNCH_CHECK();
+        fallback_scatter_kernel<T><<<fb_grid, threads, 0, stream>>>(
+            flag, static_cast<const T*>(grad), channel_ids, time_steps, n_events, n_channels,
             (int)seqlen, static_cast<T*>(dx));
         BCM_LAUNCH_CHECK();
         return BCM_OK;

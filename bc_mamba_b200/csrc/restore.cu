@@ -107,17 +107,19 @@ __device__ __forceinline__ void tile_load(float (*tile)[kDB], const T* src, int 
 // sets the channel's mask words, optionally stores the values in order, and
 // returns the number of events taken (warp-uniform).  Events are loaded 32 at
 // a time with one coalesced load per array.
+// (t0_pre, v0_pre) are this lane's first-batch event time and value, loaded
+// by the caller for all of a warp's channels at once so their latencies overlap.
 template <typename Tin, bool VALUES>
 __device__ __forceinline__ int stage_channel(const int32_t* ts, const Tin* y, int beg, int n, int p,
                                              int t0, int wend, uint32_t* mask, float* vals,
-                                             int lane, float& last_val) {
+                                             int lane, float& last_val, int t_pre, float v_pre) {
     uint32_t m[kMW];
 #pragma unroll
     for (int w = 0; w < kMW; ++w) m[w] = 0u;
     int taken = 0;
+    int t = t_pre;
+    float v = v_pre;
     while (true) {
-        const int j = p + taken + lane;
-        const int t = (j < n) ? ts[beg + j] : INT_MAX;
         const bool valid = t >= t0 && t < wend && taken + lane < kTT;
         const int cnt = __popc(__ballot_sync(kFull, valid));
         const int rel = valid ? t - t0 : -1;
@@ -125,12 +127,15 @@ __device__ __forceinline__ int stage_channel(const int32_t* ts, const Tin* y, in
         for (int w = 0; w < kMW; ++w)
             m[w] |= __reduce_or_sync(kFull, (valid && (rel >> 5) == w) ? (1u << (rel & 31)) : 0u);
         if (VALUES) {
-            const float v = valid ? to_f32<Tin>(y[beg + j]) : 0.f;
             if (valid) vals[taken + lane] = v;
             if (cnt > 0) last_val = __shfl_sync(kFull, v, cnt - 1);
         }
         taken += cnt;
         if (cnt < 32) break;
+        // a dense window: the next 32 events of this channel
+        const int j = p + taken + lane;
+        t = (j < n) ? ts[beg + j] : INT_MAX;
+        if (VALUES) v = (j < n) ? to_f32<Tin>(y[beg + j]) : 0.f;
     }
     if (lane < kMW) {
 #pragma unroll
@@ -183,16 +188,23 @@ restore_fwd_kernel(const Tin* __restrict__ y, const int32_t* __restrict__ ts,
 
     for (int t0 = t_beg; t0 < t_end; t0 += kTT) {
         const int wend = min(t0 + kTT, t_end);
-        // 1. staging
-        float carry_new[kChPerWarp];
-        int p_new[kChPerWarp];
+        // 1. staging (first 32 events of every channel loaded up front)
+        float carry_new[kChPerWarp], v_pre[kChPerWarp];
+        int p_new[kChPerWarp], t_pre[kChPerWarp];
+#pragma unroll
+        for (int ci = 0; ci < kChPerWarp; ++ci) {
+            const int j = s_p[warp * kChPerWarp + ci] + lane;
+            const bool in = j < c_n[ci];
+            t_pre[ci] = in ? ts[c_beg[ci] + j] : INT_MAX;
+            v_pre[ci] = in ? to_f32<Tin>(y[c_beg[ci] + j]) : 0.f;
+        }
 #pragma unroll
         for (int ci = 0; ci < kChPerWarp; ++ci) {
             const int c = warp * kChPerWarp + ci;
             const int p = s_p[c];
             float last = s_carry[c];
             const int taken = stage_channel<Tin, true>(ts, y, c_beg[ci], c_n[ci], p, t0, wend, s_mask[c],
-                                                       s_val[c], lane, last);
+                                                       s_val[c], lane, last, t_pre[ci], v_pre[ci]);
             carry_new[ci] = last;
             p_new[ci] = p + taken;
         }
@@ -296,13 +308,19 @@ restore_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ ts,
                 if (ci == lane) s_p[warp * kChPerWarp + ci] = p_next[ci];
         }
         __syncwarp();
+        int t_pre[kChPerWarp];
+#pragma unroll
+        for (int ci = 0; ci < kChPerWarp; ++ci) {
+            const int j = s_p[warp * kChPerWarp + ci] + lane;
+            t_pre[ci] = (j < c_n[ci]) ? ts[c_beg[ci] + j] : INT_MAX;
+        }
 #pragma unroll
         for (int ci = 0; ci < kChPerWarp; ++ci) {
             const int c = warp * kChPerWarp + ci;
             float dummy = 0.f;
             const int p = s_p[c];
             p_next[ci] = p + stage_channel<T, false>(ts, nullptr, c_beg[ci], c_n[ci], p, t0, wend,
-                                                     s_mask[c], nullptr, lane, dummy);
+                                                     s_mask[c], nullptr, lane, dummy, t_pre[ci], 0.f);
         }
         __syncthreads();
         // 2. sweep: lane = channel, positions [32w, 32w+32) of the window

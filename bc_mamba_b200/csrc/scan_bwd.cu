@@ -153,7 +153,7 @@ dw_bwd_kernel(ScanArgs a) {
                 const float w = ok ? delta * uv[i] * uv[i] : 0.f;
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    const float dec = ok ? decay_fast(delta, A2[g]) : 1.f;
+                    const float dec = ok ? decay_exact(delta, A2[g]) : 1.f;
                     eta[g] = fmaf(dec, eta[g], w);
                 }
             }
@@ -197,7 +197,7 @@ dw_bwd_kernel(ScanArgs a) {
                 float te = 0.f;
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    const float dec = ok ? decay_fast(delta, A2[g]) : 1.f;
+                    const float dec = ok ? decay_exact(delta, A2[g]) : 1.f;
                     et[g] = fmaf(dec, et[g], w);
                     eti[i][g] = et[g];
                     deci[i][g] = dec;
@@ -497,6 +497,7 @@ __global__ void reduce_parts_kernel(const float* __restrict__ part, int stride, 
     if (f < 3 * N) off = (f / N) * NP + f % N;
     else off = 3 * NP + (f - 3 * N);
     float acc = 0.f;
+#pragma unroll 8
     for (int ch = d; ch < n_ch; ch += dim) acc += part[(int64_t)ch * stride + off];
     if (f < N) dA[d * N + f] = acc;
     else if (f < 2 * N) {

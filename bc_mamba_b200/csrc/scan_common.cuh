@@ -43,6 +43,15 @@ __device__ __forceinline__ float decay_fast(float delta, float A2) {
     return exp2f(fmaxf(fminf(delta * A2, 126.0f), -126.0f));
 }
 
+// Same decay, correctly rounded to fp32 (exp2 evaluated in double).  The
+// depthwise path tabulates decays per integer gap, so each rounded value is
+// reused by every event with that gap; rounding it correctly keeps the
+// coherent error of long-memory states (a close to 1) at the fp32 limit.
+__device__ __forceinline__ float decay_exact(float delta, float A2) {
+    const float x = fmaxf(fminf(delta * A2, 126.0f), -126.0f);
+    return (float)exp2((double)x);
+}
+
 // delta of an event with gap k: dt_idle*(k-1) + dt_active (one rounding, as
 // the reference's contracted expression).
 __device__ __forceinline__ float event_delta(float dt_idle, float dt_active, int k) {

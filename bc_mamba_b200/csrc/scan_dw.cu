@@ -18,6 +18,8 @@
 //    NE*log2(LPC));
 //  * the chunk product prod(a) is formed as exp2(A*log2e*sum(delta) +
 //    clamp corrections) instead of one multiply per (event, state).
+#include <stdlib.h>
+
 #include "scan_common.cuh"
 
 namespace bcm {
@@ -51,7 +53,7 @@ __device__ void build_table(float* tab, const ScanArgs& a, int d, int lane) {
         float v = 1.f;
         if (s < a.dstate) {
             const float A2 = (float)((double)a.A[d * a.A_sd + s * a.A_sn] * 1.4426950408889634);
-            v = decay_fast(event_delta(dti, dta, kk), A2);
+            v = decay_exact(event_delta(dti, dta, kk), A2);
         }
         tab[e] = v;
     }
@@ -87,7 +89,7 @@ __device__ __forceinline__ void lookup(const float* tab, bool tab_ok, int k, flo
         table_row<G>(tab + (k - 1) * NP + q * G, dec);
     } else {
 #pragma unroll
-        for (int g = 0; g < G; ++g) dec[g] = decay_fast(delta, A2[g]);
+        for (int g = 0; g < G; ++g) dec[g] = decay_exact(delta, A2[g]);
     }
 }
 
@@ -631,13 +633,25 @@ bcm_status launch_dw_tl(const ScanArgs& a, bool bwd, cudaStream_t st) {
 template <typename T>
 bcm_status launch_dw_t(const ScanArgs& a, bool bwd, cudaStream_t st) {
     const int N = a.dstate;
-    // Fewer states per lane (more lanes per channel) when the channels alone
-    // would leave fewer than ~2 warps per SM scheduler.
-    const int64_t want_warps = (int64_t)sm_count() * 4 * 2;
-    auto warps = [&](int lpc) { return (int64_t)a.n_channels * lpc / 32; };
-    if (N <= 4) return warps(1) >= want_warps ? launch_dw_tl<T, 4, 1>(a, bwd, st) : launch_dw_tl<T, 2, 2>(a, bwd, st);
-    if (N <= 8) return warps(2) >= want_warps ? launch_dw_tl<T, 4, 2>(a, bwd, st) : launch_dw_tl<T, 2, 4>(a, bwd, st);
-    if (N <= 16) return warps(4) >= want_warps ? launch_dw_tl<T, 4, 4>(a, bwd, st) : launch_dw_tl<T, 2, 8>(a, bwd, st);
+    // States per lane: more states give each lane more independent recurrences
+    // (instruction-level parallelism), fewer give more warps.  BCM_SCAN_LPC
+    // (lanes per channel) overrides the default for tuning.
+    static const int lpc_env = [] {
+        const char* e = getenv("BCM_SCAN_LPC");
+        return e ? atoi(e) : 0;
+    }();
+    if (N <= 16) {
+        const int lpc = lpc_env ? lpc_env : 4;
+        if (N <= 8) {
+            if (lpc >= 4) return launch_dw_tl<T, 2, 4>(a, bwd, st);
+            if (lpc == 2) return launch_dw_tl<T, 4, 2>(a, bwd, st);
+            return launch_dw_tl<T, 8, 1>(a, bwd, st);
+        }
+        if (lpc >= 8) return launch_dw_tl<T, 2, 8>(a, bwd, st);
+        if (lpc == 4) return launch_dw_tl<T, 4, 4>(a, bwd, st);
+        if (lpc == 2) return launch_dw_tl<T, 8, 2>(a, bwd, st);
+        return bwd ? launch_dw_tl<T, 8, 2>(a, bwd, st) : launch_dw_tl<T, 16, 1>(a, bwd, st);
+    }
     if (N <= 32) return launch_dw_tl<T, 4, 8>(a, bwd, st);
     return launch_dw_tl<T, 8, 8>(a, bwd, st);
 }
@@ -649,7 +663,6 @@ bcm_status launch_dw_t(const ScanArgs& a, bool bwd, cudaStream_t st) {
 bool dw_fast_supported(int dstate) { return dstate <= 64; }
 
 int dw_fast_np(int dstate) {
-    if (dstate <= 4) return 4;
     if (dstate <= 8) return 8;
     if (dstate <= 16) return 16;
     if (dstate <= 32) return 32;

@@ -70,7 +70,7 @@ dw_fwd_kernel(ScanArgs a) {
             float acc = 0.f;
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-                const float dec = ok ? decay_fast(delta, A2[g]) : 1.f;
+                const float dec = ok ? decay_exact(delta, A2[g]) : 1.f;
                 eta[g] = fmaf(dec, eta[g], ok ? w : 0.f);
                 P[g] *= dec;
                 acc = fmaf(cc[g], eta[g], acc);

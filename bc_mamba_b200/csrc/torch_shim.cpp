@@ -157,9 +157,10 @@ std::vector<Tensor> gather_events_bwd(Tensor grad_x, Tensor channel_ids, Tensor 
     auto dx = torch::empty({NC, L}, g.options());
     auto ch = channel_ids.contiguous();
     auto ts = time_steps.contiguous();
+    Tensor ws = workspace((int64_t)bcm_gather_bwd_workspace_bytes(NC), g.device());
     check_status(bcm_gather_events_bwd(g.data_ptr(), to_bcm(g.scalar_type(), "gather_events_bwd"),
                                        ch.data_ptr<int32_t>(), ts.data_ptr<int32_t>(), g.size(0),
-                                       NC, L, dx.data_ptr(), cur_stream()),
+                                       NC, L, dx.data_ptr(), ws.data_ptr(), ws.numel(), cur_stream()),
                  "gather_events_bwd");
     return {dx};
 }

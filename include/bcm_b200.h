@@ -110,6 +110,10 @@ BCM_API bcm_status bcm_expand_base_events(const int32_t* base_ch_ids,
  * Replaces extract_events_cuda.gather_events_fwd / gather_events_bwd
  *   (reference csrc/extract/extract_events_cuda.cu:670-708, 717-754).
  * bcm_gather_events_bwd writes all of dx[NC, L]: zeros, then grad at events.
+ * It takes a workspace of bcm_gather_bwd_workspace_bytes(NC) bytes; streams
+ * in extraction order (channel_ids non-decreasing, time_steps increasing
+ * within a channel) are written row by row in one pass, any other order
+ * falls back to zero-fill + scatter on the device.
  * ------------------------------------------------------------------------- */
 BCM_API bcm_status bcm_gather_events_fwd(const void* x, bcm_dtype dtype,
                                  int64_t n_channels, int64_t seqlen,
@@ -117,11 +121,14 @@ BCM_API bcm_status bcm_gather_events_fwd(const void* x, bcm_dtype dtype,
                                  const int32_t* time_steps, int64_t n_events,
                                  void* out, cudaStream_t stream);
 
+BCM_API size_t bcm_gather_bwd_workspace_bytes(int64_t n_channels);
+
 BCM_API bcm_status bcm_gather_events_bwd(const void* grad, bcm_dtype dtype,
                                  const int32_t* channel_ids,
                                  const int32_t* time_steps, int64_t n_events,
                                  int64_t n_channels, int64_t seqlen,
-                                 void* dx, cudaStream_t stream);
+                                 void* dx, void* workspace, size_t workspace_bytes,
+                                 cudaStream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Flat per-channel sparse selective scan with inter-spike decay.

@@ -43,6 +43,26 @@ def test_extract_expand_configs(cfg):
     assert_exact(dx, ev.gather_events_bwd(g.cpu().numpy(), ref[0], ref[1], c.B * c.D, c.L), "scatter")
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float64])
+def test_gather_bwd_any_order(dtype):
+    """Rows in extraction order take the one-pass row writer; a shuffled
+    stream (same unique (ch, t) pairs) falls back to zero-fill + scatter on
+    the device and gives the same dx."""
+    c = CONFIGS["c0"].with_(L=250)   # L not a multiple of the vector width
+    inp = make_inputs(c)
+    r = ev.extract_base_events(inp["v"].numpy(), inp["threshold"])
+    ch, t, k, cu, mx = ev.expand_base_events(*r[:4], c.B, c.d_model, c.expand)
+    NC = c.B * c.D
+    g = torch.randn(ch.size, generator=torch.Generator().manual_seed(1)).to(dtype)
+    ref = ev.gather_events_bwd(g.double().numpy(), ch, t, NC, c.L)
+    ops = load_ops()
+    for perm in [np.arange(ch.size), np.random.default_rng(2).permutation(ch.size)]:
+        dx = ops.gather_events_bwd(g[perm].to(dev), torch.as_tensor(ch[perm]).to(dev),
+                                   torch.as_tensor(t[perm]).to(dev), NC, c.L)[0]
+        assert dx.dtype == dtype
+        assert_exact(dx.double(), ref, "dx")
+
+
 def test_known_answer():
     # x = [0.1, 0.9, 0.6, 0.2, 0.7], thr 0.5 -> t = [1, 2, 4], k = [2, 1, 2]
     x = torch.tensor([[[0.1, 0.9, 0.6, 0.2, 0.7]]])
