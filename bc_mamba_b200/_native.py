@@ -27,6 +27,7 @@ ABI_SYMBOLS = (
     "bcm_gather_events_fwd",
     "bcm_gather_bwd_workspace_bytes",
     "bcm_gather_events_bwd",
+    "bcm_gather_events_bwd_noalloc",
     "bcm_flat_ch_fwd_workspace_bytes",
     "bcm_flat_ch_bwd_workspace_bytes",
     "bcm_flat_ch_fwd",

@@ -13,6 +13,8 @@
 //           is then written out with coalesced stores.
 // The row is read once (the reference reads it twice) and the fill pass reads
 // L/8 bytes of mask instead of the L*sizeof(T) input row.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace bcm {
@@ -519,4 +521,66 @@ extern "C" bcm_status bcm_gather_events_bwd(const void* grad, bcm_dtype dtype,
         BCM_LAUNCH_CHECK();
         return BCM_OK;
     });
+}
+
+// ---- gather backward without allocation -------------------------------------
+// Callers that may not allocate device memory (an FFI host whose device memory
+// is carved from its own arena up front; code where cudaMalloc/cudaFree would
+// stall or synchronise the GPU) get the same backward with its scratch in a
+// fixed array: the order flag, 63 ints of padding and row_start[NC + 1], i.e.
+// the layout bcm_gather_events_bwd expects of its workspace.  Every GPU that
+// loads this library holds the array (about 1 MiB) until the process exits.
+namespace bcm {
+namespace {
+constexpr int64_t kNoallocScratchInts =
+    ((64 + BCM_GATHER_BWD_NOALLOC_MAX_CHANNELS + 1) + 63) / 64 * 64;
+static __device__ __align__(256) int32_t g_gather_bwd_scratch[kNoallocScratchInts];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device.  Host code may
+// not use g_gather_bwd_scratch as a pointer (it names a host-side stand-in),
+// so the address is looked up once per device and cached.
+bcm_status noalloc_scratch(void** out) {
+    int dev = -1;
+    BCM_CUDA_TRY(cudaGetDevice(&dev));
+    BCM_REQUIRE(dev >= 0 && dev < kMaxDevices, "gather_events_bwd_noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_gather_bwd_scratch);
+        if (err != cudaSuccess || !p) {
+            set_error("gather_events_bwd_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                      cudaGetErrorString(err));
+            return BCM_ERR_CUDA;
+        }
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return BCM_OK;
+}
+}  // namespace
+}  // namespace bcm
+
+extern "C" bcm_status bcm_gather_events_bwd_noalloc(const void* grad, bcm_dtype dtype,
+                                                    const int32_t* channel_ids,
+                                                    const int32_t* time_steps, int64_t n_events,
+                                                    int64_t n_channels, int64_t seqlen, void* dx,
+                                                    cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(n_channels <= BCM_GATHER_BWD_NOALLOC_MAX_CHANNELS,
+                "gather_events_bwd_noalloc: n_channels %lld exceeds the fixed scratch limit of %d "
+                "channels; use bcm_gather_events_bwd with a workspace",
+                (long long)n_channels, BCM_GATHER_BWD_NOALLOC_MAX_CHANNELS);
+    void* scratch = nullptr;
+    const bcm_status st = noalloc_scratch(&scratch);
+    if (st != BCM_OK) return st;
+    // bcm_gather_events_bwd clears the flag word itself and rewrites every
+    // row_start entry it reads, so nothing left from the previous call leaks.
+    static_assert(sizeof(g_gather_bwd_scratch) >= 4 * (64 + BCM_GATHER_BWD_NOALLOC_MAX_CHANNELS + 1),
+                  "scratch smaller than the workspace of the largest allowed call");
+    return bcm_gather_events_bwd(grad, dtype, channel_ids, time_steps, n_events, n_channels, seqlen, dx,
+                                 scratch, sizeof(g_gather_bwd_scratch), stream);
 }

@@ -131,6 +131,34 @@ BCM_API bcm_status bcm_gather_events_bwd(const void* grad, bcm_dtype dtype,
                                  cudaStream_t stream);
 
 /* ------------------------------------------------------------------------- *
+ * Gather backward that allocates nothing.  No counterpart in the reference:
+ * the reference's gather_events_bwd always gets its memory from PyTorch.
+ *
+ * For callers that may not allocate device memory on the hot path: hosts
+ * binding this library over FFI whose device memory is all carved out of
+ * their own arena up front, and code that runs where cudaMalloc/cudaFree
+ * would block or synchronise the device (cudaFree waits for all work on
+ * the GPU).  They pass grad, the event stream and dx, and nothing else.
+ *
+ * Results are identical to bcm_gather_events_bwd.  Its scratch (the order
+ * flag and the row table) lives in a fixed array that every GPU which loads
+ * this library holds until the process exits, about 1 MiB, so n_channels is
+ * limited to BCM_GATHER_BWD_NOALLOC_MAX_CHANNELS; larger calls fail with
+ * BCM_ERR_INVALID_ARGUMENT.  The array is shared by every call on a device:
+ * calls that can overlap on the GPU (on different streams without ordering
+ * between them) race on it and must not be issued.  The first call on each
+ * device looks up the array's device address (the device must be current)
+ * and should come before any stream capture.
+ * ------------------------------------------------------------------------- */
+#define BCM_GATHER_BWD_NOALLOC_MAX_CHANNELS 262144
+
+BCM_API bcm_status bcm_gather_events_bwd_noalloc(const void* grad, bcm_dtype dtype,
+                                 const int32_t* channel_ids,
+                                 const int32_t* time_steps, int64_t n_events,
+                                 int64_t n_channels, int64_t seqlen,
+                                 void* dx, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------- *
  * Flat per-channel sparse selective scan with inter-spike decay.
  * Replaces selective_scan_cuda.fwd_flat_ch / bwd_flat_ch
  *   (reference csrc/selective_scan/selective_scan.cpp:674-884, 890-1153).
