@@ -33,15 +33,41 @@ def install_shim() -> None:
         sys.path.insert(0, p)
 
 
+_stage_log = None   # list of (name, start, end) CUDA events while stage_timing() is open
+
+
+@contextlib.contextmanager
+def stage_timing():
+    """Record a CUDA event pair on the launching stream around every
+    cuda_stage entered while the context is open (autograd's backward thread
+    included).  Yields the list of (name, start_event, end_event); read the
+    times after a synchronize."""
+    global _stage_log
+    prev, _stage_log = _stage_log, []
+    try:
+        yield _stage_log
+    finally:
+        _stage_log = prev
+
+
 @contextlib.contextmanager
 def cuda_stage(name: str):
     """NVTX range named like the reference's profiling stages
-    (spike_mamba/runtime_breakdown.py:12-15)."""
+    (spike_mamba/runtime_breakdown.py:12-15), timed with CUDA events while
+    stage_timing() is open."""
     if torch.cuda.is_available():
+        log = _stage_log
         torch.cuda.nvtx.range_push(name)
+        if log is not None:
+            start = torch.cuda.Event(enable_timing=True)
+            start.record()
         try:
             yield
         finally:
+            if log is not None:
+                end = torch.cuda.Event(enable_timing=True)
+                end.record()
+                log.append((name, start, end))
             torch.cuda.nvtx.range_pop()
     else:
         yield

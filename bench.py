@@ -110,6 +110,28 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# the API stages of one step (interface.cuda_stage names) -> op keys
+STAGE_OPS = {
+    "routing_index_extraction": "extract", "active_token_packing": "expand",
+    "active_gather_forward": "gather_fwd", "sparse_scan_forward": "scan_fwd",
+    "dense_restoration_forward": "restore_fwd", "restore_backward": "restore_bwd",
+    "sparse_scan_backward": "scan_bwd", "gather_scatter_backward": "gather_bwd",
+}
+# kernels each stage launches (all ours): extract 3, expand 2, gather 1,
+# scan fwd 1, restore fwd 1, restore bwd 1, scan bwd 2, gather bwd 4
+KERNELS_PER_STEP = 15
+
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per stage on the
+# c1 workload, summed over the stage's kernels, from one ncu capture of
+# `python bench.py --steps 3 --warmup 3 --no-cpu-baseline` (summary in
+# profiles/dram_traffic_c1.txt).  Writes that stay in the 126 MB L2 when a
+# kernel ends are not counted.  Re-measured whenever a kernel changes.
+NCU_TRAFFIC_C1 = {
+    "extract": 34.72e6, "expand": 20.18e6, "gather_fwd": 95.43e6, "scan_fwd": 27.07e6,
+    "restore_fwd": 36.11e6, "restore_bwd": 81.32e6, "scan_bwd": 46.05e6, "gather_bwd": 49.20e6,
+}
+
+
 def algorithmic_bytes(cfg, E, NC, n_chunks):
     """Bytes each API call must move once (inputs read once, outputs written
     once), per op, for one fwd+bwd step."""
@@ -181,7 +203,6 @@ def run_ours(args):
         zero()
         step(hs, u_leaf, inp["dout"])
     torch.cuda.synchronize()
-    u_dev = inp["u"].detach()
 
     # ---- value: device-resident inputs, K timed steps, L2 flushed before each
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -201,6 +222,19 @@ def run_ours(args):
     if world > 1:
         torch.distributed.barrier()
     clk = clocks.stop()
+    # per-op device time: the same K steps again with every API stage
+    # bracketed by CUDA events on its launching stream (mean per step).  A
+    # separate pass, because creating and recording the events costs host time
+    # the timed steps above should not carry.
+    with itf.stage_timing() as stage_log:
+        for i in range(args.steps):
+            zero()
+            flush.zero_()
+            step(hs, u_leaf, inp["dout"])
+    torch.cuda.synchronize()
+    per_op = {k: 0.0 for k in STAGE_OPS.values()}
+    for name, s_ev, e_ev in stage_log:
+        per_op[STAGE_OPS[name]] += s_ev.elapsed_time(e_ev) / args.steps
     t_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
     t_max = torch.tensor([t_ms], device=dev)
     if world > 1:
@@ -239,8 +273,6 @@ def run_ours(args):
         torch.distributed.barrier()
     e2e_ms = float(te.item()) / args.steps
 
-    # ---- per-op device time (flush before each op hides the host launch gap)
-    per_op = time_ops(ops, itf, cfg, hs, u_dev, inp, params, thr, flush, reps=max(3, min(args.steps, 10)))
     n_chunks = max(1, (mx + 2047) // 2048)
     alg = algorithmic_bytes(cfg, E, NC, n_chunks)
     peak, peak_kind = measured_peak_gbs()
@@ -262,7 +294,8 @@ def run_ours(args):
         "e2e": {"value": world * E / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
-                     "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                     "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": NCU_TRAFFIC_C1.get(dominant) if args.config == "c1" and args.rho is None else None,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650 GB/s",
                      "algorithmic_bytes": alg[dominant], "ms": dom_ms},
         "pipeline_roofline": {"algorithmic_bytes": total_alg, "kernel_ms_sum": kernel_ms,
@@ -273,7 +306,7 @@ def run_ours(args):
         "per_op_ms": per_op,
         "per_op_frac_hbm": {k: alg[k] / (per_op[k] * 1e-3) / 1e9 / peak for k in per_op},
         "clocks": clk,
-        "gpu_launches": 12 * args.steps,
+        "gpu_launches": KERNELS_PER_STEP * args.steps,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
@@ -284,46 +317,6 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
-
-
-def time_ops(ops, itf, cfg, hs, u_dev, inp, params, thr, flush, reps=5):
-    """Device time of each API call of the step (ms, mean over reps)."""
-    p = params
-    res = {k: 0.0 for k in ["extract", "expand", "gather_fwd", "scan_fwd", "restore_fwd", "restore_bwd",
-                            "scan_bwd", "gather_bwd"]}
-    base = hs
-
-    counting = [False]
-
-    def timed(key, fn):
-        flush.zero_()
-        s = torch.cuda.Event(enable_timing=True)
-        e = torch.cuda.Event(enable_timing=True)
-        s.record()
-        r = fn()
-        e.record()
-        torch.cuda.synchronize()
-        if counting[0]:
-            res[key] += s.elapsed_time(e) / reps
-        return r
-
-    with torch.no_grad():
-        for rep in range(reps + 1):   # the first pass warms the allocator and is not counted
-            counting[0] = rep > 0
-            bch, bt, bk, bcu, _c, _m = timed("extract", lambda: ops.extract_base_events(base, thr))
-            ch, ts, kf, cu, mx = timed("expand", lambda: ops.expand_base_events(bch, bt, bk, bcu, cfg.B,
-                                                                                 cfg.d_model, cfg.expand))
-            mxi = int(mx.item())
-            uf = timed("gather_fwd", lambda: ops.gather_events_fwd(u_dev, ch, ts)[0])
-            args = (uf, kf, cu, mxi, p["dt_idle"].detach(), p["dt_active"].detach(), p["A"].detach(),
-                    p["W_B"].detach(), p["W_C"].detach())
-            out, x = timed("scan_fwd", lambda: ops.fwd_flat_ch(*args, p["D"].detach(), None, None, 0, True))
-            timed("restore_fwd", lambda: ops.restore_dense_fwd(out, ts, cu, cfg.D, cfg.L))
-            dy = timed("restore_bwd", lambda: ops.restore_dense_bwd(inp["dout"], ts, cu, cfg.D, cfg.L))
-            dy = dy.to(out.dtype)
-            g = timed("scan_bwd", lambda: ops.bwd_flat_ch(*args, dy, x, p["D"].detach(), None, None, None, 0, True))
-            timed("gather_bwd", lambda: ops.gather_events_bwd(g[0], ch, ts, cfg.B * cfg.D, cfg.L))
-    return res
 
 
 # ------------------------------------------------------------- CPU arm ----
