@@ -74,6 +74,24 @@ __device__ __forceinline__ int group_max_warp(int v) {
     return v;
 }
 
+// Sum v[0..NE) over the LPC lanes of a group.  Afterwards lane q holds the
+// totals of events q*(NE/LPC) + j in v[j], j < NE/LPC.
+template <int LPC, int NE>
+__device__ __forceinline__ void group_transpose_sum(float (&v)[NE], int q) {
+#pragma unroll
+    for (int lvl = 0; (LPC >> lvl) > 1; ++lvl) {
+        const int o = (LPC >> lvl) / 2;
+        const int half = (NE >> lvl) / 2;
+        const bool up = (q & o) != 0;
+#pragma unroll
+        for (int j = 0; j < half; ++j) {
+            const float send = up ? v[j] : v[j + half];
+            const float recv = __shfl_xor_sync(kFull, send, o);
+            v[j] = (up ? v[j + half] : v[j]) + recv;
+        }
+    }
+}
+
 __device__ __forceinline__ float silu(float z) { return z / (1.0f + expf(-z)); }
 
 // Reference event-chunk size for the tiled B/C layout: the forward kernel's
@@ -109,5 +127,10 @@ inline void pick_layout(int N, int& G, int& LPC) {
 bool dw_fast_supported(int dstate);
 int dw_fast_np(int dstate);
 bcm_status dw_fast_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t st);
+
+// Staged lane-group kernels (scan_v3.cu) for dstate <= 16 when the channels
+// of one feature fill whole warps; dw_fast_launch prefers them.
+bool v3_supported(const ScanArgs& a, bool bwd);
+bcm_status v3_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t st);
 
 }  // namespace bcm

@@ -93,38 +93,13 @@ __device__ __forceinline__ void lookup(const float* tab, bool tab_ok, int k, flo
     }
 }
 
-// Sum v[0..NE) over the LPC lanes of a group.  Afterwards lane q holds the
-// totals of events q*(NE/LPC) + j in v[j], j < NE/LPC.
-template <int LPC, int NE>
-__device__ __forceinline__ void group_transpose_sum(float (&v)[NE], int q) {
-#pragma unroll
-    for (int lvl = 0; (LPC >> lvl) > 1; ++lvl) {
-        const int o = (LPC >> lvl) / 2;
-        const int half = (NE >> lvl) / 2;
-        const bool up = (q & o) != 0;
-#pragma unroll
-        for (int j = 0; j < half; ++j) {
-            const float send = up ? v[j] : v[j + half];
-            const float recv = __shfl_xor_sync(kFull, send, o);
-            v[j] = (up ? v[j + half] : v[j]) + recv;
-        }
-    }
-}
-
-// Compensated (Kahan) accumulation of per-tile partial sums: parameter
-// gradients of long channels sum thousands of tile partials in fp32.
-__device__ __forceinline__ void kahan_add(float& sum, float& comp, float v) {
-    const float y = v - comp;
-    const float t = sum + y;
-    comp = (t - sum) - y;
-    sum = t;
-}
-
 // Per-lane constants of the depthwise scan.
 template <int G>
 struct DwParams {
     float A2[G], Ar[G], WB[G], WC[G], cc[G];
-    float dti, dta, Dv, dlim;
+    float dti, dta, Dv;
+    float dclamp;   // delta above this may hit the +-126 exponent clamp
+    float dlim;     // the fast forward path takes events with delta <= dlim
 };
 
 template <int G>
@@ -144,8 +119,16 @@ __device__ __forceinline__ void load_params(DwParams<G>& P, const ScanArgs& a, b
     P.dti = ok ? a.dt_idle[d] : 0.f;
     P.dta = ok ? a.dt_active[d] : 0.f;
     P.Dv = (ok && a.D) ? a.D[d] : 0.f;
-    // events with delta above dlim may hit the +-126 exponent clamp
-    P.dlim = amax > 0.f ? 126.0f / amax : INFINITY;
+    P.dclamp = amax > 0.f ? 126.0f / amax : INFINITY;
+    // With dt_idle, dt_active >= 0 and every A <= 0 each exponent delta*A is
+    // <= 0, so a clamp at -126 leaves the chunk product prod(a) at or below
+    // 2^-126 whether or not the clamp is applied: the fast forward path skips
+    // those corrections.  Otherwise it must leave every clamping event to the
+    // general path, which applies them exactly.
+    bool decaying = P.dti >= 0.f && P.dta >= 0.f;
+#pragma unroll
+    for (int g = 0; g < G; ++g) decaying = decaying && P.A2[g] <= 0.f;
+    P.dlim = decaying ? INFINITY : P.dclamp;
 }
 
 template <typename T>
@@ -245,7 +228,7 @@ dw_fwd_v2(ScanArgs a, int bn, int dmajor) {
                 acc[i] = s;
                 if (ok) {
                     sdel += delta;
-                    if (delta > P.dlim) {
+                    if (delta > P.dclamp) {
 #pragma unroll
                         for (int g = 0; g < G; ++g) {
                             const float x = delta * P.A2[g];
@@ -379,20 +362,25 @@ dw_bwd_v2(ScanArgs a, int bn, int dmajor) {
     T* du = static_cast<T*>(a.du) + beg;
     float* ck = a.ws_ckpt + ((int64_t)(beg >> 3) + ch) * NP + q * G;
 
+    // Parameter-gradient sums: per-tile partials are added into per-chunk
+    // sums (at most 256 tiles), which are added into the totals at the end
+    // of each chunk, so no fp32 sum runs over more than 256 terms.
     float gam[G], anx[G], SA[G], SB[G], QE[G], cA[G], cB[G], cQ[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         gam[g] = 0.f; anx[g] = 1.f;
         SA[g] = SB[g] = QE[g] = 0.f;
-        cA[g] = cB[g] = cQ[g] = 0.f;
     }
-    float s_ddi = 0.f, s_dda = 0.f, s_dD = 0.f, c_ddi = 0.f, c_dda = 0.f, c_dD = 0.f;
+    float s_ddi = 0.f, s_dda = 0.f, s_dD = 0.f;
 
     for (int c = nch_warp - 1; c >= 0; --c) {
         const bool c_ok = c < nch;
         const int cs = c * kChunkX;
         const int len = c_ok ? min(n - cs, kChunkX) : 0;
         const int len_warp = group_max_warp<LPC>(len);
+#pragma unroll
+        for (int g = 0; g < G; ++g) cA[g] = cB[g] = cQ[g] = 0.f;
+        float c_ddi = 0.f, c_dda = 0.f, c_dD = 0.f;
         // ---- pass 1: state every kB events of the chunk -> workspace --------
         float eta[G];
 #pragma unroll
@@ -457,12 +445,12 @@ dw_bwd_v2(ScanArgs a, int bn, int dmajor) {
         for (int m = nt_warp - 1; m >= 0; --m) {
             const int jb = cs + m * kB;
             const int cnt = (m < nt) ? min(kB, cs + len - jb) : 0;
-            float uv[kB], dv[kB], et[G];
+            float uv[kB], dv[kB], et[G], e0[G];
             int kv[kB];
 #pragma unroll
             for (int i = 0; i < kB; ++i) { uv[i] = uN[i]; kv[i] = kN[i]; dv[i] = dN[i]; }
 #pragma unroll
-            for (int g = 0; g < G; ++g) et[g] = eN[g];
+            for (int g = 0; g < G; ++g) et[g] = e0[g] = eN[g];
             if (m > 0) {  // prefetch the previous tile
                 const int jp = jb - kB;
                 const int cp = (m - 1 < nt) ? min(kB, cs + len - jp) : 0;
@@ -509,7 +497,8 @@ dw_bwd_v2(ScanArgs a, int bn, int dmajor) {
 #pragma unroll
                     for (int g = 0; g < G; ++g) {
                         gam[g] = fmaf(anx[g], gam[g], qv);
-                        const float pr = gam[g] * (eti[i][g] - w);
+                        // gam * (eta_i - w_i) as gam * a_i * eta_{i-1} (no cancellation)
+                        const float pr = gam[g] * (dec[g] * (i > 0 ? eti[i > 0 ? i - 1 : 0][g] : e0[g]));
                         tSA[g] = fmaf(pr, delta, tSA[g]);
                         ta = fmaf(ccA[g], pr, ta);
                         tSB[g] = fmaf(gam[g], w, tSB[g]);
@@ -551,7 +540,7 @@ dw_bwd_v2(ScanArgs a, int bn, int dmajor) {
 #pragma unroll
                         for (int g = 0; g < G; ++g) {
                             gam[g] = fmaf(anx[g], gam[g], qv);
-                            const float pr = gam[g] * (eti[i][g] - w);
+                            const float pr = gam[g] * (dec[g] * (i > 0 ? eti[i > 0 ? i - 1 : 0][g] : e0[g]));
                             tSA[g] = fmaf(pr, delta, tSA[g]);
                             ta = fmaf(ccA[g], pr, ta);
                             tSB[g] = fmaf(gam[g], w, tSB[g]);
@@ -565,9 +554,9 @@ dw_bwd_v2(ScanArgs a, int bn, int dmajor) {
             }
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-                kahan_add(SA[g], cA[g], tSA[g]);
-                kahan_add(SB[g], cB[g], tSB[g]);
-                kahan_add(QE[g], cQ[g], tQE[g]);
+                cA[g] += tSA[g];
+                cB[g] += tSB[g];
+                cQ[g] += tQE[g];
             }
             group_transpose_sum<LPC, kB>(teta, q);
             group_transpose_sum<LPC, kB>(tgam, q);
@@ -586,10 +575,19 @@ dw_bwd_v2(ScanArgs a, int bn, int dmajor) {
                     t_dD = fmaf(dv[i], uv[i], t_dD);
                 }
             }
-            kahan_add(s_ddi, c_ddi, t_ddi);
-            kahan_add(s_dda, c_dda, t_dda);
-            kahan_add(s_dD, c_dD, t_dD);
+            c_ddi += t_ddi;
+            c_dda += t_dda;
+            c_dD += t_dD;
         }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            SA[g] += cA[g];
+            SB[g] += cB[g];
+            QE[g] += cQ[g];
+        }
+        s_ddi += c_ddi;
+        s_dda += c_dda;
+        s_dD += c_dD;
     }
     // per-channel partials; the scalar sums are spread over the group's lanes
     const float r_ddi = group_sum<LPC>(s_ddi);
@@ -670,6 +668,7 @@ int dw_fast_np(int dstate) {
 }
 
 bcm_status dw_fast_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t st) {
+    if (v3_supported(a, bwd)) return v3_launch(a, dtype, bwd, st);
     return dispatch_dtype(dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);
         return launch_dw_t<T>(a, bwd, st);

@@ -1,0 +1,1044 @@
+// scan_v3.cu — staged depthwise scan kernels for dstate <= 16 (forward and
+// backward), used when the channels of one feature d fill whole warps.
+// Semantics are those of scan_fwd.cu / scan_bwd.cu (reference
+// selective_scan_fwd_kernel.cuh:403-728, selective_scan_bwd_kernel.cuh:
+// 635-1169, depthwise B/C); the layout is:
+//
+//  * a warp owns CPW = 32/LPC channels of the same feature d (batch rows
+//    b..b+CPW-1) and each channel's states are split over LPC lanes (G states
+//    per lane), so every lane of the warp shares one per-warp decay table
+//    (rows k = 1..kKT3 for the integer gap k, row 0 = identity);
+//  * events are staged 32 per channel at a time: one coalesced load per
+//    channel and array brings them into registers while the previous batch is
+//    processed, then a transposed shared-memory copy hands each lane its own
+//    channel's events (conflict-free);
+//  * slots past a channel's last event read the identity row with u = 0, so
+//    the inner loop needs no per-event predicate; per-event outputs go back
+//    through shared memory and leave as coalesced stores;
+//  * the backward keeps the eight recomputed states of a tile in registers
+//    and sums per-event quantities over the LPC lanes with shuffles.
+#include <stdlib.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "scan_common.cuh"
+
+namespace bcm {
+
+namespace {
+
+constexpr int kR3 = 32;          // events per channel per staged batch
+constexpr int kKT3 = 128;        // tabulated gaps 1..kKT3
+constexpr int kRows3 = kKT3 + 1; // row 0 = identity (padding slots)
+static_assert(kChunkX % kR3 == 0, "chunk boundaries must fall on batch boundaries");
+static_assert(kR3 % kCkpt == 0, "tiles must not straddle batches");
+
+template <int G, int LPC>
+struct V3 {
+    static constexpr int NP = G * LPC;     // padded states per channel
+    static constexpr int CPW = 32 / LPC;   // channels per warp
+    static constexpr int P = CPW + 1;      // staging pitch (conflict-free transposes)
+    static constexpr int TAB = NP * kRows3;
+};
+
+// Table layout: float4 groups of states, [s/4][row] -> a lane's G decays of
+// one row are G/4 vector loads; rows of different lanes spread over banks.
+template <int NP>
+__device__ void build_table3(float* tab, const ScanArgs& a, int d, int lane) {
+    const float dti = a.dt_idle[d], dta = a.dt_active[d];
+    for (int e = lane; e < kRows3 * NP; e += 32) {
+        const int row = e / NP, s = e % NP;
+        float v = 1.f;
+        if (row > 0 && s < a.dstate) {
+            const float A2 = (float)((double)a.A[d * a.A_sd + s * a.A_sn] * 1.4426950408889634);
+            v = decay_exact(event_delta(dti, dta, row), A2);
+        }
+        tab[((s >> 2) * kRows3 + row) * 4 + (s & 3)] = v;
+    }
+    __syncwarp();
+}
+
+template <int G>
+__device__ __forceinline__ void tab_row3(const float* tab, int row, int q, float (&dec)[G]) {
+    const float4* t4 = reinterpret_cast<const float4*>(tab);
+#pragma unroll
+    for (int j = 0; j < G / 4; ++j) {
+        const float4 v = t4[(q * (G / 4) + j) * kRows3 + row];
+        dec[4 * j] = v.x;
+        dec[4 * j + 1] = v.y;
+        dec[4 * j + 2] = v.z;
+        dec[4 * j + 3] = v.w;
+    }
+}
+
+// One channel's batch of events -> registers: slot c of lane l holds event
+// j0 + l of warp channel c (coalesced: the 32 lanes read 32 consecutive events).
+template <typename T, int CPW>
+__device__ __forceinline__ void fetch_f(const T* src, const int* s_base, const int* s_len, int j0,
+                                        int lane, float (&r)[CPW]) {
+    const int j = j0 + lane;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) r[c] = (j < s_len[c]) ? to_f32<T>(src[s_base[c] + j]) : 0.f;
+}
+
+template <int CPW>
+__device__ __forceinline__ void fetch_k(const int32_t* src, const int* s_base, const int* s_len, int j0,
+                                        int lane, int (&r)[CPW]) {
+    const int j = j0 + lane;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) r[c] = (j < s_len[c]) ? src[s_base[c] + j] : 0;
+}
+
+template <int CPW, int P, typename V>
+__device__ __forceinline__ void stage(V* s, const V (&r)[CPW], int lane) {
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) s[lane * P + c] = r[c];
+}
+
+__device__ __forceinline__ int warp_max(int v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = max(v, __shfl_xor_sync(kFull, v, off));
+    return v;
+}
+
+__device__ __forceinline__ float warp_all_min(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = fminf(v, __shfl_xor_sync(kFull, v, off));
+    return v;
+}
+
+// True when some real event of the batch in registers (slot c = channel c,
+// event j0 + lane; padding slots hold k = 0) needs the exact path: a gap
+// outside the table, or (forward, non-decaying parameters) a delta that may
+// clamp.  Warp-uniform.
+template <int CPW>
+__device__ __forceinline__ bool batch_needs_exact(const int (&pk)[CPW], const int* s_len, int j0, int lane,
+                                                  float dti, float dta, float dlim) {
+    bool miss = false;
+    const int j = j0 + lane;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+        const int kk = pk[c];
+        const bool bad = (unsigned)(kk - 1) >= (unsigned)kKT3 || event_delta(dti, dta, kk) > dlim;
+        miss = miss || (j < s_len[c] && bad);
+    }
+    return __any_sync(kFull, miss);
+}
+
+// Sum v[0..CPW) over the 32 lanes so that afterwards every lane holds the
+// total of its own channel (lane / LPC) in v[0].
+template <int CPW>
+__device__ __forceinline__ float warp_channel_sum(float (&v)[CPW], int lane) {
+#pragma unroll
+    for (int lvl = 0; (CPW >> lvl) > 1; ++lvl) {
+        const int o = 16 >> lvl;
+        const int half = (CPW >> lvl) / 2;
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int j = 0; j < half; ++j) {
+            const float send = up ? v[j] : v[j + half];
+            const float recv = __shfl_xor_sync(kFull, send, o);
+            v[j] = (up ? v[j + half] : v[j]) + recv;
+        }
+    }
+    float t = v[0];
+#pragma unroll
+    for (int o = 32 / CPW / 2; o > 0; o >>= 1) t += __shfl_xor_sync(kFull, t, o);
+    return t;
+}
+
+// ============================================================ forward ====
+// Staging turns each event into (u, w = delta*u^2, table row) once; the fast
+// loop then only reads them, with the next event's decays loaded one event
+// ahead.  The exact path (gaps outside the table, clamping deltas of
+// non-decaying parameters) recomputes from (u, k).
+template <typename T, int G, int LPC>
+__global__ void __launch_bounds__(32)
+dw_fwd_v3(ScanArgs a, int bgroups) {
+    using V = V3<G, LPC>;
+    constexpr int CPW = V::CPW, P = V::P, NP = V::NP;
+    extern __shared__ __align__(16) float sm3[];
+    float* tab = sm3;
+    float* s_u = tab + V::TAB;
+    int* s_k = reinterpret_cast<int*>(s_u + kR3 * P);
+    float* s_w = reinterpret_cast<float*>(s_k + kR3 * P);
+    int* s_r = reinterpret_cast<int*>(s_w + kR3 * P);
+    float* s_y = reinterpret_cast<float*>(s_r + kR3 * P);
+    int* s_beg = reinterpret_cast<int*>(s_y + kR3 * P);
+    int* s_n = s_beg + CPW;
+
+    const int lane = threadIdx.x, grp = lane / LPC, q = lane % LPC;
+    const int d = blockIdx.x / bgroups;
+    const int b0 = (blockIdx.x % bgroups) * CPW;
+    const int N = a.dstate;
+    if (lane < CPW) {
+        const int c = (b0 + lane) * a.dim + d;
+        s_beg[lane] = a.cu[c];
+        s_n[lane] = a.cu[c + 1] - a.cu[c];
+    }
+    build_table3<NP>(tab, a, d, lane);   // ends with __syncwarp
+    const int ch = (b0 + grp) * a.dim + d;
+    const int n = s_n[grp];
+    const int n_max = warp_max(n);
+
+    float A2[G], cc[G], eta[G], corr[G];
+    float amax = 0.f;
+    bool decaying = true;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int s = q * G + g;
+        const bool o = s < N;
+        const float Ar = o ? a.A[d * a.A_sd + s * a.A_sn] : 0.f;
+        A2[g] = (float)((double)Ar * 1.4426950408889634);
+        cc[g] = o ? a.B[d * N + s] * a.C[d * N + s] : 0.f;
+        eta[g] = corr[g] = 0.f;
+        amax = fmaxf(amax, fabsf(A2[g]));
+        decaying = decaying && A2[g] <= 0.f;
+    }
+    const float dti = a.dt_idle[d], dta = a.dt_active[d];
+    const float Dv = a.D ? a.D[d] : 0.f;
+    decaying = decaying && dti >= 0.f && dta >= 0.f;
+    // exponents beyond +-126 clamp; with decaying parameters every exponent is
+    // <= 0 and a clamped one leaves prod(a) at or below 2^-126 either way, so
+    // only non-decaying warps send those events to the exact path
+    const float dclamp = amax > 0.f ? 126.0f / amax : INFINITY;
+    const float dlim = warp_all_min(decaying ? INFINITY : dclamp);
+    // sum of the deltas of each warp channel's events staged by this lane
+    float sd[CPW];
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) sd[c] = 0.f;
+
+    const T* u = static_cast<const T*>(a.u);
+    float pu[CPW];
+    int pk[CPW];
+    fetch_f<T, CPW>(u, s_beg, s_n, 0, lane, pu);
+    fetch_k<CPW>(a.k, s_beg, s_n, 0, lane, pk);
+    for (int j0 = 0; j0 < n_max; j0 += kR3) {
+        const bool exact = batch_needs_exact<CPW>(pk, s_n, j0, lane, dti, dta, dlim);
+        {
+            const int j = j0 + lane;
+#pragma unroll
+            for (int c = 0; c < CPW; ++c) {
+                const bool real = j < s_n[c];
+                const int kk = pk[c];
+                const float dl = event_delta(dti, dta, kk);
+                sd[c] += real ? dl : 0.f;
+                s_u[lane * P + c] = pu[c];
+                s_k[lane * P + c] = kk;
+                s_w[lane * P + c] = dl * pu[c] * pu[c];
+                s_r[lane * P + c] = (real && (unsigned)(kk - 1) < (unsigned)kKT3) ? kk : 0;
+            }
+        }
+        __syncwarp();
+        if (j0 + kR3 < n_max) {
+            fetch_f<T, CPW>(u, s_beg, s_n, j0 + kR3, lane, pu);
+            fetch_k<CPW>(a.k, s_beg, s_n, j0 + kR3, lane, pk);
+        }
+        if (!exact) {
+            // every real event has a tabulated gap; padding slots read the
+            // identity row with w = 0: no branch in the loop
+            float dec[G], u0 = s_u[grp], w0 = s_w[grp];
+            tab_row3<G>(tab, s_r[grp], q, dec);
+            int r1 = s_r[P + grp];
+#pragma unroll 8
+            for (int i = 0; i < kR3; ++i) {
+                const int i1 = min(i + 1, kR3 - 1), i2 = min(i + 2, kR3 - 1);
+                float dn[G];
+                tab_row3<G>(tab, r1, q, dn);
+                const float u1 = s_u[i1 * P + grp], w1 = s_w[i1 * P + grp];
+                r1 = s_r[i2 * P + grp];
+                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+                for (int g = 0; g < G; g += 4) {
+                    eta[g] = fmaf(dec[g], eta[g], w0);
+                    eta[g + 1] = fmaf(dec[g + 1], eta[g + 1], w0);
+                    eta[g + 2] = fmaf(dec[g + 2], eta[g + 2], w0);
+                    eta[g + 3] = fmaf(dec[g + 3], eta[g + 3], w0);
+                    s0 = fmaf(cc[g], eta[g], s0);
+                    s1 = fmaf(cc[g + 1], eta[g + 1], s1);
+                    s2 = fmaf(cc[g + 2], eta[g + 2], s2);
+                    s3 = fmaf(cc[g + 3], eta[g + 3], s3);
+                }
+                float acc = (s0 + s1) + (s2 + s3);
+                if (LPC > 1) acc = group_sum<LPC>(acc);
+                if (q == 0) s_y[i * P + grp] = fmaf(Dv, u0, u0 * acc);
+#pragma unroll
+                for (int g = 0; g < G; ++g) dec[g] = dn[g];
+                u0 = u1;
+                w0 = w1;
+            }
+        } else {
+#pragma unroll 1
+            for (int i = 0; i < kR3; ++i) {
+                const float uv = s_u[i * P + grp];
+                const int kv = s_k[i * P + grp];
+                const bool real = j0 + i < n;
+                const float dl = event_delta(dti, dta, kv);
+                const bool hit = (unsigned)(kv - 1) < (unsigned)kKT3;
+                float dec[G];
+                tab_row3<G>(tab, (real && hit) ? kv : 0, q, dec);
+                if (real && (!hit || dl > dlim)) {
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        dec[g] = decay_exact(dl, A2[g]);
+                        if (dl > dclamp) {
+                            const float x = dl * A2[g];
+                            corr[g] += fmaxf(fminf(x, 126.0f), -126.0f) - x;
+                        }
+                    }
+                }
+                const float w = real ? dl * uv * uv : 0.f;
+                float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    eta[g] = fmaf(dec[g], eta[g], w);
+                    if (g & 1) s1 = fmaf(cc[g], eta[g], s1); else s0 = fmaf(cc[g], eta[g], s0);
+                }
+                float acc = s0 + s1;
+                if (LPC > 1) acc = group_sum<LPC>(acc);
+                if (q == 0) s_y[i * P + grp] = fmaf(Dv, uv, uv * acc);
+            }
+        }
+        // chunk state after a chunk end or after the channel's last event
+        // (padding slots leave the state unchanged)
+        const int jend = j0 + kR3;
+        const bool xw = n > j0 && (n <= jend || jend % kChunkX == 0);
+        if (__any_sync(kFull, xw)) {
+            float t[CPW];
+#pragma unroll
+            for (int c = 0; c < CPW; ++c) t[c] = sd[c];
+            const float sdel = warp_channel_sum<CPW>(t, lane);
+            const int c = (min(n, jend) - 1) / kChunkX;
+            if (xw && c < a.n_chunks) {
+                float* xo = a.x + ((int64_t)ch * a.n_chunks + c) * 2 * N;
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const int s = q * G + g;
+                    if (s < N) {
+                        xo[2 * s] = exp2f(fmaf(A2[g], sdel, corr[g]));
+                        xo[2 * s + 1] = a.B[d * N + s] * eta[g];
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        {
+            const int j = j0 + lane;
+            T* out = static_cast<T*>(a.out);
+#pragma unroll 4
+            for (int c = 0; c < CPW; ++c) {
+                if (j < s_n[c]) {
+                    const int e = s_beg[c] + j;
+                    const float y = s_y[lane * P + c];
+                    out[e] = from_f32<T>(y);
+                    if (a.z != nullptr) {
+                        const float zv = to_f32<T>(static_cast<const T*>(a.z)[e]);
+                        static_cast<T*>(a.out_z)[e] = from_f32<T>(y * silu(zv));
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    }
+}
+
+// =========================================================== backward ====
+// Per channel and chunk of 2048 events: pass 1 runs the recurrence forward
+// from the chunk's start state and saves the state entering every tile of
+// kCkpt events (workspace slots as scan_bwd.cu); pass 2 walks batches, tiles
+// and events last to first, recomputing each tile's states from its
+// checkpoint into registers.  Per-event sums over a channel's states are
+// reduced over its LPC lanes once per tile (transposed: lane q finalises
+// events q*TB/LPC .. q*TB/LPC + TB/LPC - 1 of the tile).
+template <typename T, int G, int LPC>
+__global__ void __launch_bounds__(32)
+dw_bwd_v3(ScanArgs a, int bgroups) {
+    using V = V3<G, LPC>;
+    constexpr int CPW = V::CPW, P = V::P, NP = V::NP;
+    constexpr int TB = kCkpt;
+    constexpr int EPL = TB / LPC;
+    extern __shared__ __align__(16) float sm3[];
+    float* tab = sm3;
+    float* s_u = tab + V::TAB;
+    int* s_k = reinterpret_cast<int*>(s_u + kR3 * P);
+    float* s_d = reinterpret_cast<float*>(s_k + kR3 * P);
+    float* s_du = s_d + kR3 * P;
+    int* s_cb = reinterpret_cast<int*>(s_du + kR3 * P);   // chunk start of each channel
+    int* s_len = s_cb + CPW;                               // chunk length of each channel
+    int* s_beg = s_len + CPW;
+    int* s_n = s_beg + CPW;
+
+    const int lane = threadIdx.x, grp = lane / LPC, q = lane % LPC;
+    const int d = blockIdx.x / bgroups;
+    const int b0 = (blockIdx.x % bgroups) * CPW;
+    const int N = a.dstate;
+    if (lane < CPW) {
+        const int c = (b0 + lane) * a.dim + d;
+        s_beg[lane] = a.cu[c];
+        s_n[lane] = a.cu[c + 1] - a.cu[c];
+    }
+    build_table3<NP>(tab, a, d, lane);
+    const int ch = (b0 + grp) * a.dim + d;
+    const int beg = s_beg[grp], n = s_n[grp];
+    const int nch = (n + kChunkX - 1) / kChunkX;
+    const int nch_max = warp_max(nch);
+
+    float cc[G], ccA[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int s = q * G + g;
+        const bool o = s < N;
+        const float Ar = o ? a.A[d * a.A_sd + s * a.A_sn] : 0.f;
+        cc[g] = o ? a.B[d * N + s] * a.C[d * N + s] : 0.f;
+        ccA[g] = cc[g] * Ar;
+    }
+    const float dti = a.dt_idle[d], dta = a.dt_active[d];
+    const float Dv = a.D ? a.D[d] : 0.f;
+    const T* u = static_cast<const T*>(a.u);
+    const T* dout = static_cast<const T*>(a.dout);
+    float* ck = a.ws_ckpt + ((int64_t)(beg >> 3) + ch) * NP + q * G;
+
+    // decays of one event: table row (row 0 = identity for padding slots);
+    // EXACT batches send real events outside the table to exp2 in double
+    auto decays = [&](auto exact_c, int kv, bool real, float dl, float (&dec)[G]) {
+        constexpr bool EXACT = decltype(exact_c)::value;
+        if (!EXACT) {
+            tab_row3<G>(tab, kv, q, dec);
+        } else {
+            const bool hit = (unsigned)(kv - 1) < (unsigned)kKT3;
+            tab_row3<G>(tab, (real && hit) ? kv : 0, q, dec);
+            if (real && !hit) {
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const int s = q * G + g;
+                    const float Ar = s < N ? a.A[d * a.A_sd + s * a.A_sn] : 0.f;
+                    dec[g] = decay_exact(dl, (float)((double)Ar * 1.4426950408889634));
+                }
+            }
+        }
+    };
+
+    float gam[G], anx[G], SA[G], SB[G], QE[G], tA[G], tB[G], tQ[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        gam[g] = 0.f; anx[g] = 1.f;
+        tA[g] = tB[g] = tQ[g] = 0.f;
+    }
+    float t_ddi = 0.f, t_dda = 0.f, t_dD = 0.f;
+
+    for (int c = nch_max - 1; c >= 0; --c) {
+        const int cs = c * kChunkX;
+        const int len = (c < nch) ? min(n - cs, kChunkX) : 0;
+        const int len_max = warp_max(len);
+        __syncwarp();
+        if (lane < CPW) {
+            const int nl = s_n[lane];
+            s_cb[lane] = s_beg[lane] + cs;
+            s_len[lane] = (cs < nl) ? min(nl - cs, kChunkX) : 0;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int g = 0; g < G; ++g) SA[g] = SB[g] = QE[g] = 0.f;
+        float c_ddi = 0.f, c_dda = 0.f, c_dD = 0.f;
+
+        // ---- pass 1: checkpoints of the chunk -----------------------------
+        {
+            float eta[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                eta[g] = 0.f;
+                const int s = q * G + g;
+                if (c < nch && c > 0 && c - 1 < a.n_chunks && s < N) {
+                    const float hv = a.x[((int64_t)ch * a.n_chunks + c - 1) * 2 * N + 2 * s + 1];
+                    const float wb = a.B[d * N + s];
+                    eta[g] = (wb != 0.f) ? hv / wb : 0.f;
+                }
+            }
+            float pu[CPW];
+            int pk[CPW];
+            fetch_f<T, CPW>(u, s_cb, s_len, 0, lane, pu);
+            fetch_k<CPW>(a.k, s_cb, s_len, 0, lane, pk);
+            for (int j0 = 0; j0 < len_max; j0 += kR3) {
+                const bool exact = batch_needs_exact<CPW>(pk, s_len, j0, lane, dti, dta, INFINITY);
+                __syncwarp();
+                stage<CPW, P>(s_u, pu, lane);
+                stage<CPW, P>(s_k, pk, lane);
+                __syncwarp();
+                if (j0 + kR3 < len_max) {
+                    fetch_f<T, CPW>(u, s_cb, s_len, j0 + kR3, lane, pu);
+                    fetch_k<CPW>(a.k, s_cb, s_len, j0 + kR3, lane, pk);
+                }
+                auto run = [&](auto exact_c) {
+#pragma unroll 1
+                    for (int t = 0; t < kR3 / TB; ++t) {
+                        if (j0 + t * TB < len) {
+                            float4* p = reinterpret_cast<float4*>(ck + (int64_t)((j0 + t * TB) / TB) * NP);
+#pragma unroll
+                            for (int j = 0; j < G / 4; ++j)
+                                p[j] = make_float4(eta[4 * j], eta[4 * j + 1], eta[4 * j + 2], eta[4 * j + 3]);
+                        }
+#pragma unroll
+                        for (int ii = 0; ii < TB; ++ii) {
+                            const int i = t * TB + ii;
+                            const float uv = s_u[i * P + grp];
+                            const int kv = s_k[i * P + grp];
+                            const float dl = event_delta(dti, dta, kv);
+                            float dec[G];
+                            decays(exact_c, kv, j0 + i < len, dl, dec);
+                            const float w = dl * uv * uv;
+#pragma unroll
+                            for (int g = 0; g < G; ++g) eta[g] = fmaf(dec[g], eta[g], w);
+                        }
+                    }
+                };
+                if (exact) run(std::true_type{}); else run(std::false_type{});
+            }
+        }
+
+        // ---- pass 2: batches, tiles and events last to first --------------
+        if (len_max > 0) {
+            float pu[CPW], pd[CPW];
+            int pk[CPW];
+            const int jlast = ((len_max - 1) / kR3) * kR3;
+            auto fetch_all = [&](int jb) {
+                fetch_f<T, CPW>(u, s_cb, s_len, jb, lane, pu);
+                fetch_k<CPW>(a.k, s_cb, s_len, jb, lane, pk);
+                fetch_f<T, CPW>(dout, s_cb, s_len, jb, lane, pd);
+                if (a.z != nullptr) {
+                    // gate: dout * z * sigmoid(z); dz written by the one lane that holds the event
+                    const int j = jb + lane;
+#pragma unroll
+                    for (int c2 = 0; c2 < CPW; ++c2) {
+                        if (j < s_len[c2]) {
+                            const int e = s_cb[c2] + j;
+                            const float zv = to_f32<T>(static_cast<const T*>(a.z)[e]);
+                            const float sg = 1.0f / (1.0f + expf(-zv));
+                            const float ov = to_f32<T>(static_cast<const T*>(a.out_fwd)[e]);
+                            static_cast<T*>(a.dz)[e] = from_f32<T>(pd[c2] * ov * sg * (1.0f + zv * (1.0f - sg)));
+                            pd[c2] = pd[c2] * (zv * sg);
+                        }
+                    }
+                }
+            };
+            fetch_all(jlast);
+            for (int jb = jlast; jb >= 0; jb -= kR3) {
+                const bool exact = batch_needs_exact<CPW>(pk, s_len, jb, lane, dti, dta, INFINITY);
+                __syncwarp();
+                stage<CPW, P>(s_u, pu, lane);
+                stage<CPW, P>(s_k, pk, lane);
+                stage<CPW, P>(s_d, pd, lane);
+                __syncwarp();
+                if (jb > 0) fetch_all(jb - kR3);
+                float eN[G];
+                {
+                    const int jt = jb + (kR3 / TB - 1) * TB;
+                    const bool ok = jt < len;
+                    const float4* p = reinterpret_cast<const float4*>(ck + (int64_t)(jt / TB) * NP);
+#pragma unroll
+                    for (int j = 0; j < G / 4; ++j) {
+                        const float4 v = ok ? p[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+                        eN[4 * j] = v.x; eN[4 * j + 1] = v.y; eN[4 * j + 2] = v.z; eN[4 * j + 3] = v.w;
+                    }
+                }
+                auto run = [&](auto exact_c) {
+#pragma unroll 1
+                    for (int t = kR3 / TB - 1; t >= 0; --t) {
+                        const int i0 = t * TB;
+                        float et[G], e0[G];
+#pragma unroll
+                        for (int g = 0; g < G; ++g) et[g] = e0[g] = eN[g];
+                        if (t > 0) {   // next (earlier) tile's checkpoint
+                            const int jt = jb + i0 - TB;
+                            const bool ok = jt < len;
+                            const float4* p = reinterpret_cast<const float4*>(ck + (int64_t)(jt / TB) * NP);
+#pragma unroll
+                            for (int j = 0; j < G / 4; ++j) {
+                                const float4 v = ok ? p[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+                                eN[4 * j] = v.x; eN[4 * j + 1] = v.y; eN[4 * j + 2] = v.z; eN[4 * j + 3] = v.w;
+                            }
+                        }
+                        // forward recompute of the tile
+                        float eti[TB][G], te[TB], tg[TB], ta[TB];
+#pragma unroll
+                        for (int ii = 0; ii < TB; ++ii) {
+                            const int i = i0 + ii;
+                            const float uv = s_u[i * P + grp];
+                            const int kv = s_k[i * P + grp];
+                            const float qv = s_d[i * P + grp] * uv;
+                            const float dl = event_delta(dti, dta, kv);
+                            float dec[G];
+                            decays(exact_c, kv, jb + i < len, dl, dec);
+                            const float w = dl * uv * uv;
+                            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+                            for (int g = 0; g < G; ++g) {
+                                et[g] = fmaf(dec[g], et[g], w);
+                                eti[ii][g] = et[g];
+                                if (g & 1) s1 = fmaf(cc[g], et[g], s1); else s0 = fmaf(cc[g], et[g], s0);
+                                QE[g] = fmaf(qv, et[g], QE[g]);
+                            }
+                            te[ii] = s0 + s1;
+                        }
+                        // reverse over the tile: per-lane partial sums
+#pragma unroll
+                        for (int ii = TB - 1; ii >= 0; --ii) {
+                            const int i = i0 + ii;
+                            const float uv = s_u[i * P + grp];
+                            const int kv = s_k[i * P + grp];
+                            const float qv = s_d[i * P + grp] * uv;
+                            const float dl = event_delta(dti, dta, kv);
+                            float dec[G];
+                            decays(exact_c, kv, jb + i < len, dl, dec);
+                            const float w = dl * uv * uv;
+                            float tg0 = 0.f, tg1 = 0.f, ta0 = 0.f, ta1 = 0.f;
+#pragma unroll
+                            for (int g = 0; g < G; ++g) {
+                                gam[g] = fmaf(anx[g], gam[g], qv);
+                                // gam * (eta_i - w_i), formed as gam * a_i * eta_{i-1}:
+                                // no cancellation when the state has decayed
+                                const float ep = (ii > 0) ? eti[ii > 0 ? ii - 1 : 0][g] : e0[g];
+                                const float pr = gam[g] * (dec[g] * ep);
+                                SB[g] = fmaf(gam[g], w, SB[g]);
+                                SA[g] = fmaf(pr, dl, SA[g]);
+                                if (g & 1) {
+                                    ta1 = fmaf(ccA[g], pr, ta1);
+                                    tg1 = fmaf(cc[g], gam[g], tg1);
+                                } else {
+                                    ta0 = fmaf(ccA[g], pr, ta0);
+                                    tg0 = fmaf(cc[g], gam[g], tg0);
+                                }
+                                anx[g] = dec[g];
+                            }
+                            tg[ii] = tg0 + tg1;
+                            ta[ii] = ta0 + ta1;
+                        }
+                        group_transpose_sum<LPC, TB>(te, q);
+                        group_transpose_sum<LPC, TB>(tg, q);
+                        group_transpose_sum<LPC, TB>(ta, q);
+                        // this lane finalises events i0 + q*EPL + e of the tile
+#pragma unroll
+                        for (int e = 0; e < EPL; ++e) {
+                            const int i = i0 + q * EPL + e;
+                            if (jb + i < s_len[grp]) {
+                                const float uv = s_u[i * P + grp];
+                                const int kv = s_k[i * P + grp];
+                                const float dv = s_d[i * P + grp];
+                                const float dl = event_delta(dti, dta, kv);
+                                s_du[i * P + grp] = fmaf(Dv, dv, fmaf(2.f * uv * dl, tg[e], dv * te[e]));
+                                const float ddel = fmaf(uv * uv, tg[e], ta[e]);
+                                c_ddi = fmaf(ddel, (float)(kv - 1), c_ddi);
+                                c_dda += ddel;
+                                c_dD = fmaf(dv, uv, c_dD);
+                            }
+                        }
+                    }
+                };
+                if (exact) run(std::true_type{}); else run(std::false_type{});
+                __syncwarp();
+                {
+                    const int j = jb + lane;
+                    T* du = static_cast<T*>(a.du);
+#pragma unroll 4
+                    for (int c2 = 0; c2 < CPW; ++c2)
+                        if (j < s_len[c2]) du[s_cb[c2] + j] = from_f32<T>(s_du[lane * P + c2]);
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            tA[g] += SA[g];
+            tB[g] += SB[g];
+            tQ[g] += QE[g];
+        }
+        t_ddi += c_ddi;
+        t_dda += c_dda;
+        t_dD += c_dD;
+    }
+    // the scalar sums of a channel are spread over its LPC lanes
+    t_ddi = group_sum<LPC>(t_ddi);
+    t_dda = group_sum<LPC>(t_dda);
+    t_dD = group_sum<LPC>(t_dD);
+    float* part = a.ws_part + (int64_t)ch * a.part_stride;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int s = q * G + g;
+        if (s < N) {
+            part[s] = cc[g] * tA[g];
+            part[NP + s] = a.C[d * N + s] * tB[g];
+            part[2 * NP + s] = a.B[d * N + s] * tQ[g];
+        }
+    }
+    if (q == 0) {
+        part[3 * NP] = t_ddi;
+        part[3 * NP + 1] = t_dda;
+        part[3 * NP + 2] = t_dD;
+    }
+}
+
+// ====================================================== forward, split ====
+// Two phases per staged batch of 32 events:
+//   A  lane (channel, state group of G states) runs the recurrence
+//      eta = a*eta + w over the batch and stores every state to shared memory
+//      (only the state chain is sequential; a handful of instructions per
+//      event and G <= 4 states per lane give many warps);
+//   B  lane = event: y = D*u + u*sum_s cc_s*eta_s read back from shared
+//      memory for each of the warp's channels, stored coalesced.
+// A CTA holds the WPB warps of one feature d, which share one decay table.
+template <int G, int NP>
+struct V4 {
+    static constexpr int LPC = NP / G;
+    static constexpr int CPW = 32 / LPC;
+    static constexpr int P = CPW + 1;
+    static constexpr int EP = CPW * NP + 4;   // floats per event row of s_eta (== 4 mod 32)
+    static constexpr int WARP_FLOATS = 4 * kR3 * P + kR3 * EP + 2 * CPW;
+};
+
+// Decay table of a CTA: [state][row] for G < 4 (scalar reads), float4
+// groups [state/4][row] (as build_table3) for G >= 4.
+template <int NP, int G>
+__device__ void build_table_block(float* tab, const ScanArgs& a, int d) {
+    const float dti = a.dt_idle[d], dta = a.dt_active[d];
+    for (int e = threadIdx.x; e < kRows3 * NP; e += blockDim.x) {
+        const int row = e / NP, s = e % NP;
+        float v = 1.f;
+        if (row > 0 && s < a.dstate) {
+            const float A2 = (float)((double)a.A[d * a.A_sd + s * a.A_sn] * 1.4426950408889634);
+            v = decay_exact(event_delta(dti, dta, row), A2);
+        }
+        if (G >= 4) tab[((s >> 2) * kRows3 + row) * 4 + (s & 3)] = v;
+        else tab[s * kRows3 + row] = v;
+    }
+}
+
+template <int G>
+__device__ __forceinline__ void tab_row4(const float* tab, int row, int s0, float (&dec)[G]) {
+    if constexpr (G >= 4) {
+        tab_row3<G>(tab, row, s0 / G, dec);
+    } else {
+#pragma unroll
+        for (int g = 0; g < G; ++g) dec[g] = tab[(s0 + g) * kRows3 + row];
+    }
+}
+
+template <int G>
+__device__ __forceinline__ void sts_vec(float* p, const float (&v)[G]) {
+    if constexpr (G % 4 == 0) {
+#pragma unroll
+        for (int g = 0; g < G; g += 4)
+            *reinterpret_cast<float4*>(p + g) = make_float4(v[g], v[g + 1], v[g + 2], v[g + 3]);
+    } else if constexpr (G == 2) {
+        *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+    } else {
+#pragma unroll
+        for (int g = 0; g < G; ++g) p[g] = v[g];
+    }
+}
+
+// widest CTA of a layout (G >= 8 keeps more state per lane: smaller CTAs)
+template <int G>
+constexpr int v4_max_warps() { return G >= 8 ? 2 : 16; }
+
+template <typename T, int G, int NP>
+__global__ void __launch_bounds__(32 * v4_max_warps<G>())
+dw_fwd_v4(ScanArgs a, int blocks_per_d) {
+    using V = V4<G, NP>;
+    constexpr int CPW = V::CPW, P = V::P, LPC = V::LPC, EP = V::EP;
+    extern __shared__ __align__(16) float sm4[];
+    const int nwarps = blockDim.x >> 5;
+    {
+        // the layout below needs this much dynamic shared memory; never touch more
+        unsigned dyn;
+        asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+        if ((size_t)dyn < (size_t)(NP * kRows3 + nwarps * V::WARP_FLOATS) * sizeof(float)) return;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = lane / LPC, q = lane % LPC;
+    const int d = blockIdx.x / blocks_per_d;
+    const int b0 = ((blockIdx.x % blocks_per_d) * nwarps + warp) * CPW;
+    float* tab = sm4;
+    float* wbase = sm4 + NP * kRows3 + warp * V::WARP_FLOATS;
+    float* s_u = wbase;
+    int* s_k = reinterpret_cast<int*>(s_u + kR3 * P);
+    float* s_w = reinterpret_cast<float*>(s_k + kR3 * P);
+    int* s_r = reinterpret_cast<int*>(s_w + kR3 * P);
+    float* s_eta = reinterpret_cast<float*>(s_r + kR3 * P);
+    int* s_beg = reinterpret_cast<int*>(s_eta + kR3 * EP);
+    int* s_n = s_beg + CPW;
+    const int N = a.dstate;
+
+    if (lane < CPW) {
+        const int c = (b0 + lane) * a.dim + d;
+        s_beg[lane] = a.cu[c];
+        s_n[lane] = a.cu[c + 1] - a.cu[c];
+    }
+    build_table_block<NP, G>(tab, a, d);
+    __syncthreads();
+
+    const int ch = (b0 + grp) * a.dim + d;
+    const int n = s_n[grp];
+    const int n_max = warp_max(n);
+    const int s0 = q * G;
+
+    float A2[G], eta[G], corr[G];
+    float amax = 0.f;
+    bool decaying = true;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int st = s0 + g;
+        const float Ar = st < N ? a.A[d * a.A_sd + st * a.A_sn] : 0.f;
+        A2[g] = (float)((double)Ar * 1.4426950408889634);
+        eta[g] = corr[g] = 0.f;
+        amax = fmaxf(amax, fabsf(A2[g]));
+        decaying = decaying && A2[g] <= 0.f;
+    }
+    // phase B needs cc of every state
+    float ccall[NP];
+#pragma unroll
+    for (int st = 0; st < NP; ++st) ccall[st] = st < N ? a.B[d * N + st] * a.C[d * N + st] : 0.f;
+    const float dti = a.dt_idle[d], dta = a.dt_active[d];
+    const float Dv = a.D ? a.D[d] : 0.f;
+    decaying = decaying && dti >= 0.f && dta >= 0.f;
+    const float dclamp = amax > 0.f ? 126.0f / amax : INFINITY;
+    const float dlim = warp_all_min(decaying ? INFINITY : dclamp);
+    float sd[CPW];
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) sd[c] = 0.f;
+
+    const T* u = static_cast<const T*>(a.u);
+    float pu[CPW];
+    int pk[CPW];
+    fetch_f<T, CPW>(u, s_beg, s_n, 0, lane, pu);
+    fetch_k<CPW>(a.k, s_beg, s_n, 0, lane, pk);
+    for (int j0 = 0; j0 < n_max; j0 += kR3) {
+        const bool exact = batch_needs_exact<CPW>(pk, s_n, j0, lane, dti, dta, dlim);
+        {
+            const int j = j0 + lane;
+#pragma unroll
+            for (int c = 0; c < CPW; ++c) {
+                const bool real = j < s_n[c];
+                const int kk = pk[c];
+                const float dl = event_delta(dti, dta, kk);
+                sd[c] += real ? dl : 0.f;
+                s_u[lane * P + c] = pu[c];
+                s_k[lane * P + c] = kk;
+                s_w[lane * P + c] = dl * pu[c] * pu[c];
+                s_r[lane * P + c] = (real && (unsigned)(kk - 1) < (unsigned)kKT3) ? kk : 0;
+            }
+        }
+        __syncwarp();
+        if (j0 + kR3 < n_max) {
+            fetch_f<T, CPW>(u, s_beg, s_n, j0 + kR3, lane, pu);
+            fetch_k<CPW>(a.k, s_beg, s_n, j0 + kR3, lane, pk);
+        }
+        float* erow = s_eta + grp * NP + s0;
+        // ---- phase A: the state recurrence of the batch
+        if (!exact) {
+            float dec[G];
+            tab_row4<G>(tab, s_r[grp], s0, dec);
+            float w0 = s_w[grp];
+            int r1 = s_r[P + grp];
+#pragma unroll 8
+            for (int i = 0; i < kR3; ++i) {
+                const int i1 = min(i + 1, kR3 - 1), i2 = min(i + 2, kR3 - 1);
+                float dn[G];
+                tab_row4<G>(tab, r1, s0, dn);
+                const float w1 = s_w[i1 * P + grp];
+                r1 = s_r[i2 * P + grp];
+#pragma unroll
+                for (int g = 0; g < G; ++g) eta[g] = fmaf(dec[g], eta[g], w0);
+                sts_vec<G>(erow + i * EP, eta);
+#pragma unroll
+                for (int g = 0; g < G; ++g) dec[g] = dn[g];
+                w0 = w1;
+            }
+        } else {
+#pragma unroll 1
+            for (int i = 0; i < kR3; ++i) {
+                const float uv = s_u[i * P + grp];
+                const int kv = s_k[i * P + grp];
+                const bool real = j0 + i < n;
+                const float dl = event_delta(dti, dta, kv);
+                const bool hit = (unsigned)(kv - 1) < (unsigned)kKT3;
+                float dec[G];
+                tab_row4<G>(tab, (real && hit) ? kv : 0, s0, dec);
+                if (real && (!hit || dl > dlim)) {
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        dec[g] = decay_exact(dl, A2[g]);
+                        if (dl > dclamp) {
+                            const float x = dl * A2[g];
+                            corr[g] += fmaxf(fminf(x, 126.0f), -126.0f) - x;
+                        }
+                    }
+                }
+                const float w = real ? dl * uv * uv : 0.f;
+#pragma unroll
+                for (int g = 0; g < G; ++g) eta[g] = fmaf(dec[g], eta[g], w);
+                sts_vec<G>(erow + i * EP, eta);
+            }
+        }
+        // chunk state after a chunk end or after the channel's last event
+        const int jend = j0 + kR3;
+        const bool xw = n > j0 && (n <= jend || jend % kChunkX == 0);
+        if (__any_sync(kFull, xw)) {
+            float t[CPW];
+#pragma unroll
+            for (int c = 0; c < CPW; ++c) t[c] = sd[c];
+            const float sdel = warp_channel_sum<CPW>(t, lane);
+            const int c = (min(n, jend) - 1) / kChunkX;
+            if (xw && c < a.n_chunks) {
+                float* xo = a.x + ((int64_t)ch * a.n_chunks + c) * 2 * N;
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const int st = s0 + g;
+                    if (st < N) {
+                        xo[2 * st] = exp2f(fmaf(A2[g], sdel, corr[g]));
+                        xo[2 * st + 1] = a.B[d * N + st] * eta[g];
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        // ---- phase B: lane = event, one output per warp channel
+        {
+            const int j = j0 + lane;
+            T* out = static_cast<T*>(a.out);
+            const float* ev = s_eta + lane * EP;
+#pragma unroll 2
+            for (int c = 0; c < CPW; ++c) {
+                float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int st = 0; st < NP; st += 4) {
+                    const float4 e4 = *reinterpret_cast<const float4*>(ev + c * NP + st);
+                    s4[0] = fmaf(ccall[st], e4.x, s4[0]);
+                    s4[1] = fmaf(ccall[st + 1], e4.y, s4[1]);
+                    s4[2] = fmaf(ccall[st + 2], e4.z, s4[2]);
+                    s4[3] = fmaf(ccall[st + 3], e4.w, s4[3]);
+                }
+                const float acc = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+                const float uv = s_u[lane * P + c];
+                const float y = fmaf(Dv, uv, uv * acc);
+                if (j < s_n[c]) {
+                    const int e = s_beg[c] + j;
+                    out[e] = from_f32<T>(y);
+                    if (a.z != nullptr) {
+                        const float zv = to_f32<T>(static_cast<const T*>(a.z)[e]);
+                        static_cast<T*>(a.out_z)[e] = from_f32<T>(y * silu(zv));
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    }
+}
+
+template <typename T, int G, int NP>
+bcm_status launch_fwd_v4(const ScanArgs& a, cudaStream_t st) {
+    using V = V4<G, NP>;
+    const int bn = a.n_channels / a.dim;
+    const int groups = bn / V::CPW;          // warps per feature
+    int wpb = 1;
+    while (wpb * 2 <= v4_max_warps<G>() && groups % (wpb * 2) == 0) wpb *= 2;
+    const int blocks_per_d = groups / wpb;
+    const size_t smem = (size_t)(NP * kRows3 + wpb * V::WARP_FLOATS) * sizeof(float);
+    if (smem > 48 * 1024) {
+        // allow this kernel the device's opt-in maximum (once per device)
+        static std::mutex mu;
+        static int optin[64] = {};
+        int dev = 0;
+        BCM_CUDA_TRY(cudaGetDevice(&dev));
+        BCM_REQUIRE(dev >= 0 && dev < 64, "flat_ch fwd: device %d out of range", dev);
+        std::lock_guard<std::mutex> lock(mu);
+        if (optin[dev] == 0) {
+            int mx = 0;
+            BCM_CUDA_TRY(cudaDeviceGetAttribute(&mx, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+            BCM_CUDA_TRY(cudaFuncSetAttribute(dw_fwd_v4<T, G, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx));
+            optin[dev] = mx;
+        }
+        if (smem > (size_t)optin[dev]) {
+            set_error("flat_ch fwd: %zu bytes of shared memory exceed the device limit %d", smem, optin[dev]);
+            return BCM_ERR_UNSUPPORTED;
+        }
+    }
+    dw_fwd_v4<T, G, NP><<<a.dim * blocks_per_d, wpb * 32, smem, st>>>(a, blocks_per_d);
+    BCM_LAUNCH_CHECK();
+    return BCM_OK;
+}
+
+template <int G, int LPC>
+size_t v3_smem(bool bwd) {
+    using V = V3<G, LPC>;
+    const size_t stg = (size_t)kR3 * V::P * sizeof(float);
+    return V::TAB * sizeof(float) + (bwd ? 4 : 5) * stg + (bwd ? 4 : 2) * V::CPW * sizeof(int);
+}
+
+template <typename T, int G, int LPC>
+bcm_status launch_v3(const ScanArgs& a, bool bwd, cudaStream_t st) {
+    constexpr int CPW = V3<G, LPC>::CPW;
+    const int bn = a.n_channels / a.dim;
+    const int bgroups = bn / CPW;
+    const int grid = a.dim * bgroups;
+    const size_t smem = v3_smem<G, LPC>(bwd);   // < 48 KB for every layout used
+    if (bwd) dw_bwd_v3<T, G, LPC><<<grid, 32, smem, st>>>(a, bgroups);
+    else dw_fwd_v3<T, G, LPC><<<grid, 32, smem, st>>>(a, bgroups);
+    BCM_LAUNCH_CHECK();
+    return BCM_OK;
+}
+
+int env_int(const char* name, int dflt) {
+    const char* e = getenv(name);
+    return e ? atoi(e) : dflt;
+}
+
+// Lanes per channel of each direction for dstate N (states per lane =
+// padded N / LPC).  BCM_V3_FWD_LPC / BCM_V3_BWD_LPC override the default.
+int v3_lpc(int N, bool bwd) {
+    static const int f = env_int("BCM_V3_FWD_LPC", 2);
+    static const int b = env_int("BCM_V3_BWD_LPC", 4);
+    if (N <= 8) return bwd ? 2 : 1;
+    const int l = bwd ? b : f;
+    return (l == 1 || l == 2 || l == 4) ? l : (bwd ? 4 : 2);
+}
+
+}  // namespace
+
+// The staged kernels apply when dstate <= 16 and the channels of one feature
+// fill whole warps (n_channels / dim a multiple of the channels per warp).
+bool v3_supported(const ScanArgs& a, bool bwd) {
+    static const int mode = env_int("BCM_SCAN_V3", 1);
+    if (mode == 0 || a.dstate > 16 || a.dim <= 0 || a.n_channels % a.dim != 0) return false;
+    const int bn = a.n_channels / a.dim;
+    return bn % (32 / v3_lpc(a.dstate, bwd)) == 0;
+}
+
+bcm_status v3_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t st) {
+    const int lpc = v3_lpc(a.dstate, bwd);
+    static const int v4g = env_int("BCM_V4_G", 2);
+    return dispatch_dtype(dtype, [&](auto tag) -> bcm_status {
+        using T = decltype(tag);
+        if (!bwd && v4g > 0) {
+            const int NP = a.dstate <= 8 ? 8 : 16;
+            const int cpw = 32 * min(v4g, NP) / NP;
+            if ((a.n_channels / a.dim) % cpw == 0) {
+                if (NP == 8) {
+                    if (v4g == 1) return launch_fwd_v4<T, 1, 8>(a, st);
+                    if (v4g == 2) return launch_fwd_v4<T, 2, 8>(a, st);
+                    if (v4g >= 8) return launch_fwd_v4<T, 8, 8>(a, st);
+                    return launch_fwd_v4<T, 4, 8>(a, st);
+                }
+                if (v4g == 1) return launch_fwd_v4<T, 1, 16>(a, st);
+                if (v4g == 2) return launch_fwd_v4<T, 2, 16>(a, st);
+                if (v4g == 8) return launch_fwd_v4<T, 8, 16>(a, st);
+                if (v4g == 16) return launch_fwd_v4<T, 16, 16>(a, st);
+                return launch_fwd_v4<T, 4, 16>(a, st);
+            }
+        }
+        if (a.dstate <= 8) return bwd ? launch_v3<T, 4, 2>(a, true, st) : launch_v3<T, 8, 1>(a, false, st);
+        if (lpc == 1) return launch_v3<T, 16, 1>(a, bwd, st);
+        if (lpc == 2) return launch_v3<T, 8, 2>(a, bwd, st);
+        return launch_v3<T, 4, 4>(a, bwd, st);
+    });
+}
+
+}  // namespace bcm
