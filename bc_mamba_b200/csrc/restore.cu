@@ -13,18 +13,17 @@
 // range of positions, walked in windows of kTT = 128 positions:
 //   1. staging: each warp loads the window's events of 8 channels (32 events
 //      per coalesced load) and builds a 128-bit event mask per channel with
-//      warp OR-reductions (plus, forward, the event values in order);
-//   2. sweep: warp w takes positions [32w, 32w+32) of the window, lane c takes
-//      channel c, and walks them in order from its mask word: the forward
-//      writes the held value into a shared tile [128][32], the backward adds
-//      tile values and closes a segment at each set bit;
-//   3. the tile moves to or from HBM as 16-byte pieces of contiguous
-//      32-feature rows of (B, L, D).
-// No global load sits in the inner loop and every shared access is conflict
-// free.  The backward combines the four sub-window partials of each channel
-// in order and the CTA owning an event's start keeps reading past its range
-// until the event ends, so each dy is summed in one fixed order (the
-// reference uses fp32 atomics).
+//      warp OR-reductions (plus, forward, the event values in order); the
+//      first batch of the next window is loaded while the current one is swept;
+//   2. sweep: warp w takes positions [32w, 32w+32) of the window and lane c
+//      takes channel c, so every position is one coalesced row of 32 features
+//      of (B, L, D): the forward stores the held value row by row, the
+//      backward loads its 32 rows up front and closes a segment sum at each
+//      set bit of the mask.
+// No global load sits in the sweep.  The backward combines the four
+// sub-window partials of each channel in order and the CTA owning an event's
+// start keeps reading past its range until the event ends, so each dy is
+// summed in one fixed order (the reference uses fp32 atomics).
 #include "common.cuh"
 
 namespace bcm {
@@ -45,62 +44,6 @@ __device__ __forceinline__ int lower_bound_i32(const int32_t* a, int n, int key)
         if (a[mid] < key) lo = mid + 1; else hi = mid;
     }
     return lo;
-}
-
-template <typename T>
-__device__ __forceinline__ bool rows_vectorizable(int D, int d0, const void* p) {
-    constexpr int EPV = 16 / sizeof(T);
-    return (D % EPV == 0) && (d0 + kDB <= D) && (reinterpret_cast<uintptr_t>(p) % 16 == 0);
-}
-
-template <typename T>
-__device__ __forceinline__ void tile_store(const float (*tile)[kDB], T* out, int b, int L, int D,
-                                           int d0, int t0, int rows, bool vec) {
-    constexpr int EPV = 16 / sizeof(T);
-    constexpr int VPR = kDB / EPV;
-    if (vec) {
-        for (int idx = threadIdx.x; idx < rows * VPR; idx += kWarpsR * 32) {
-            const int r = idx / VPR, v = idx % VPR;
-            alignas(16) T pack[EPV];
-#pragma unroll
-            for (int e = 0; e < EPV; ++e) pack[e] = from_f32<T>(tile[r][v * EPV + e]);
-            *reinterpret_cast<uint4*>(out + ((int64_t)b * L + t0 + r) * D + d0 + v * EPV) =
-                *reinterpret_cast<const uint4*>(pack);
-        }
-    } else {
-        for (int idx = threadIdx.x; idx < rows * kDB; idx += kWarpsR * 32) {
-            const int r = idx / kDB, c = idx % kDB;
-            if (d0 + c < D) out[((int64_t)b * L + t0 + r) * D + d0 + c] = from_f32<T>(tile[r][c]);
-        }
-    }
-}
-
-template <typename T>
-__device__ __forceinline__ void tile_load(float (*tile)[kDB], const T* src, int b, int L, int D, int d0,
-                                          int t0, int rows, bool vec) {
-    constexpr int EPV = 16 / sizeof(T);
-    constexpr int VPR = kDB / EPV;
-    if (vec) {
-        for (int idx = threadIdx.x; idx < kTT * VPR; idx += kWarpsR * 32) {
-            const int r = idx / VPR, v = idx % VPR;
-            alignas(16) T pack[EPV];
-            if (r < rows) {
-                *reinterpret_cast<uint4*>(pack) =
-                    *reinterpret_cast<const uint4*>(src + ((int64_t)b * L + t0 + r) * D + d0 + v * EPV);
-#pragma unroll
-                for (int e = 0; e < EPV; ++e) tile[r][v * EPV + e] = to_f32<T>(pack[e]);
-            } else {
-#pragma unroll
-                for (int e = 0; e < EPV; ++e) tile[r][v * EPV + e] = 0.f;
-            }
-        }
-    } else {
-        for (int idx = threadIdx.x; idx < kTT * kDB; idx += kWarpsR * 32) {
-            const int r = idx / kDB, c = idx % kDB;
-            tile[r][c] = (r < rows && d0 + c < D)
-                             ? to_f32<T>(src[((int64_t)b * L + t0 + r) * D + d0 + c]) : 0.f;
-        }
-    }
 }
 
 // Staging of one channel's events in [t0, wend) starting at local index p:
@@ -150,7 +93,6 @@ __global__ void __launch_bounds__(kWarpsR * 32)
 restore_fwd_kernel(const Tin* __restrict__ y, const int32_t* __restrict__ ts,
                    const int32_t* __restrict__ cu, int D, int L, int part_len,
                    int n_dblk, Tout* __restrict__ out) {
-    __shared__ __align__(16) float tile[kTT][kDB];
     __shared__ float s_val[kDB][kTT + 1];    // event values of the window, in order
     __shared__ uint32_t s_mask[kDB][kMP];
     __shared__ float s_carry[kDB];           // value held at the window start
@@ -162,7 +104,6 @@ restore_fwd_kernel(const Tin* __restrict__ y, const int32_t* __restrict__ ts,
     const int t_beg = part * part_len;
     const int t_end = min(L, t_beg + part_len);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const bool vec = rows_vectorizable<Tout>(D, d0, out);
 
     int c_beg[kChPerWarp], c_n[kChPerWarp];
 #pragma unroll
@@ -185,19 +126,31 @@ restore_fwd_kernel(const Tin* __restrict__ y, const int32_t* __restrict__ ts,
         s_carry[warp * kChPerWarp + lane] = (p > 0) ? to_f32<Tin>(y[beg + p - 1]) : 0.f;
     }
     __syncwarp();
-
-    for (int t0 = t_beg; t0 < t_end; t0 += kTT) {
-        const int wend = min(t0 + kTT, t_end);
-        // 1. staging (first 32 events of every channel loaded up front)
-        float carry_new[kChPerWarp], v_pre[kChPerWarp];
-        int p_new[kChPerWarp], t_pre[kChPerWarp];
+    // first 32 events of every channel of the next window, loaded ahead
+    float v_pre[kChPerWarp];
+    int t_pre[kChPerWarp];
+    auto prefetch = [&](const int (&pp)[kChPerWarp]) {
 #pragma unroll
         for (int ci = 0; ci < kChPerWarp; ++ci) {
-            const int j = s_p[warp * kChPerWarp + ci] + lane;
+            const int j = pp[ci] + lane;
             const bool in = j < c_n[ci];
             t_pre[ci] = in ? ts[c_beg[ci] + j] : INT_MAX;
             v_pre[ci] = in ? to_f32<Tin>(y[c_beg[ci] + j]) : 0.f;
         }
+    };
+    {
+        int p0[kChPerWarp];
+#pragma unroll
+        for (int ci = 0; ci < kChPerWarp; ++ci) p0[ci] = s_p[warp * kChPerWarp + ci];
+        prefetch(p0);
+    }
+    const bool cvalid = d0 + lane < D;
+
+    for (int t0 = t_beg; t0 < t_end; t0 += kTT) {
+        const int wend = min(t0 + kTT, t_end);
+        // 1. staging of this warp's 8 channels
+        float carry_new[kChPerWarp];
+        int p_new[kChPerWarp];
 #pragma unroll
         for (int ci = 0; ci < kChPerWarp; ++ci) {
             const int c = warp * kChPerWarp + ci;
@@ -208,8 +161,10 @@ restore_fwd_kernel(const Tin* __restrict__ y, const int32_t* __restrict__ ts,
             carry_new[ci] = last;
             p_new[ci] = p + taken;
         }
+        if (t0 + kTT < t_end) prefetch(p_new);   // in flight during the sweep
         __syncthreads();
-        // 2. sweep: lane = channel, this warp's 32 positions
+        // 2. sweep: lane = channel, this warp's 32 positions, each a coalesced
+        //    row of 32 features stored straight to (B, L, D)
         {
             const int c = lane;
             uint32_t before = 0;
@@ -219,10 +174,12 @@ restore_fwd_kernel(const Tin* __restrict__ y, const int32_t* __restrict__ ts,
             const uint32_t mw = s_mask[c][warp];
             int e = (int)before;
             float cur = e > 0 ? s_val[c][e - 1] : s_carry[c];
+            const int tw = t0 + warp * 32;
+            Tout* col = out + ((int64_t)b * L + tw) * D + d0 + c;
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 if ((mw >> i) & 1u) cur = s_val[c][e++];
-                tile[warp * 32 + i][c] = cur;
+                if (cvalid && tw + i < wend) col[(int64_t)i * D] = from_f32<Tout>(cur);
             }
         }
         __syncthreads();
@@ -232,9 +189,7 @@ restore_fwd_kernel(const Tin* __restrict__ y, const int32_t* __restrict__ ts,
             for (int ci = 0; ci < kChPerWarp; ++ci)
                 if (ci == lane) { s_p[warp * kChPerWarp + ci] = p_new[ci]; s_carry[warp * kChPerWarp + ci] = carry_new[ci]; }
         }
-        // 3. tile -> rows of (B, L, D)
-        tile_store<Tout>(tile, out, b, L, D, d0, t0, wend - t0, vec);
-        __syncthreads();
+        __syncwarp();
     }
 }
 
@@ -243,7 +198,6 @@ __global__ void __launch_bounds__(kWarpsR * 32)
 restore_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ ts,
                    const int32_t* __restrict__ cu, int D, int L, int part_len,
                    int n_dblk, float* __restrict__ dy) {
-    __shared__ __align__(16) float tile[kTT][kDB];
     __shared__ uint32_t s_mask[kDB][kMP];
     __shared__ float s_head[kWarpsR][kDB], s_tail[kWarpsR][kDB];
     __shared__ int s_cnt[kWarpsR][kDB];
@@ -256,7 +210,6 @@ restore_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ ts,
     const int t_beg = part * part_len;
     const int t_own_end = min(L, t_beg + part_len);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const bool vec = rows_vectorizable<T>(D, d0, dout);
 
     int c_beg[kChPerWarp], c_n[kChPerWarp];
 #pragma unroll
@@ -285,8 +238,24 @@ restore_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ ts,
     float open_acc = 0.f;
     int p_next[kChPerWarp];
     const int my_d = d0 + lane;
-    const int my_beg = (warp == 0 && my_d < D) ? cu[b * D + my_d] : 0;
+    const bool cvalid = my_d < D;
+    const int my_beg = cvalid ? cu[b * D + my_d] : 0;
     __syncthreads();
+    // first 32 events of every channel of the next window, loaded ahead
+    int t_pre[kChPerWarp];
+    auto prefetch = [&](const int (&pp)[kChPerWarp]) {
+#pragma unroll
+        for (int ci = 0; ci < kChPerWarp; ++ci) {
+            const int j = pp[ci] + lane;
+            t_pre[ci] = (j < c_n[ci]) ? ts[c_beg[ci] + j] : INT_MAX;
+        }
+    };
+    {
+        int p0[kChPerWarp];
+#pragma unroll
+        for (int ci = 0; ci < kChPerWarp; ++ci) p0[ci] = s_p[warp * kChPerWarp + ci];
+        prefetch(p0);
+    }
 
     for (int t0 = t_beg; t0 < L; t0 += kTT) {
         const bool owning = t0 < t_own_end;
@@ -298,22 +267,24 @@ restore_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ ts,
             if (!s_any) break;
         }
         const int wend = min(t0 + kTT, L);
-        // 1. tile + staging (event masks only).  Each warp first publishes the
-        //    advanced pointers of its own channels from the previous window (the
-        //    previous combine read the old values).
-        tile_load<T>(tile, dout, b, L, D, d0, t0, wend - t0, vec);
+        // 1. this warp's 32 rows of the window (lane = channel: each row one
+        //    coalesced load of 32 features) are issued first, then the staging
+        //    of event masks.  Each warp publishes the advanced pointers of its
+        //    own channels from the previous window (the previous combine read
+        //    the old values).
+        const int tw = t0 + warp * 32;
+        float v[32];
+        {
+            const T* col = dout + ((int64_t)b * L + tw) * D + my_d;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = (cvalid && tw + i < wend) ? to_f32<T>(col[(int64_t)i * D]) : 0.f;
+        }
         if (t0 != t_beg && lane < kChPerWarp) {
 #pragma unroll
             for (int ci = 0; ci < kChPerWarp; ++ci)
                 if (ci == lane) s_p[warp * kChPerWarp + ci] = p_next[ci];
         }
         __syncwarp();
-        int t_pre[kChPerWarp];
-#pragma unroll
-        for (int ci = 0; ci < kChPerWarp; ++ci) {
-            const int j = s_p[warp * kChPerWarp + ci] + lane;
-            t_pre[ci] = (j < c_n[ci]) ? ts[c_beg[ci] + j] : INT_MAX;
-        }
 #pragma unroll
         for (int ci = 0; ci < kChPerWarp; ++ci) {
             const int c = warp * kChPerWarp + ci;
@@ -322,6 +293,7 @@ restore_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ ts,
             p_next[ci] = p + stage_channel<T, false>(ts, nullptr, c_beg[ci], c_n[ci], p, t0, wend,
                                                      s_mask[c], nullptr, lane, dummy, t_pre[ci], 0.f);
         }
+        prefetch(p_next);   // in flight during the sweep and combine
         __syncthreads();
         // 2. sweep: lane = channel, positions [32w, 32w+32) of the window
         {
@@ -331,8 +303,7 @@ restore_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ ts,
             for (int w = 0; w < kMW; ++w)
                 if (w < warp) before += __popc(s_mask[c][w]);
             const uint32_t mw = s_mask[c][warp];
-            const int cbeg = (d0 + c < D) ? cu[b * D + d0 + c] : 0;
-            const int ebase = cbeg + s_p[c] + (int)before;   // global index of this piece's first event
+            const int ebase = my_beg + s_p[c] + (int)before;   // global index of this piece's first event
             float acc = 0.f, head = 0.f;
             int e = 0;
 #pragma unroll
@@ -343,7 +314,7 @@ restore_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ ts,
                     acc = 0.f;
                     ++e;
                 }
-                acc += tile[warp * 32 + i][c];
+                acc += v[i];
             }
             if (e == 0) head = acc;
             s_head[warp][c] = head;

@@ -4,19 +4,26 @@
 // selective_scan_fwd_kernel.cuh:403-728, selective_scan_bwd_kernel.cuh:
 // 635-1169, depthwise B/C); the layout is:
 //
-//  * a warp owns CPW = 32/LPC channels of the same feature d (batch rows
-//    b..b+CPW-1) and each channel's states are split over LPC lanes (G states
-//    per lane), so every lane of the warp shares one per-warp decay table
-//    (rows k = 1..kKT3 for the integer gap k, row 0 = identity);
+//  * warps own channels of one feature d (batch rows b..), so they share one
+//    decay table per feature (rows k = 1..kKT3 for the integer gap k, row 0 =
+//    identity), built once per CTA or warp with exp2 in double (correctly
+//    rounded: each entry is reused by every event with that gap);
 //  * events are staged 32 per channel at a time: one coalesced load per
 //    channel and array brings them into registers while the previous batch is
 //    processed, then a transposed shared-memory copy hands each lane its own
-//    channel's events (conflict-free);
-//  * slots past a channel's last event read the identity row with u = 0, so
-//    the inner loop needs no per-event predicate; per-event outputs go back
-//    through shared memory and leave as coalesced stores;
-//  * the backward keeps the eight recomputed states of a tile in registers
-//    and sums per-event quantities over the LPC lanes with shuffles.
+//    channel's events (conflict-free); padding slots past a channel's last
+//    event read the identity row with u = 0, so inner loops carry no per-event
+//    predicate, and a batch holding a gap outside the table (or, forward, a
+//    clamping exponent of non-decaying parameters) takes a separate exact loop;
+//  * forward (dw_fwd_v4): phase A runs the state recurrence with G <= 4 states
+//    per lane and stores the states of the batch to shared memory; phase B
+//    maps lanes to events and forms y = D*u + u*sum_s cc_s*eta_s for each
+//    channel, stored coalesced;
+//  * backward (dw_bwd_v3): 4 states per lane; per 2048-event chunk a forward
+//    pass saves the state entering every 8-event tile, then batches, tiles and
+//    events are walked last to first with the tile's states recomputed into
+//    registers; per-event sums over a channel's lanes are transposed
+//    reductions once per tile.
 #include <stdlib.h>
 
 #include <mutex>
@@ -146,201 +153,6 @@ __device__ __forceinline__ float warp_channel_sum(float (&v)[CPW], int lane) {
 #pragma unroll
     for (int o = 32 / CPW / 2; o > 0; o >>= 1) t += __shfl_xor_sync(kFull, t, o);
     return t;
-}
-
-// ============================================================ forward ====
-// Staging turns each event into (u, w = delta*u^2, table row) once; the fast
-// loop then only reads them, with the next event's decays loaded one event
-// ahead.  The exact path (gaps outside the table, clamping deltas of
-// non-decaying parameters) recomputes from (u, k).
-template <typename T, int G, int LPC>
-__global__ void __launch_bounds__(32)
-dw_fwd_v3(ScanArgs a, int bgroups) {
-    using V = V3<G, LPC>;
-    constexpr int CPW = V::CPW, P = V::P, NP = V::NP;
-    extern __shared__ __align__(16) float sm3[];
-    float* tab = sm3;
-    float* s_u = tab + V::TAB;
-    int* s_k = reinterpret_cast<int*>(s_u + kR3 * P);
-    float* s_w = reinterpret_cast<float*>(s_k + kR3 * P);
-    int* s_r = reinterpret_cast<int*>(s_w + kR3 * P);
-    float* s_y = reinterpret_cast<float*>(s_r + kR3 * P);
-    int* s_beg = reinterpret_cast<int*>(s_y + kR3 * P);
-    int* s_n = s_beg + CPW;
-
-    const int lane = threadIdx.x, grp = lane / LPC, q = lane % LPC;
-    const int d = blockIdx.x / bgroups;
-    const int b0 = (blockIdx.x % bgroups) * CPW;
-    const int N = a.dstate;
-    if (lane < CPW) {
-        const int c = (b0 + lane) * a.dim + d;
-        s_beg[lane] = a.cu[c];
-        s_n[lane] = a.cu[c + 1] - a.cu[c];
-    }
-    build_table3<NP>(tab, a, d, lane);   // ends with __syncwarp
-    const int ch = (b0 + grp) * a.dim + d;
-    const int n = s_n[grp];
-    const int n_max = warp_max(n);
-
-    float A2[G], cc[G], eta[G], corr[G];
-    float amax = 0.f;
-    bool decaying = true;
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const int s = q * G + g;
-        const bool o = s < N;
-        const float Ar = o ? a.A[d * a.A_sd + s * a.A_sn] : 0.f;
-        A2[g] = (float)((double)Ar * 1.4426950408889634);
-        cc[g] = o ? a.B[d * N + s] * a.C[d * N + s] : 0.f;
-        eta[g] = corr[g] = 0.f;
-        amax = fmaxf(amax, fabsf(A2[g]));
-        decaying = decaying && A2[g] <= 0.f;
-    }
-    const float dti = a.dt_idle[d], dta = a.dt_active[d];
-    const float Dv = a.D ? a.D[d] : 0.f;
-    decaying = decaying && dti >= 0.f && dta >= 0.f;
-    // exponents beyond +-126 clamp; with decaying parameters every exponent is
-    // <= 0 and a clamped one leaves prod(a) at or below 2^-126 either way, so
-    // only non-decaying warps send those events to the exact path
-    const float dclamp = amax > 0.f ? 126.0f / amax : INFINITY;
-    const float dlim = warp_all_min(decaying ? INFINITY : dclamp);
-    // sum of the deltas of each warp channel's events staged by this lane
-    float sd[CPW];
-#pragma unroll
-    for (int c = 0; c < CPW; ++c) sd[c] = 0.f;
-
-    const T* u = static_cast<const T*>(a.u);
-    float pu[CPW];
-    int pk[CPW];
-    fetch_f<T, CPW>(u, s_beg, s_n, 0, lane, pu);
-    fetch_k<CPW>(a.k, s_beg, s_n, 0, lane, pk);
-    for (int j0 = 0; j0 < n_max; j0 += kR3) {
-        const bool exact = batch_needs_exact<CPW>(pk, s_n, j0, lane, dti, dta, dlim);
-        {
-            const int j = j0 + lane;
-#pragma unroll
-            for (int c = 0; c < CPW; ++c) {
-                const bool real = j < s_n[c];
-                const int kk = pk[c];
-                const float dl = event_delta(dti, dta, kk);
-                sd[c] += real ? dl : 0.f;
-                s_u[lane * P + c] = pu[c];
-                s_k[lane * P + c] = kk;
-                s_w[lane * P + c] = dl * pu[c] * pu[c];
-                s_r[lane * P + c] = (real && (unsigned)(kk - 1) < (unsigned)kKT3) ? kk : 0;
-            }
-        }
-        __syncwarp();
-        if (j0 + kR3 < n_max) {
-            fetch_f<T, CPW>(u, s_beg, s_n, j0 + kR3, lane, pu);
-            fetch_k<CPW>(a.k, s_beg, s_n, j0 + kR3, lane, pk);
-        }
-        if (!exact) {
-            // every real event has a tabulated gap; padding slots read the
-            // identity row with w = 0: no branch in the loop
-            float dec[G], u0 = s_u[grp], w0 = s_w[grp];
-            tab_row3<G>(tab, s_r[grp], q, dec);
-            int r1 = s_r[P + grp];
-#pragma unroll 8
-            for (int i = 0; i < kR3; ++i) {
-                const int i1 = min(i + 1, kR3 - 1), i2 = min(i + 2, kR3 - 1);
-                float dn[G];
-                tab_row3<G>(tab, r1, q, dn);
-                const float u1 = s_u[i1 * P + grp], w1 = s_w[i1 * P + grp];
-                r1 = s_r[i2 * P + grp];
-                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-                for (int g = 0; g < G; g += 4) {
-                    eta[g] = fmaf(dec[g], eta[g], w0);
-                    eta[g + 1] = fmaf(dec[g + 1], eta[g + 1], w0);
-                    eta[g + 2] = fmaf(dec[g + 2], eta[g + 2], w0);
-                    eta[g + 3] = fmaf(dec[g + 3], eta[g + 3], w0);
-                    s0 = fmaf(cc[g], eta[g], s0);
-                    s1 = fmaf(cc[g + 1], eta[g + 1], s1);
-                    s2 = fmaf(cc[g + 2], eta[g + 2], s2);
-                    s3 = fmaf(cc[g + 3], eta[g + 3], s3);
-                }
-                float acc = (s0 + s1) + (s2 + s3);
-                if (LPC > 1) acc = group_sum<LPC>(acc);
-                if (q == 0) s_y[i * P + grp] = fmaf(Dv, u0, u0 * acc);
-#pragma unroll
-                for (int g = 0; g < G; ++g) dec[g] = dn[g];
-                u0 = u1;
-                w0 = w1;
-            }
-        } else {
-#pragma unroll 1
-            for (int i = 0; i < kR3; ++i) {
-                const float uv = s_u[i * P + grp];
-                const int kv = s_k[i * P + grp];
-                const bool real = j0 + i < n;
-                const float dl = event_delta(dti, dta, kv);
-                const bool hit = (unsigned)(kv - 1) < (unsigned)kKT3;
-                float dec[G];
-                tab_row3<G>(tab, (real && hit) ? kv : 0, q, dec);
-                if (real && (!hit || dl > dlim)) {
-#pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        dec[g] = decay_exact(dl, A2[g]);
-                        if (dl > dclamp) {
-                            const float x = dl * A2[g];
-                            corr[g] += fmaxf(fminf(x, 126.0f), -126.0f) - x;
-                        }
-                    }
-                }
-                const float w = real ? dl * uv * uv : 0.f;
-                float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    eta[g] = fmaf(dec[g], eta[g], w);
-                    if (g & 1) s1 = fmaf(cc[g], eta[g], s1); else s0 = fmaf(cc[g], eta[g], s0);
-                }
-                float acc = s0 + s1;
-                if (LPC > 1) acc = group_sum<LPC>(acc);
-                if (q == 0) s_y[i * P + grp] = fmaf(Dv, uv, uv * acc);
-            }
-        }
-        // chunk state after a chunk end or after the channel's last event
-        // (padding slots leave the state unchanged)
-        const int jend = j0 + kR3;
-        const bool xw = n > j0 && (n <= jend || jend % kChunkX == 0);
-        if (__any_sync(kFull, xw)) {
-            float t[CPW];
-#pragma unroll
-            for (int c = 0; c < CPW; ++c) t[c] = sd[c];
-            const float sdel = warp_channel_sum<CPW>(t, lane);
-            const int c = (min(n, jend) - 1) / kChunkX;
-            if (xw && c < a.n_chunks) {
-                float* xo = a.x + ((int64_t)ch * a.n_chunks + c) * 2 * N;
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const int s = q * G + g;
-                    if (s < N) {
-                        xo[2 * s] = exp2f(fmaf(A2[g], sdel, corr[g]));
-                        xo[2 * s + 1] = a.B[d * N + s] * eta[g];
-                    }
-                }
-            }
-        }
-        __syncwarp();
-        {
-            const int j = j0 + lane;
-            T* out = static_cast<T*>(a.out);
-#pragma unroll 4
-            for (int c = 0; c < CPW; ++c) {
-                if (j < s_n[c]) {
-                    const int e = s_beg[c] + j;
-                    const float y = s_y[lane * P + c];
-                    out[e] = from_f32<T>(y);
-                    if (a.z != nullptr) {
-                        const float zv = to_f32<T>(static_cast<const T*>(a.z)[e]);
-                        static_cast<T*>(a.out_z)[e] = from_f32<T>(y * silu(zv));
-                    }
-                }
-            }
-        }
-        __syncwarp();
-    }
 }
 
 // =========================================================== backward ====
@@ -967,21 +779,17 @@ bcm_status launch_fwd_v4(const ScanArgs& a, cudaStream_t st) {
 }
 
 template <int G, int LPC>
-size_t v3_smem(bool bwd) {
+size_t bwd_v3_smem() {
     using V = V3<G, LPC>;
     const size_t stg = (size_t)kR3 * V::P * sizeof(float);
-    return V::TAB * sizeof(float) + (bwd ? 4 : 5) * stg + (bwd ? 4 : 2) * V::CPW * sizeof(int);
+    return V::TAB * sizeof(float) + 4 * stg + 4 * V::CPW * sizeof(int);   // < 48 KB
 }
 
 template <typename T, int G, int LPC>
-bcm_status launch_v3(const ScanArgs& a, bool bwd, cudaStream_t st) {
+bcm_status launch_bwd_v3(const ScanArgs& a, cudaStream_t st) {
     constexpr int CPW = V3<G, LPC>::CPW;
-    const int bn = a.n_channels / a.dim;
-    const int bgroups = bn / CPW;
-    const int grid = a.dim * bgroups;
-    const size_t smem = v3_smem<G, LPC>(bwd);   // < 48 KB for every layout used
-    if (bwd) dw_bwd_v3<T, G, LPC><<<grid, 32, smem, st>>>(a, bgroups);
-    else dw_fwd_v3<T, G, LPC><<<grid, 32, smem, st>>>(a, bgroups);
+    const int bgroups = (a.n_channels / a.dim) / CPW;
+    dw_bwd_v3<T, G, LPC><<<a.dim * bgroups, 32, bwd_v3_smem<G, LPC>(), st>>>(a, bgroups);
     BCM_LAUNCH_CHECK();
     return BCM_OK;
 }
@@ -991,14 +799,20 @@ int env_int(const char* name, int dflt) {
     return e ? atoi(e) : dflt;
 }
 
-// Lanes per channel of each direction for dstate N (states per lane =
-// padded N / LPC).  BCM_V3_FWD_LPC / BCM_V3_BWD_LPC override the default.
-int v3_lpc(int N, bool bwd) {
-    static const int f = env_int("BCM_V3_FWD_LPC", 2);
-    static const int b = env_int("BCM_V3_BWD_LPC", 4);
-    if (N <= 8) return bwd ? 2 : 1;
-    const int l = bwd ? b : f;
-    return (l == 1 || l == 2 || l == 4) ? l : (bwd ? 4 : 2);
+// States per lane of the split forward (BCM_V4_G = 1, 2 or 4 overrides the
+// default 2) and channels per warp of each direction.
+int fwd_g() {
+    static const int g = [] {
+        const int v = env_int("BCM_V4_G", 2);
+        return (v == 1 || v == 2 || v == 4) ? v : 2;
+    }();
+    return g;
+}
+
+int channels_per_warp(int N, bool bwd) {
+    const int NP = N <= 8 ? 8 : 16;
+    if (bwd) return N <= 8 ? 16 : 8;        // backward: 4 states per lane
+    return 32 * fwd_g() / NP;
 }
 
 }  // namespace
@@ -1008,36 +822,22 @@ int v3_lpc(int N, bool bwd) {
 bool v3_supported(const ScanArgs& a, bool bwd) {
     static const int mode = env_int("BCM_SCAN_V3", 1);
     if (mode == 0 || a.dstate > 16 || a.dim <= 0 || a.n_channels % a.dim != 0) return false;
-    const int bn = a.n_channels / a.dim;
-    return bn % (32 / v3_lpc(a.dstate, bwd)) == 0;
+    return (a.n_channels / a.dim) % channels_per_warp(a.dstate, bwd) == 0;
 }
 
 bcm_status v3_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t st) {
-    const int lpc = v3_lpc(a.dstate, bwd);
-    static const int v4g = env_int("BCM_V4_G", 2);
+    const int g = fwd_g();
     return dispatch_dtype(dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);
-        if (!bwd && v4g > 0) {
-            const int NP = a.dstate <= 8 ? 8 : 16;
-            const int cpw = 32 * min(v4g, NP) / NP;
-            if ((a.n_channels / a.dim) % cpw == 0) {
-                if (NP == 8) {
-                    if (v4g == 1) return launch_fwd_v4<T, 1, 8>(a, st);
-                    if (v4g == 2) return launch_fwd_v4<T, 2, 8>(a, st);
-                    if (v4g >= 8) return launch_fwd_v4<T, 8, 8>(a, st);
-                    return launch_fwd_v4<T, 4, 8>(a, st);
-                }
-                if (v4g == 1) return launch_fwd_v4<T, 1, 16>(a, st);
-                if (v4g == 2) return launch_fwd_v4<T, 2, 16>(a, st);
-                if (v4g == 8) return launch_fwd_v4<T, 8, 16>(a, st);
-                if (v4g == 16) return launch_fwd_v4<T, 16, 16>(a, st);
-                return launch_fwd_v4<T, 4, 16>(a, st);
-            }
+        if (bwd) return a.dstate <= 8 ? launch_bwd_v3<T, 4, 2>(a, st) : launch_bwd_v3<T, 4, 4>(a, st);
+        if (a.dstate <= 8) {
+            if (g == 1) return launch_fwd_v4<T, 1, 8>(a, st);
+            if (g == 4) return launch_fwd_v4<T, 4, 8>(a, st);
+            return launch_fwd_v4<T, 2, 8>(a, st);
         }
-        if (a.dstate <= 8) return bwd ? launch_v3<T, 4, 2>(a, true, st) : launch_v3<T, 8, 1>(a, false, st);
-        if (lpc == 1) return launch_v3<T, 16, 1>(a, bwd, st);
-        if (lpc == 2) return launch_v3<T, 8, 2>(a, bwd, st);
-        return launch_v3<T, 4, 4>(a, bwd, st);
+        if (g == 1) return launch_fwd_v4<T, 1, 16>(a, st);
+        if (g == 4) return launch_fwd_v4<T, 4, 16>(a, st);
+        return launch_fwd_v4<T, 2, 16>(a, st);
     });
 }
 
