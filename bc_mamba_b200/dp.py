@@ -47,9 +47,16 @@ def init_from_env(backend: Optional[str] = None, timeout_s: float = 120.0) -> tu
 
 
 class GradBucket:
-    """One flat buffer holding the gradients of `params`, all-reduced at once."""
+    """One flat buffer holding the gradients of `params`, all-reduced at once.
 
-    def __init__(self, params: Iterable[torch.Tensor], average: bool = True, group=None):
+    The parameters' .grad tensors are views into the buffer (as DDP's
+    gradient-as-bucket-view), so autograd accumulates straight into it and the
+    reduction is a single collective with no packing copies.  Call
+    `zero_grad()` instead of resetting .grad to None between steps (a None
+    grad would make autograd allocate a fresh tensor outside the bucket)."""
+
+    def __init__(self, params: Iterable[torch.Tensor], average: bool = True, group=None,
+                 overlap: bool = False):
         self.params: List[torch.Tensor] = [p for p in params]
         if not self.params:
             raise ValueError("GradBucket needs at least one parameter")
@@ -63,54 +70,78 @@ class GradBucket:
         self.group = group
         self._stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
         self._work = None
-
-    def _pack(self):
-        off = 0
-        for p in self.params:
-            n = p.numel()
-            if p.grad is None:
-                self.flat[off:off + n].zero_()
-            else:
-                self.flat[off:off + n].copy_(p.grad.reshape(-1))
-            off += n
-
-    def _unpack(self):
+        self._views = []
         off = 0
         for p in self.params:
             n = p.numel()
             v = self.flat[off:off + n].view_as(p)
-            if p.grad is None:
-                p.grad = v.clone()
-            else:
-                p.grad.copy_(v)
+            if p.grad is not None:
+                v.copy_(p.grad)
+            p.grad = v
+            self._views.append(v)
             off += n
+        # overlap: launch the reduction from autograd as soon as every
+        # parameter's gradient of this backward has been accumulated, so it
+        # runs beside the rest of the backward (e.g. the input-gradient ops)
+        self._pending = len(self.params)
+        self._armed = overlap
+        if overlap:
+            for p in self.params:
+                p.register_post_accumulate_grad_hook(self._on_accumulated)
+
+    def _on_accumulated(self, p):
+        if not self._armed or self._work is not None:
+            return
+        self._pending -= 1
+        if self._pending == 0:
+            self.start()
+
+    def zero_grad(self):
+        """Zero every gradient (one fill of the bucket) and re-arm the overlap."""
+        self._rebind()
+        self.flat.zero_()
+        self._pending = len(self.params)
+
+    def _rebind(self):
+        # a caller that replaced .grad (e.g. set it to None) gets the view back
+        for p, v in zip(self.params, self._views):
+            if p.grad is None:
+                v.zero_()
+                p.grad = v
+            elif p.grad.data_ptr() != v.data_ptr():
+                v.copy_(p.grad)
+                p.grad = v
 
     def start(self):
-        """Pack and launch the all-reduce (asynchronous with respect to the host)."""
+        """Launch the all-reduce (asynchronous with respect to the host)."""
         world = dist.get_world_size(self.group) if dist.is_initialized() else 1
         if world == 1:
             return self
+        self._rebind()
+        op = dist.ReduceOp.SUM
+        if self.average:
+            if dist.get_backend(self.group) == "nccl":
+                op = dist.ReduceOp.AVG
+            else:
+                self.flat.div_(world)
         if self._stream is not None:
             cur = torch.cuda.current_stream(self.flat.device)
             self._stream.wait_stream(cur)
             with torch.cuda.stream(self._stream):
-                self._pack()
-                if self.average:
-                    self.flat.div_(world)
-                self._work = dist.all_reduce(self.flat, group=self.group, async_op=True)
+                self._work = dist.all_reduce(self.flat, op=op, group=self.group, async_op=True)
         else:
-            self._pack()
-            if self.average:
-                self.flat.div_(world)
-            self._work = dist.all_reduce(self.flat, group=self.group, async_op=True)
+            self._work = dist.all_reduce(self.flat, op=op, group=self.group, async_op=True)
         return self
 
     def finish(self):
-        """Wait for the reduction and write the result back into .grad."""
+        """Wait for the reduction (the result is already in .grad); launches it
+        first when it has not been launched (no overlap, or some parameter got
+        no gradient in this backward)."""
+        if self._work is None:
+            self.start()
         if self._work is None:
             return
         self._work.wait()
         if self._stream is not None:
             torch.cuda.current_stream(self.flat.device).wait_stream(self._stream)
-        self._unpack()
         self._work = None

@@ -172,7 +172,10 @@ def run_ours(args):
     hs = inp["v"].contiguous()   # membrane in the (B, d_model, L) layout extract_base_events takes
     names = ["dt_idle", "dt_active", "A", "W_B", "W_C", "D"]
     params = {n: inp[n].clone().requires_grad_(True) for n in names}
-    bucket = dp.GradBucket([params[n] for n in names]) if world > 1 else None
+    # parameter gradients live in one bucket; its all-reduce is launched from
+    # autograd as soon as the scan backward has produced them, beside the rest
+    # of the backward
+    bucket = dp.GradBucket([params[n] for n in names], overlap=True) if world > 1 else None
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     def step(hs_, u_, dout_):
@@ -184,7 +187,6 @@ def run_ours(args):
         dense = itf.restore_dense_fn(y, ts, cu, cfg.D, cfg.L)
         dense.backward(dout_)
         if bucket is not None:
-            bucket.start()
             bucket.finish()
         return int(ch.numel()), int(cu.numel() - 1), mx
 
@@ -194,8 +196,11 @@ def run_ours(args):
     u_leaf = inp["u"].detach().clone().requires_grad_(True)
 
     def zero():
-        for p in params.values():
-            p.grad = None
+        if bucket is not None:
+            bucket.zero_grad()      # gradients are views into the all-reduce bucket
+        else:
+            for p in params.values():
+                p.grad = None
         u_leaf.grad = None
 
     E, NC, mx = step(hs, u_leaf, inp["dout"])

@@ -68,9 +68,19 @@ def _worker(rank, world, port, outdir, mode):
                 params[n].grad = torch.zeros_like(params[n])
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected rank failure before the collective")
-        bucket = dp.GradBucket([params[n] for n in names], average=False)
-        bucket.start().finish()
-        if mode == "ok":
+        if mode == "overlap":
+            # launched from autograd hooks; two steps re-arm through zero_grad
+            leaves = {n: params[n].detach().clone().requires_grad_(True) for n in names}
+            bucket = dp.GradBucket([leaves[n] for n in names], average=False, overlap=True)
+            for _ in range(2):
+                bucket.zero_grad()
+                sum((leaves[n] * torch.as_tensor(g[n])).sum() for n in names).backward()
+                bucket.finish()
+            params = leaves
+        else:
+            bucket = dp.GradBucket([params[n] for n in names], average=False)
+            bucket.start().finish()
+        if mode in ("ok", "overlap"):
             full = _oracle_grads(cfg, inp, 0, cfg.B)
             for n in names:
                 np.testing.assert_allclose(params[n].grad.numpy(), full[n], rtol=1e-9, atol=1e-9)
@@ -104,6 +114,11 @@ def test_sharded_grads_allreduce_equal_full_batch():
     assert res == ["ok", "ok"], res
 
 
+def test_allreduce_launched_from_autograd_hooks():
+    res = _run("overlap")
+    assert res == ["ok", "ok"], res
+
+
 def test_rank_failure_surfaces_on_host():
     res = _run("fail")
     assert res[1].startswith("error") and "injected" in res[1]
@@ -123,3 +138,23 @@ def test_shard_range_partitions():
             parts = [shard_range(n, r, w) for r in range(w)]
             assert parts[0][0] == 0 and parts[-1][1] == n
             assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
+
+
+def test_bucket_gradients_are_views_that_autograd_accumulates_into():
+    """Gradients live in the bucket: autograd adds into the views, zero_grad
+    clears them with one fill, and a .grad reset to None is re-bound."""
+    from bc_mamba_b200 import dp
+
+    a = torch.zeros(3, 4, dtype=torch.float32, requires_grad=True)
+    b = torch.zeros(5, dtype=torch.float32, requires_grad=True)
+    bucket = dp.GradBucket([a, b])
+    lo, hi = bucket.flat.data_ptr(), bucket.flat.data_ptr() + bucket.flat.numel() * 4
+    for step in range(2):
+        bucket.zero_grad()
+        ((a * 2.0).sum() + (b * 3.0).sum()).backward()
+        for p in (a, b):
+            assert lo <= p.grad.data_ptr() < hi
+        assert torch.all(a.grad == 2.0) and torch.all(b.grad == 3.0)
+    a.grad = None
+    bucket.zero_grad()
+    assert a.grad is not None and lo <= a.grad.data_ptr() < hi and float(bucket.flat.abs().sum()) == 0.0
