@@ -247,7 +247,12 @@ def run_ours(args):
     ms_per_step = float(t_max.item()) / args.steps
     value = world * E / (ms_per_step * 1e-3)
 
-    # ---- e2e: pinned host inputs in, parameter gradients out, every step
+    # ---- e2e: pinned host inputs in, parameter gradients out, every step.
+    # Step i+1's inputs are copied on a second stream into the other half of a
+    # double buffer while step i computes (the way a data loader feeds a
+    # training loop); the window runs from the first copy to the last
+    # gradient read-back and is divided by K.  Each step reads 167 MB of fresh
+    # inputs (larger than L2), so no flush is needed between steps.
     h_v = hs.cpu().pin_memory()
     h_u = inp["u"].cpu().pin_memory()
     h_dout = inp["dout"].cpu().pin_memory()
@@ -255,24 +260,42 @@ def run_ours(args):
     h2d = h_v.numel() * h_v.element_size() + h_u.numel() * h_u.element_size() + \
         h_dout.numel() * h_dout.element_size()
     d2h = sum(g.numel() * 4 for g in h_grads)
-    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    bufs = [(torch.empty_like(hs), torch.empty_like(inp["u"]), torch.empty_like(inp["dout"])) for _ in range(2)]
+    copy_stream = torch.cuda.Stream(device=dev)
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    comp = torch.cuda.current_stream(dev)
+
+    def h2d_into(b, wait_free):
+        with torch.cuda.stream(copy_stream):
+            if wait_free:
+                copy_stream.wait_event(free[b])
+            for d_t, h_t in zip(bufs[b], (h_v, h_u, h_dout)):
+                d_t.copy_(h_t, non_blocking=True)
+            ready[b].record(copy_stream)
+
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
+    e_start.record(comp)
+    copy_stream.wait_stream(comp)
+    h2d_into(0, False)
     for i in range(args.steps):
+        b = i % 2
+        if i + 1 < args.steps:
+            h2d_into(1 - b, i >= 1)          # the other half was last used by step i-1
+        comp.wait_event(ready[b])
         zero()
-        flush.zero_()
-        e_starts[i].record()
-        d_v = h_v.to(dev, non_blocking=True)
-        d_u = h_u.to(dev, non_blocking=True)
-        d_dout = h_dout.to(dev, non_blocking=True)
-        step(d_v, d_u, d_dout)
+        d_v, d_u, d_dout = bufs[b]
+        step(d_v, d_u.detach(), d_dout)      # a fresh x_conv leaf over the buffer
         for g, n in zip(h_grads, names):
             g.copy_(params[n].grad, non_blocking=True)
-        e_ends[i].record()
+        free[b].record(comp)
+    e_end.record(comp)
     torch.cuda.synchronize()
-    te = torch.tensor([sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends))], device=dev)
+    te = torch.tensor([e_start.elapsed_time(e_end)], device=dev)
     if world > 1:
         torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.barrier()
@@ -297,7 +320,8 @@ def run_ours(args):
                    "parallelism": f"dp{world} (batch-sharded, grad all-reduce)",
                    "l2": "256 MiB memset flush before every timed step, outside its timing window"},
         "e2e": {"value": world * E / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "copies": "pinned host -> device on a copy stream, step i+1's inputs overlapping step i"},
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak,
                      "traffic": NCU_TRAFFIC_C1.get(dominant) if args.config == "c1" and args.rho is None else None,
