@@ -23,6 +23,7 @@ ABI_SYMBOLS = (
     "bcm_extract_workspace_bytes",
     "bcm_extract_base_count",
     "bcm_extract_base_fill",
+    "bcm_extract_base_count_bld",
     "bcm_expand_base_events",
     "bcm_gather_events_fwd",
     "bcm_gather_bwd_workspace_bytes",

@@ -60,6 +60,53 @@ threshold_mask_kernel(const T* __restrict__ x, int64_t n_rows, int L, int n_word
     if (lane == 0) counts[row] = cnt;
 }
 
+// ---- pass 1, (B, L, d_model) input ----------------------------------------
+// The same mask and counts from the layout the model holds its spikes in
+// (rows of d_model features per position), so callers need no transposed
+// copy.  A warp owns one batch row b, 32 consecutive features (lane =
+// channel) and kBldWords mask words (32 positions each): per word it issues
+// the 32 row loads (each a coalesced row of 32 features) and packs the lane's
+// 32 comparisons into the channel's word.  Counts are per-warp partial sums
+// added with integer atomics (exact and order-independent).
+constexpr int kBldWords = 2;
+
+template <typename T>
+__global__ void __launch_bounds__(kCountWarps * 32)
+threshold_mask_bld_kernel(const T* __restrict__ x, int L, int Dm, int n_words, int n_dblk, int n_wparts,
+                          int64_t n_units, float thr, uint32_t* __restrict__ mask,
+                          int32_t* __restrict__ counts) {
+    const int64_t unit = (int64_t)blockIdx.x * kCountWarps + (threadIdx.x >> 5);
+    if (unit >= n_units) return;
+    const int lane = lane_id();
+    const int wpart = (int)(unit % n_wparts);
+    const int64_t rest = unit / n_wparts;
+    const int dblk = (int)(rest % n_dblk);
+    const int64_t b = rest / n_dblk;
+    const int d = dblk * 32 + lane;
+    const bool valid = d < Dm;
+    const T* col = x + b * L * (int64_t)Dm + d;
+    uint32_t* mrow = mask + (b * Dm + d) * (int64_t)n_words;
+    const int w_beg = wpart * kBldWords;
+    const int w_end = min(n_words, w_beg + kBldWords);
+    int cnt = 0;
+    for (int w = w_beg; w < w_end; ++w) {
+        float v[32];
+#pragma unroll
+        for (int r = 0; r < 32; ++r) {
+            const int t = w * 32 + r;
+            v[r] = (valid && t < L) ? to_f32<T>(col[(int64_t)t * Dm]) : -INFINITY;
+        }
+        uint32_t word = 0u;
+#pragma unroll
+        for (int r = 0; r < 32; ++r) word |= (v[r] > thr ? 1u : 0u) << r;   // NaN > thr is false
+        if (valid) {
+            mrow[w] = word;
+            cnt += __popc(word);
+        }
+    }
+    if (valid && cnt > 0) atomicAdd(&counts[b * Dm + d], cnt);
+}
+
 // ---- pass 2: exclusive scan of counts into cu_seqlens + max ----------------
 constexpr int kScanThreads = 1024;
 
@@ -314,6 +361,21 @@ inline int grid_for(int64_t n, int threads) {
 
 using namespace bcm;
 
+// counts -> cu_seqlens and max on the device, then the event total to the
+// host (the one synchronisation the reference API implies: outputs are sized
+// by it).
+static bcm_status scan_counts_and_sync(const int32_t* counts, int64_t n_base_channels, int32_t* cu_seqlens,
+                                       int32_t* max_seqlen, int64_t* n_events_host, cudaStream_t stream) {
+    counts_scan_kernel<<<1, kScanThreads, 0, stream>>>(counts, n_base_channels, cu_seqlens, max_seqlen);
+    BCM_LAUNCH_CHECK();
+    int32_t e_host = 0;
+    BCM_CUDA_TRY(cudaMemcpyAsync(&e_host, cu_seqlens + n_base_channels, sizeof(int32_t),
+                                 cudaMemcpyDeviceToHost, stream));
+    BCM_CUDA_TRY(cudaStreamSynchronize(stream));
+    *n_events_host = e_host;
+    return BCM_OK;
+}
+
 extern "C" size_t bcm_extract_workspace_bytes(int64_t n_base_channels, int64_t seqlen) {
     if (n_base_channels < 0 || seqlen < 0) return 0;
     const int64_t words = (seqlen + 31) / 32;
@@ -363,15 +425,54 @@ extern "C" bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype d
         });
         if (st != BCM_OK) return st;
     }
-    counts_scan_kernel<<<1, kScanThreads, 0, stream>>>(counts, n_base_channels, cu_seqlens,
-                                                       max_seqlen);
-    BCM_LAUNCH_CHECK();
-    int32_t e_host = 0;
-    BCM_CUDA_TRY(cudaMemcpyAsync(&e_host, cu_seqlens + n_base_channels, sizeof(int32_t),
-                                 cudaMemcpyDeviceToHost, stream));
-    BCM_CUDA_TRY(cudaStreamSynchronize(stream));
-    *n_events_host = e_host;
-    return BCM_OK;
+    return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, n_events_host, stream);
+}
+
+extern "C" bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtype dtype, int64_t batch,
+                                                 int64_t seqlen, int64_t d_model, float threshold,
+                                                 int32_t* counts, int32_t* cu_seqlens, int32_t* max_seqlen,
+                                                 void* workspace, size_t workspace_bytes,
+                                                 int64_t* n_events_host, cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(dtype_ok64(dtype), "extract_base_events_bld: unsupported dtype %d", (int)dtype);
+    BCM_REQUIRE(batch >= 0 && seqlen >= 0 && d_model >= 0, "extract_base_events_bld: negative size");
+    const int64_t n_base_channels = batch * d_model;
+    BCM_REQUIRE(seqlen < (1ll << 31) && n_base_channels * seqlen < (1ll << 31) * 64,
+                "extract_base_events_bld: sizes exceed int32 event indexing");
+    BCM_REQUIRE(cu_seqlens && max_seqlen && n_events_host, "extract_base_events_bld: null output");
+    const size_t need = bcm_extract_workspace_bytes(n_base_channels, seqlen);
+    if (workspace_bytes < need || (need > 0 && !workspace)) {
+        set_error("extract_base_events_bld: workspace of %zu bytes < required %zu", workspace_bytes, need);
+        return BCM_ERR_WORKSPACE;
+    }
+    BCM_CUDA_TRY(cudaMemsetAsync(max_seqlen, 0, sizeof(int32_t), stream));
+    if (n_base_channels == 0) {
+        BCM_CUDA_TRY(cudaMemsetAsync(cu_seqlens, 0, sizeof(int32_t), stream));
+        BCM_CUDA_TRY(cudaStreamSynchronize(stream));
+        *n_events_host = 0;
+        return BCM_OK;
+    }
+    BCM_REQUIRE(input_bld && counts, "extract_base_events_bld: null pointer");
+    BCM_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * n_base_channels, stream));
+    const int L = (int)seqlen;
+    if (L > 0) {
+        const int n_words = (L + 31) / 32;
+        const int n_dblk = (int)((d_model + 31) / 32);
+        const int n_wparts = (n_words + kBldWords - 1) / kBldWords;
+        const int64_t n_units = batch * n_dblk * n_wparts;
+        const int64_t grid = (n_units + kCountWarps - 1) / kCountWarps;
+        BCM_REQUIRE(grid < (1ll << 31), "extract_base_events_bld: too many rows");
+        bcm_status st = dispatch_dtype64(dtype, [&](auto tag) -> bcm_status {
+            using T = decltype(tag);
+            threshold_mask_bld_kernel<T><<<(unsigned)grid, kCountWarps * 32, 0, stream>>>(
+                static_cast<const T*>(input_bld), L, (int)d_model, n_words, n_dblk, n_wparts, n_units, threshold,
+                static_cast<uint32_t*>(workspace), counts);
+            BCM_LAUNCH_CHECK();
+            return BCM_OK;
+        });
+        if (st != BCM_OK) return st;
+    }
+    return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, n_events_host, stream);
 }
 
 extern "C" bcm_status bcm_extract_base_fill(int64_t n_base_channels, int64_t seqlen,

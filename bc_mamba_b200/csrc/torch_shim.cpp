@@ -54,26 +54,17 @@ Tensor workspace(int64_t bytes, const at::Device& dev) {
 }
 
 // ---------------------------------------------------------------- extract ----
-std::vector<Tensor> extract_base_events_fwd(Tensor base_input, double threshold) {
-    TORCH_CHECK(base_input.is_cuda(), "base_input must be CUDA");
-    TORCH_CHECK(base_input.is_contiguous(), "base_input must be contiguous");
-    TORCH_CHECK(base_input.dim() == 3, "base_input must be 3-D [B, d_model, L]");
-    const bcm_dtype dt = to_bcm(base_input.scalar_type(), "count_base_kernel");
-    c10::cuda::CUDAGuard guard(base_input.device());
-    const int64_t B = base_input.size(0), d_model = base_input.size(1), L = base_input.size(2);
-    const int64_t NCb = B * d_model;
-    const float thr = (float)threshold;
-    auto opt_i = torch::TensorOptions().dtype(torch::kInt32).device(base_input.device());
+// count pass (the given call) + fill, shared by both input layouts
+template <typename CountFn>
+std::vector<Tensor> extract_with(const Tensor& like, int64_t NCb, int64_t L, CountFn count, const char* what) {
+    c10::cuda::CUDAGuard guard(like.device());
+    auto opt_i = torch::TensorOptions().dtype(torch::kInt32).device(like.device());
     auto counts = torch::empty({NCb}, opt_i);
     auto cu = torch::empty({NCb + 1}, opt_i);
     auto mx = torch::empty({}, opt_i);
-    auto ws = workspace((int64_t)bcm_extract_workspace_bytes(NCb, L), base_input.device());
+    auto ws = workspace((int64_t)bcm_extract_workspace_bytes(NCb, L), like.device());
     int64_t E = 0;
-    check_status(bcm_extract_base_count(base_input.data_ptr(), dt, NCb, L, thr,
-                                        counts.data_ptr<int32_t>(), cu.data_ptr<int32_t>(),
-                                        mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), &E,
-                                        cur_stream()),
-                 "extract_base_events");
+    check_status(count(counts, cu, mx, ws, &E), what);
     if (E == 0) {
         auto ei = torch::zeros({0}, opt_i);
         auto ms = torch::zeros({1}, opt_i);
@@ -85,8 +76,43 @@ std::vector<Tensor> extract_base_events_fwd(Tensor base_input, double threshold)
     check_status(bcm_extract_base_fill(NCb, L, cu.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(),
                                        ch.data_ptr<int32_t>(), ts.data_ptr<int32_t>(),
                                        kf.data_ptr<int32_t>(), cur_stream()),
-                 "extract_base_events");
+                 what);
     return {ch, ts, kf, cu, counts, mx};
+}
+
+std::vector<Tensor> extract_base_events_fwd(Tensor base_input, double threshold) {
+    TORCH_CHECK(base_input.is_cuda(), "base_input must be CUDA");
+    TORCH_CHECK(base_input.is_contiguous(), "base_input must be contiguous");
+    TORCH_CHECK(base_input.dim() == 3, "base_input must be 3-D [B, d_model, L]");
+    const bcm_dtype dt = to_bcm(base_input.scalar_type(), "count_base_kernel");
+    const int64_t B = base_input.size(0), d_model = base_input.size(1), L = base_input.size(2);
+    const float thr = (float)threshold;
+    return extract_with(base_input, B * d_model, L,
+                        [&](Tensor& counts, Tensor& cu, Tensor& mx, Tensor& ws, int64_t* E) {
+                            return bcm_extract_base_count(base_input.data_ptr(), dt, B * d_model, L, thr,
+                                                          counts.data_ptr<int32_t>(), cu.data_ptr<int32_t>(),
+                                                          mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), E,
+                                                          cur_stream());
+                        },
+                        "extract_base_events");
+}
+
+// Same outputs from the (B, L, d_model) layout (no transposed copy).
+std::vector<Tensor> extract_base_events_bld_fwd(Tensor x, double threshold) {
+    TORCH_CHECK(x.is_cuda(), "x must be CUDA");
+    TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
+    TORCH_CHECK(x.dim() == 3, "x must be 3-D [B, L, d_model]");
+    const bcm_dtype dt = to_bcm(x.scalar_type(), "extract_base_events_bld");
+    const int64_t B = x.size(0), L = x.size(1), d_model = x.size(2);
+    const float thr = (float)threshold;
+    return extract_with(x, B * d_model, L,
+                        [&](Tensor& counts, Tensor& cu, Tensor& mx, Tensor& ws, int64_t* E) {
+                            return bcm_extract_base_count_bld(x.data_ptr(), dt, B, L, d_model, thr,
+                                                              counts.data_ptr<int32_t>(), cu.data_ptr<int32_t>(),
+                                                              mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), E,
+                                                              cur_stream());
+                        },
+                        "extract_base_events_bld");
 }
 
 std::vector<Tensor> expand_base_events_fwd(Tensor base_ch_ids, Tensor base_t_steps,
@@ -530,6 +556,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("extract_events", &extract_events_fwd, "bool mask -> (ch_ids, t_steps, k_flat, cu_seqlens, max_seqlen, head_flags)");
     m.def("extract_base_events", &extract_base_events_fwd,
           "float base_input + threshold -> (base_ch_ids, base_t_steps, base_k_flat, base_cu_seqlens, base_counts, base_max_seqlen)");
+    m.def("extract_base_events_bld", &extract_base_events_bld_fwd, py::arg("x"), py::arg("threshold"),
+          "extract_base_events from the (B, L, d_model) layout: same 6 outputs, no transposed copy");
     m.def("expand_base_events", &expand_base_events_fwd,
           "expand the base event stream by `expand` (repeat_interleave order)");
     m.def("gather_events_fwd", &gather_events_fwd, "gather x[B,D,L] at (channel_ids, time_steps)");

@@ -232,9 +232,10 @@ def extract_events_1d(hidden_states, x_conv, threshold: float, expand: int):
     """
     ops = load_ops()
     B, L, d_model = hidden_states.shape
-    base_input = hidden_states.transpose(1, 2).contiguous()
     with cuda_stage("routing_index_extraction"):
-        bch, bt, bk, bcu, _counts, _bmax = ops.extract_base_events(base_input, threshold)
+        # straight from the (B, L, d_model) layout: the reference first makes a
+        # transposed (B, d_model, L) copy (e_model.py:376)
+        bch, bt, bk, bcu, _counts, _bmax = ops.extract_base_events_bld(hidden_states.contiguous(), threshold)
     with cuda_stage("active_token_packing"):
         ch, ts, kf, cu, mx = ops.expand_base_events(bch, bt, bk, bcu, B, d_model, expand)
         max_seqlen = int(mx.item())

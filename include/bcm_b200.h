@@ -87,6 +87,20 @@ BCM_API bcm_status bcm_extract_base_fill(int64_t n_base_channels, int64_t seqlen
                                  int32_t* ch_ids, int32_t* t_steps,
                                  int32_t* k_flat, cudaStream_t stream);
 
+/* Count pass of the same extraction from the (B, L, d_model) layout the model
+ * keeps its spikes in, for base channel b*d_model + d: replaces the transposed
+ * copy Mamba.extract_events_1d makes before extract_base_events
+ * (reference spike_mamba/e_model.py:376).  Outputs, workspace and the
+ * synchronisation are those of bcm_extract_base_count; bcm_extract_base_fill
+ * completes it unchanged. */
+BCM_API bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtype dtype,
+                                  int64_t batch, int64_t seqlen, int64_t d_model,
+                                  float threshold,
+                                  int32_t* counts, int32_t* cu_seqlens,
+                                  int32_t* max_seqlen,
+                                  void* workspace, size_t workspace_bytes,
+                                  int64_t* n_events_host, cudaStream_t stream);
+
 /* ------------------------------------------------------------------------- *
  * Expansion of the base stream into `expand` logical replicas per channel
  * (repeat_interleave order: logical channel = base channel * expand + r).
