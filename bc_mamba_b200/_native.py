@@ -29,6 +29,9 @@ ABI_SYMBOLS = (
     "bcm_gather_bwd_workspace_bytes",
     "bcm_gather_events_bwd",
     "bcm_gather_events_bwd_noalloc",
+    "bcm_conv_events_fwd",
+    "bcm_conv_events_bwd_workspace_bytes",
+    "bcm_conv_events_bwd",
     "bcm_flat_ch_fwd_workspace_bytes",
     "bcm_flat_ch_bwd_workspace_bytes",
     "bcm_flat_ch_fwd",

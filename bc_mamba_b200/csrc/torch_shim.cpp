@@ -191,6 +191,67 @@ std::vector<Tensor> gather_events_bwd(Tensor grad_x, Tensor channel_ids, Tensor 
     return {dx};
 }
 
+// ------------------------------------------------------------- conv at events
+// weight [D, K] (or [D, 1, K]) and bias [D] are used as fp32.
+static Tensor conv_weight2d(const Tensor& w, int64_t D) {
+    TORCH_CHECK(w.is_cuda(), "conv_events: weight must be CUDA");
+    Tensor w2 = w.dim() == 3 ? w.reshape({w.size(0), w.size(2)}) : w;
+    TORCH_CHECK(w2.dim() == 2 && w2.size(0) == D, "conv_events: weight must be [D, K] or [D, 1, K]");
+    return w2.to(torch::kFloat32).contiguous();
+}
+
+std::vector<Tensor> conv_events_fwd(Tensor x, Tensor weight, const optional<Tensor>& bias,
+                                    Tensor channel_ids, Tensor time_steps) {
+    TORCH_CHECK(x.is_cuda() && x.dim() == 3, "conv_events_fwd: x must be a CUDA (B, D, L) tensor");
+    TORCH_CHECK(channel_ids.scalar_type() == torch::kInt32 && time_steps.scalar_type() == torch::kInt32,
+                "conv_events_fwd: channel_ids / time_steps must be int32");
+    c10::cuda::CUDAGuard guard(x.device());
+    auto xc = x.contiguous();
+    const int64_t B = xc.size(0), D = xc.size(1), L = xc.size(2);
+    auto w = conv_weight2d(weight, D);
+    Tensor bv;
+    if (bias.has_value() && bias->defined()) bv = bias->to(torch::kFloat32).contiguous();
+    auto ch = channel_ids.contiguous();
+    auto ts = time_steps.contiguous();
+    auto out = torch::empty({ch.size(0)}, xc.options());
+    check_status(bcm_conv_events_fwd(xc.data_ptr(), to_bcm(xc.scalar_type(), "conv_events_fwd"), B, D, L,
+                                     w.data_ptr<float>(), bv.defined() ? bv.data_ptr<float>() : nullptr,
+                                     w.size(1), ch.data_ptr<int32_t>(), ts.data_ptr<int32_t>(), ch.size(0),
+                                     out.data_ptr(), cur_stream()),
+                 "conv_events_fwd");
+    return {out};
+}
+
+std::vector<Tensor> conv_events_bwd(Tensor x, Tensor weight, const optional<Tensor>& bias,
+                                    Tensor time_steps, Tensor cu_seqlens, Tensor grad) {
+    TORCH_CHECK(x.is_cuda() && x.dim() == 3, "conv_events_bwd: x must be a CUDA (B, D, L) tensor");
+    TORCH_CHECK(time_steps.scalar_type() == torch::kInt32 && cu_seqlens.scalar_type() == torch::kInt32,
+                "conv_events_bwd: time_steps / cu_seqlens must be int32");
+    c10::cuda::CUDAGuard guard(x.device());
+    auto xc = x.contiguous();
+    const int64_t B = xc.size(0), D = xc.size(1), L = xc.size(2);
+    TORCH_CHECK(cu_seqlens.numel() == B * D + 1, "conv_events_bwd: cu_seqlens must have B*D+1 entries");
+    auto w = conv_weight2d(weight, D);
+    const int64_t K = w.size(1);
+    Tensor bv;
+    if (bias.has_value() && bias->defined()) bv = bias->to(torch::kFloat32).contiguous();
+    auto g = grad.to(xc.scalar_type()).contiguous();
+    auto ts = time_steps.contiguous();
+    auto cu = cu_seqlens.contiguous();
+    auto dx = torch::empty_like(xc);
+    auto fopt = xc.options().dtype(torch::kFloat32);
+    auto dw = torch::empty({D, K}, fopt);
+    auto db = torch::empty({D}, fopt);
+    Tensor ws = workspace((int64_t)bcm_conv_events_bwd_workspace_bytes(B * D, K), xc.device());
+    check_status(bcm_conv_events_bwd(xc.data_ptr(), to_bcm(xc.scalar_type(), "conv_events_bwd"), B, D, L,
+                                     w.data_ptr<float>(), bv.defined() ? bv.data_ptr<float>() : nullptr, K,
+                                     ts.data_ptr<int32_t>(), cu.data_ptr<int32_t>(), ts.size(0), g.data_ptr(),
+                                     dx.data_ptr(), dw.data_ptr<float>(), db.data_ptr<float>(), ws.data_ptr(),
+                                     ws.numel(), cur_stream()),
+                 "conv_events_bwd");
+    return {dx, dw, db};
+}
+
 // Legacy bool-mask extraction (extract_events_cuda.cu:117-179): the same event
 // stream as extract_base_events on mask > 0.5, plus head_flags.
 std::vector<Tensor> extract_events_fwd(Tensor mask) {
@@ -558,6 +619,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "float base_input + threshold -> (base_ch_ids, base_t_steps, base_k_flat, base_cu_seqlens, base_counts, base_max_seqlen)");
     m.def("extract_base_events_bld", &extract_base_events_bld_fwd, py::arg("x"), py::arg("threshold"),
           "extract_base_events from the (B, L, d_model) layout: same 6 outputs, no transposed copy");
+    m.def("conv_events_fwd", &conv_events_fwd, py::arg("x"), py::arg("weight"), py::arg("bias"),
+          py::arg("channel_ids"), py::arg("time_steps"),
+          "silu(causal depthwise conv1d(x)) evaluated at the events -> [u_flat]");
+    m.def("conv_events_bwd", &conv_events_bwd, py::arg("x"), py::arg("weight"), py::arg("bias"),
+          py::arg("time_steps"), py::arg("cu_seqlens"), py::arg("grad"),
+          "backward of conv_events_fwd -> [dx (B, D, L), dweight (D, K) fp32, dbias (D) fp32]");
     m.def("expand_base_events", &expand_base_events_fwd,
           "expand the base event stream by `expand` (repeat_interleave order)");
     m.def("gather_events_fwd", &gather_events_fwd, "gather x[B,D,L] at (channel_ids, time_steps)");

@@ -202,6 +202,38 @@ class GatherEventsFn(torch.autograd.Function):
         return dx.view(B, D, L), None, None
 
 
+class ConvEventsFn(torch.autograd.Function):
+    """silu(causal depthwise conv1d(x) + bias) evaluated only at the events:
+    replaces the dense ``x_conv = act(conv1d(x))[..., :L]`` of Mamba.forward
+    followed by ``GatherEventsFn`` (spike_mamba/e_model.py:442-451, 404-406),
+    whose result is read nowhere else.  ``weight`` is the conv1d weight
+    ([D, 1, K] or [D, K]); ``cu_seqlens`` must describe the stream (events of a
+    channel contiguous and time-ordered, as extraction produces them)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, channel_ids_i32, time_steps_i32, cu_seqlens):
+        with cuda_stage("active_gather_forward"):
+            u_flat = load_ops().conv_events_fwd(x, weight, bias, channel_ids_i32, time_steps_i32)[0]
+        ctx.save_for_backward(x, weight, bias if bias is not None else torch.empty(0), time_steps_i32,
+                              cu_seqlens)
+        ctx.has_bias = bias is not None
+        return u_flat
+
+    @staticmethod
+    def backward(ctx, grad_u):
+        x, weight, bias, time_steps_i32, cu_seqlens = ctx.saved_tensors
+        with cuda_stage("gather_scatter_backward"):
+            dx, dw, db = load_ops().conv_events_bwd(x, weight, bias if ctx.has_bias else None,
+                                                    time_steps_i32, cu_seqlens, grad_u.contiguous())
+        dw = dw.view(weight.shape).to(weight.dtype)
+        db = db.to(bias.dtype) if ctx.has_bias else None
+        return dx, dw, db, None, None, None
+
+
+def conv_events(x, weight, bias, channel_ids_i32, time_steps_i32, cu_seqlens):
+    return ConvEventsFn.apply(x, weight, bias, channel_ids_i32, time_steps_i32, cu_seqlens)
+
+
 def gather_events(x_conv, channel_ids_i32, time_steps_i32):
     return GatherEventsFn.apply(x_conv, channel_ids_i32, time_steps_i32)
 

@@ -173,6 +173,40 @@ BCM_API bcm_status bcm_gather_events_bwd_noalloc(const void* grad, bcm_dtype dty
                                  void* dx, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------- *
+ * Causal depthwise convolution + SiLU evaluated only at the events.
+ * Replaces the dense x_conv = silu(conv1d(x))[..., :L] of Mamba.forward
+ *   (reference spike_mamba/e_model.py:306-313, 442-451) followed by the
+ *   event gather of x_conv (e_model.py:167-193): nothing else reads x_conv.
+ * x[B, dim, L] in dtype; weight[dim, K] and bias[dim] (may be NULL) fp32;
+ * K <= 8.  Forward: out[e] = silu(bias[d] + sum_j weight[d,j] *
+ * x[b, d, t_e-K+1+j]) with zeros before position 0.  Backward writes all of
+ * dx[B, dim, L] (zeros where no event reaches), dweight[dim, K] and dbias[dim]
+ * (if not NULL); it needs the events sorted by time within each channel and
+ * cu_seqlens[B*dim+1] (the extraction order), and a workspace of
+ * bcm_conv_events_bwd_workspace_bytes(B*dim, K) bytes.
+ * ------------------------------------------------------------------------- */
+BCM_API bcm_status bcm_conv_events_fwd(const void* x, bcm_dtype dtype,
+                                 int64_t batch, int64_t dim, int64_t seqlen,
+                                 const float* weight, const float* bias,
+                                 int64_t kernel_size,
+                                 const int32_t* channel_ids,
+                                 const int32_t* time_steps, int64_t n_events,
+                                 void* out, cudaStream_t stream);
+
+BCM_API size_t bcm_conv_events_bwd_workspace_bytes(int64_t n_channels, int64_t kernel_size);
+
+BCM_API bcm_status bcm_conv_events_bwd(const void* x, bcm_dtype dtype,
+                                 int64_t batch, int64_t dim, int64_t seqlen,
+                                 const float* weight, const float* bias,
+                                 int64_t kernel_size,
+                                 const int32_t* time_steps,
+                                 const int32_t* cu_seqlens, int64_t n_events,
+                                 const void* grad, void* dx,
+                                 float* dweight, float* dbias,
+                                 void* workspace, size_t workspace_bytes,
+                                 cudaStream_t stream);
+
+/* ------------------------------------------------------------------------- *
  * Flat per-channel sparse selective scan with inter-spike decay.
  * Replaces selective_scan_cuda.fwd_flat_ch / bwd_flat_ch
  *   (reference csrc/selective_scan/selective_scan.cpp:674-884, 890-1153).
