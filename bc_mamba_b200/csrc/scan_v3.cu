@@ -519,6 +519,7 @@ __device__ void build_table_block(float* tab, const ScanArgs& a, int d) {
             v = decay_exact(event_delta(dti, dta, row), A2);
         }
         if (G >= 4) tab[((s >> 2) * kRows3 + row) * 4 + (s & 3)] = v;
+        else if (G == 2) tab[((s >> 1) * kRows3 + row) * 2 + (s & 1)] = v;
         else tab[s * kRows3 + row] = v;
     }
 }
@@ -527,6 +528,10 @@ template <int G>
 __device__ __forceinline__ void tab_row4(const float* tab, int row, int s0, float (&dec)[G]) {
     if constexpr (G >= 4) {
         tab_row3<G>(tab, row, s0 / G, dec);
+    } else if constexpr (G == 2) {
+        const float2 v = reinterpret_cast<const float2*>(tab)[(s0 >> 1) * kRows3 + row];
+        dec[0] = v.x;
+        dec[1] = v.y;
     } else {
 #pragma unroll
         for (int g = 0; g < G; ++g) dec[g] = tab[(s0 + g) * kRows3 + row];
@@ -572,9 +577,8 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
     float* wbase = sm4 + NP * kRows3 + warp * V::WARP_FLOATS;
     float* s_u = wbase;
     int* s_k = reinterpret_cast<int*>(s_u + kR3 * P);
-    float* s_w = reinterpret_cast<float*>(s_k + kR3 * P);
-    int* s_r = reinterpret_cast<int*>(s_w + kR3 * P);
-    float* s_eta = reinterpret_cast<float*>(s_r + kR3 * P);
+    float2* s_wr = reinterpret_cast<float2*>(s_k + kR3 * P);   // (w, table row as bits)
+    float* s_eta = reinterpret_cast<float*>(s_wr + kR3 * P);
     int* s_beg = reinterpret_cast<int*>(s_eta + kR3 * EP);
     int* s_n = s_beg + CPW;
     const int N = a.dstate;
@@ -634,8 +638,8 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
                 sd[c] += real ? dl : 0.f;
                 s_u[lane * P + c] = pu[c];
                 s_k[lane * P + c] = kk;
-                s_w[lane * P + c] = dl * pu[c] * pu[c];
-                s_r[lane * P + c] = (real && (unsigned)(kk - 1) < (unsigned)kKT3) ? kk : 0;
+                const int row = (real && (unsigned)(kk - 1) < (unsigned)kKT3) ? kk : 0;
+                s_wr[lane * P + c] = make_float2(dl * pu[c] * pu[c], __int_as_float(row));
             }
         }
         __syncwarp();
@@ -647,16 +651,17 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
         // ---- phase A: the state recurrence of the batch
         if (!exact) {
             float dec[G];
-            tab_row4<G>(tab, s_r[grp], s0, dec);
-            float w0 = s_w[grp];
-            int r1 = s_r[P + grp];
+            const float2 wr0 = s_wr[grp];
+            tab_row4<G>(tab, __float_as_int(wr0.y), s0, dec);
+            float w0 = wr0.x;
+            float2 wr1 = s_wr[P + grp];
 #pragma unroll 8
             for (int i = 0; i < kR3; ++i) {
-                const int i1 = min(i + 1, kR3 - 1), i2 = min(i + 2, kR3 - 1);
+                const int i2 = min(i + 2, kR3 - 1);
                 float dn[G];
-                tab_row4<G>(tab, r1, s0, dn);
-                const float w1 = s_w[i1 * P + grp];
-                r1 = s_r[i2 * P + grp];
+                tab_row4<G>(tab, __float_as_int(wr1.y), s0, dn);
+                const float w1 = wr1.x;
+                wr1 = s_wr[i2 * P + grp];
 #pragma unroll
                 for (int g = 0; g < G; ++g) eta[g] = fmaf(dec[g], eta[g], w0);
                 sts_vec<G>(erow + i * EP, eta);

@@ -97,3 +97,17 @@ def test_restore_errors():
         ops.restore_dense_fwd(torch.zeros(4, device=dev), ts, cu, 3, 10)
     with pytest.raises(RuntimeError, match="bf16 input only supports bf16 output"):
         ops.restore_dense_fwd(torch.zeros(4, device=dev, dtype=torch.bfloat16), ts, cu, 1, 10, torch.float32)
+
+
+@pytest.mark.parametrize("dim,L,rho,seed", [
+    (36, 5000, [1.0, 0.9, 0.0, 0.5], 4),          # search cap
+    (44, 301, [0.0, 1.0, 0.3, 0.02], 5),          # empty / dense channels, ragged L
+    (132, 4096, [0.001, 0.0005, 0.01, 0.0], 6),   # two feature blocks (one partial), long gaps
+    (4, 97, [0.5], 7),                            # a single 4-feature lane
+])
+def test_restore_more_shapes(dim, L, rho, seed):
+    """More feature counts (partial 32-feature blocks, two blocks, a single
+    feature group) through the same edge cases, fp32 and bf16."""
+    t, cu = _random_stream(NC=2 * dim, L=L, rho=rho, seed=seed)
+    _check(t, cu, dim, L)
+    _check(t, cu, dim, L, torch.bfloat16, None, seed=seed)
