@@ -128,7 +128,7 @@ bool dw_fast_supported(int dstate);
 int dw_fast_np(int dstate);
 bcm_status dw_fast_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t st);
 
-// Staged lane-group kernels (scan_v3.cu) for dstate <= 16 when the channels
+// Staged lane-group kernels (scan_v3.cu) for dstate <= 64 when the channels
 // of one feature fill whole warps; dw_fast_launch prefers them.
 bool v3_supported(const ScanArgs& a, bool bwd);
 bcm_status v3_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t st);

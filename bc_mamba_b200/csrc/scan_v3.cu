@@ -1,4 +1,4 @@
-// scan_v3.cu — staged depthwise scan kernels for dstate <= 16 (forward and
+// scan_v3.cu — staged depthwise scan kernels for dstate <= 64 (forward and
 // backward), used when the channels of one feature d fill whole warps.
 // Semantics are those of scan_fwd.cu / scan_bwd.cu (reference
 // selective_scan_fwd_kernel.cuh:403-728, selective_scan_bwd_kernel.cuh:
@@ -503,8 +503,11 @@ struct V4 {
     static constexpr int CPW = 32 / LPC;
     static constexpr int P = CPW + 1;
     static constexpr int EP = CPW * NP + 4;   // floats per event row of s_eta (== 4 mod 32)
-    static constexpr int WARP_FLOATS = 4 * kR3 * P + kR3 * EP + 2 * CPW;
+    // per-warp region, a multiple of 4 floats so every warp's float4 rows
+    // (s_eta, read as float4 in phase B) stay 16-byte aligned
+    static constexpr int WARP_FLOATS = (4 * kR3 * P + kR3 * EP + 2 * CPW + 3) / 4 * 4;
 };
+static_assert(V4<2, 64>::WARP_FLOATS % 4 == 0 && V4<1, 16>::WARP_FLOATS % 4 == 0, "warp regions");
 
 // Decay table of a CTA: [state][row] for G < 4 (scalar reads), float4
 // groups [state/4][row] (as build_table3) for G >= 4.
@@ -552,12 +555,13 @@ __device__ __forceinline__ void sts_vec(float* p, const float (&v)[G]) {
     }
 }
 
-// widest CTA of a layout (G >= 8 keeps more state per lane: smaller CTAs)
-template <int G>
-constexpr int v4_max_warps() { return G >= 8 ? 2 : 16; }
+// widest CTA of a layout (more state per lane, or a wider cc vector for
+// phase B, needs more registers: smaller CTAs)
+template <int G, int NP>
+constexpr int v4_max_warps() { return G >= 8 ? 2 : (NP >= 32 ? 8 : 16); }
 
 template <typename T, int G, int NP>
-__global__ void __launch_bounds__(32 * v4_max_warps<G>())
+__global__ void __launch_bounds__(32 * v4_max_warps<G, NP>())
 dw_fwd_v4(ScanArgs a, int blocks_per_d) {
     using V = V4<G, NP>;
     constexpr int CPW = V::CPW, P = V::P, LPC = V::LPC, EP = V::EP;
@@ -756,7 +760,7 @@ bcm_status launch_fwd_v4(const ScanArgs& a, cudaStream_t st) {
     const int bn = a.n_channels / a.dim;
     const int groups = bn / V::CPW;          // warps per feature
     int wpb = 1;
-    while (wpb * 2 <= v4_max_warps<G>() && groups % (wpb * 2) == 0) wpb *= 2;
+    while (wpb * 2 <= v4_max_warps<G, NP>() && groups % (wpb * 2) == 0) wpb *= 2;
     const int blocks_per_d = groups / wpb;
     const size_t smem = (size_t)(NP * kRows3 + wpb * V::WARP_FLOATS) * sizeof(float);
     if (smem > 48 * 1024) {
@@ -814,19 +818,21 @@ int fwd_g() {
     return g;
 }
 
+int padded_states(int N) { return N <= 8 ? 8 : N <= 16 ? 16 : N <= 32 ? 32 : 64; }
+
 int channels_per_warp(int N, bool bwd) {
-    const int NP = N <= 8 ? 8 : 16;
-    if (bwd) return N <= 8 ? 16 : 8;        // backward: 4 states per lane
-    return 32 * fwd_g() / NP;
+    const int NP = padded_states(N);
+    if (bwd) return NP <= 16 ? 128 / NP : 256 / NP;   // 4 states per lane (8 above 16 states)
+    return NP <= 16 ? 32 * fwd_g() / NP : 64 / NP;     // 2 states per lane above 16
 }
 
 }  // namespace
 
-// The staged kernels apply when dstate <= 16 and the channels of one feature
+// The staged kernels apply when dstate <= 64 and the channels of one feature
 // fill whole warps (n_channels / dim a multiple of the channels per warp).
 bool v3_supported(const ScanArgs& a, bool bwd) {
     static const int mode = env_int("BCM_SCAN_V3", 1);
-    if (mode == 0 || a.dstate > 16 || a.dim <= 0 || a.n_channels % a.dim != 0) return false;
+    if (mode == 0 || a.dstate > 64 || a.dim <= 0 || a.n_channels % a.dim != 0) return false;
     return (a.n_channels / a.dim) % channels_per_warp(a.dstate, bwd) == 0;
 }
 
@@ -834,7 +840,14 @@ bcm_status v3_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t 
     const int g = fwd_g();
     return dispatch_dtype(dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);
-        if (bwd) return a.dstate <= 8 ? launch_bwd_v3<T, 4, 2>(a, st) : launch_bwd_v3<T, 4, 4>(a, st);
+        if (bwd) {
+            if (a.dstate <= 8) return launch_bwd_v3<T, 4, 2>(a, st);
+            if (a.dstate <= 16) return launch_bwd_v3<T, 4, 4>(a, st);
+            if (a.dstate <= 32) return launch_bwd_v3<T, 8, 4>(a, st);
+            return launch_bwd_v3<T, 8, 8>(a, st);
+        }
+        if (a.dstate > 32) return launch_fwd_v4<T, 2, 64>(a, st);
+        if (a.dstate > 16) return launch_fwd_v4<T, 2, 32>(a, st);
         if (a.dstate <= 8) {
             if (g == 1) return launch_fwd_v4<T, 1, 8>(a, st);
             if (g == 4) return launch_fwd_v4<T, 4, 8>(a, st);

@@ -1,7 +1,7 @@
-"""GPU parity of the staged depthwise scan kernels (dstate <= 16 with the
+"""GPU parity of the staged depthwise scan kernels (dstate <= 64 with the
 channels of each feature filling whole warps: batch a multiple of 16), forward
 and backward against the float64 oracle, tolerance as test_gpu_scan.py.
-Covers every dstate the layouts pad (1..16), ragged and empty channels,
+Covers every dstate the layouts pad (1..64), ragged and empty channels,
 channels over one 2048-event chunk, gaps past the decay table (sparse
 spikes), 16-bit inputs, the silu gate and growing (A > 0) states."""
 import numpy as np
@@ -15,7 +15,7 @@ from bc_mamba_b200.workloads import CONFIGS
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("N", [1, 4, 7, 8, 9, 12, 16])
+@pytest.mark.parametrize("N", [1, 4, 7, 8, 9, 12, 16, 17, 24, 32, 33, 48, 64])
 def test_staged_dstates(N):
     c = CONFIGS["c0"].with_(B=16, D=8, N=N, L=300, rho=0.25, seed=40 + N)
     inp, ch, t, k, cu, mx, u = _events(c)
@@ -90,3 +90,11 @@ def test_staged_growing_states():
     A = A.copy()
     A[:, ::3] = 1e-4          # slowly growing states: prod(a) must keep every clamp
     _run_and_check(u, k, cu, mx, 30 * dti, 30 * dta, A, 0.3 * WB, 0.3 * WC, D=Dv)
+
+
+def test_staged_c3_shape_rows():
+    """The c3 layout (N = 64, bursty Markov spikes) on a short sequence."""
+    c = CONFIGS["c3"].with_(B=16, D=8, L=300)
+    inp, ch, t, k, cu, mx, u = _events(c)
+    p = lambda n: inp[n].numpy()
+    _run_and_check(u, k, cu, mx, p("dt_idle"), p("dt_active"), p("A"), p("W_B"), p("W_C"), D=p("D"))
