@@ -66,8 +66,41 @@ __device__ void build_table3(float* tab, const ScanArgs& a, int d, int lane) {
     __syncwarp();
 }
 
+// Checkpoint state of G states (G = 2: one 8-byte, G >= 4: G/4 16-byte moves).
+template <int G>
+__device__ __forceinline__ void ck_store(float* p, const float (&v)[G]) {
+    if constexpr (G == 2) {
+        *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < G / 4; ++j)
+            reinterpret_cast<float4*>(p)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+}
+
+template <int G>
+__device__ __forceinline__ void ck_load(const float* p, bool ok, float (&v)[G]) {
+    if constexpr (G == 2) {
+        const float2 t = ok ? *reinterpret_cast<const float2*>(p) : make_float2(0.f, 0.f);
+        v[0] = t.x; v[1] = t.y;
+    } else {
+#pragma unroll
+        for (int j = 0; j < G / 4; ++j) {
+            const float4 t = ok ? reinterpret_cast<const float4*>(p)[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+        }
+    }
+}
+
 template <int G>
 __device__ __forceinline__ void tab_row3(const float* tab, int row, int q, float (&dec)[G]) {
+    if constexpr (G == 2) {   // two states inside one float4 group of the table
+        const int s0 = 2 * q;
+        const float2 v = *reinterpret_cast<const float2*>(tab + (((s0 >> 2) * kRows3 + row) * 4 + (s0 & 3)));
+        dec[0] = v.x;
+        dec[1] = v.y;
+        return;
+    }
     const float4* t4 = reinterpret_cast<const float4*>(tab);
 #pragma unroll
     for (int j = 0; j < G / 4; ++j) {
@@ -284,12 +317,7 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
                 auto run = [&](auto exact_c) {
 #pragma unroll 1
                     for (int t = 0; t < kR3 / TB; ++t) {
-                        if (j0 + t * TB < len) {
-                            float4* p = reinterpret_cast<float4*>(ck + (int64_t)((j0 + t * TB) / TB) * NP);
-#pragma unroll
-                            for (int j = 0; j < G / 4; ++j)
-                                p[j] = make_float4(eta[4 * j], eta[4 * j + 1], eta[4 * j + 2], eta[4 * j + 3]);
-                        }
+                        if (j0 + t * TB < len) ck_store<G>(ck + (int64_t)((j0 + t * TB) / TB) * NP, eta);
 #pragma unroll
                         for (int ii = 0; ii < TB; ++ii) {
                             const int i = t * TB + ii;
@@ -345,13 +373,7 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
                 float eN[G];
                 {
                     const int jt = jb + (kR3 / TB - 1) * TB;
-                    const bool ok = jt < len;
-                    const float4* p = reinterpret_cast<const float4*>(ck + (int64_t)(jt / TB) * NP);
-#pragma unroll
-                    for (int j = 0; j < G / 4; ++j) {
-                        const float4 v = ok ? p[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-                        eN[4 * j] = v.x; eN[4 * j + 1] = v.y; eN[4 * j + 2] = v.z; eN[4 * j + 3] = v.w;
-                    }
+                    ck_load<G>(ck + (int64_t)(jt / TB) * NP, jt < len, eN);
                 }
                 auto run = [&](auto exact_c) {
 #pragma unroll 1
@@ -362,13 +384,7 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
                         for (int g = 0; g < G; ++g) et[g] = e0[g] = eN[g];
                         if (t > 0) {   // next (earlier) tile's checkpoint
                             const int jt = jb + i0 - TB;
-                            const bool ok = jt < len;
-                            const float4* p = reinterpret_cast<const float4*>(ck + (int64_t)(jt / TB) * NP);
-#pragma unroll
-                            for (int j = 0; j < G / 4; ++j) {
-                                const float4 v = ok ? p[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-                                eN[4 * j] = v.x; eN[4 * j + 1] = v.y; eN[4 * j + 2] = v.z; eN[4 * j + 3] = v.w;
-                            }
+                            ck_load<G>(ck + (int64_t)(jt / TB) * NP, jt < len, eN);
                         }
                         // forward recompute of the tile
                         float eti[TB][G], te[TB], tg[TB], ta[TB];
@@ -820,9 +836,15 @@ int fwd_g() {
 
 int padded_states(int N) { return N <= 8 ? 8 : N <= 16 ? 16 : N <= 32 ? 32 : 64; }
 
+// Backward states per lane up to 16 states (BCM_BWD_G = 2 overrides the default 4).
+int bwd_g() {
+    static const int g = env_int("BCM_BWD_G", 4) == 2 ? 2 : 4;
+    return g;
+}
+
 int channels_per_warp(int N, bool bwd) {
     const int NP = padded_states(N);
-    if (bwd) return NP <= 16 ? 128 / NP : 256 / NP;   // 4 states per lane (8 above 16 states)
+    if (bwd) return NP <= 16 ? 32 * bwd_g() / NP : 256 / NP;   // 8 states per lane above 16
     return NP <= 16 ? 32 * fwd_g() / NP : 64 / NP;     // 2 states per lane above 16
 }
 
@@ -841,8 +863,8 @@ bcm_status v3_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t 
     return dispatch_dtype(dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);
         if (bwd) {
-            if (a.dstate <= 8) return launch_bwd_v3<T, 4, 2>(a, st);
-            if (a.dstate <= 16) return launch_bwd_v3<T, 4, 4>(a, st);
+            if (a.dstate <= 8) return bwd_g() == 2 ? launch_bwd_v3<T, 2, 4>(a, st) : launch_bwd_v3<T, 4, 2>(a, st);
+            if (a.dstate <= 16) return bwd_g() == 2 ? launch_bwd_v3<T, 2, 8>(a, st) : launch_bwd_v3<T, 4, 4>(a, st);
             if (a.dstate <= 32) return launch_bwd_v3<T, 8, 4>(a, st);
             return launch_bwd_v3<T, 8, 8>(a, st);
         }
