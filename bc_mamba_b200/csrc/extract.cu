@@ -365,12 +365,15 @@ using namespace bcm;
 // host (the one synchronisation the reference API implies: outputs are sized
 // by it).
 static bcm_status scan_counts_and_sync(const int32_t* counts, int64_t n_base_channels, int32_t* cu_seqlens,
-                                       int32_t* max_seqlen, int64_t* n_events_host, cudaStream_t stream) {
+                                       int32_t* max_seqlen, int64_t* n_events_host, int32_t* max_host,
+                                       cudaStream_t stream) {
     counts_scan_kernel<<<1, kScanThreads, 0, stream>>>(counts, n_base_channels, cu_seqlens, max_seqlen);
     BCM_LAUNCH_CHECK();
     int32_t e_host = 0;
     BCM_CUDA_TRY(cudaMemcpyAsync(&e_host, cu_seqlens + n_base_channels, sizeof(int32_t),
                                  cudaMemcpyDeviceToHost, stream));
+    if (max_host)
+        BCM_CUDA_TRY(cudaMemcpyAsync(max_host, max_seqlen, sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
     BCM_CUDA_TRY(cudaStreamSynchronize(stream));
     *n_events_host = e_host;
     return BCM_OK;
@@ -387,7 +390,8 @@ extern "C" bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype d
                                              float threshold, int32_t* counts,
                                              int32_t* cu_seqlens, int32_t* max_seqlen,
                                              void* workspace, size_t workspace_bytes,
-                                             int64_t* n_events_host, cudaStream_t stream) {
+                                             int64_t* n_events_host, int32_t* max_seqlen_host,
+                                             cudaStream_t stream) {
     clear_error();
     BCM_REQUIRE(dtype_ok64(dtype), "extract_base_events: unsupported dtype %d", (int)dtype);
     BCM_REQUIRE(n_base_channels >= 0 && seqlen >= 0, "extract_base_events: negative size");
@@ -405,6 +409,7 @@ extern "C" bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype d
         BCM_CUDA_TRY(cudaMemsetAsync(cu_seqlens, 0, sizeof(int32_t), stream));
         BCM_CUDA_TRY(cudaStreamSynchronize(stream));
         *n_events_host = 0;
+        if (max_seqlen_host) *max_seqlen_host = 0;
         return BCM_OK;
     }
     BCM_REQUIRE(base_input && counts, "extract_base_events: null pointer");
@@ -425,14 +430,16 @@ extern "C" bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype d
         });
         if (st != BCM_OK) return st;
     }
-    return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, n_events_host, stream);
+    return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, n_events_host, max_seqlen_host,
+                                stream);
 }
 
 extern "C" bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtype dtype, int64_t batch,
                                                  int64_t seqlen, int64_t d_model, float threshold,
                                                  int32_t* counts, int32_t* cu_seqlens, int32_t* max_seqlen,
                                                  void* workspace, size_t workspace_bytes,
-                                                 int64_t* n_events_host, cudaStream_t stream) {
+                                                 int64_t* n_events_host, int32_t* max_seqlen_host,
+                                                 cudaStream_t stream) {
     clear_error();
     BCM_REQUIRE(dtype_ok64(dtype), "extract_base_events_bld: unsupported dtype %d", (int)dtype);
     BCM_REQUIRE(batch >= 0 && seqlen >= 0 && d_model >= 0, "extract_base_events_bld: negative size");
@@ -450,6 +457,7 @@ extern "C" bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtyp
         BCM_CUDA_TRY(cudaMemsetAsync(cu_seqlens, 0, sizeof(int32_t), stream));
         BCM_CUDA_TRY(cudaStreamSynchronize(stream));
         *n_events_host = 0;
+        if (max_seqlen_host) *max_seqlen_host = 0;
         return BCM_OK;
     }
     BCM_REQUIRE(input_bld && counts, "extract_base_events_bld: null pointer");
@@ -472,7 +480,8 @@ extern "C" bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtyp
         });
         if (st != BCM_OK) return st;
     }
-    return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, n_events_host, stream);
+    return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, n_events_host, max_seqlen_host,
+                                stream);
 }
 
 extern "C" bcm_status bcm_extract_base_fill(int64_t n_base_channels, int64_t seqlen,

@@ -16,6 +16,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <tuple>
 #include <vector>
 
 #include "bcm_b200.h"
@@ -54,9 +55,11 @@ Tensor workspace(int64_t bytes, const at::Device& dev) {
 }
 
 // ---------------------------------------------------------------- extract ----
-// count pass (the given call) + fill, shared by both input layouts
+// count pass (the given call) + fill, shared by both input layouts; the
+// count call also brings the maximum per-channel count to the host (max_host)
 template <typename CountFn>
-std::vector<Tensor> extract_with(const Tensor& like, int64_t NCb, int64_t L, CountFn count, const char* what) {
+std::vector<Tensor> extract_with(const Tensor& like, int64_t NCb, int64_t L, CountFn count, const char* what,
+                                 int32_t* max_host = nullptr) {
     c10::cuda::CUDAGuard guard(like.device());
     auto opt_i = torch::TensorOptions().dtype(torch::kInt32).device(like.device());
     auto counts = torch::empty({NCb}, opt_i);
@@ -64,7 +67,9 @@ std::vector<Tensor> extract_with(const Tensor& like, int64_t NCb, int64_t L, Cou
     auto mx = torch::empty({}, opt_i);
     auto ws = workspace((int64_t)bcm_extract_workspace_bytes(NCb, L), like.device());
     int64_t E = 0;
-    check_status(count(counts, cu, mx, ws, &E), what);
+    int32_t mh = 0;
+    check_status(count(counts, cu, mx, ws, &E, &mh), what);
+    if (max_host) *max_host = mh;
     if (E == 0) {
         auto ei = torch::zeros({0}, opt_i);
         auto ms = torch::zeros({1}, opt_i);
@@ -80,7 +85,7 @@ std::vector<Tensor> extract_with(const Tensor& like, int64_t NCb, int64_t L, Cou
     return {ch, ts, kf, cu, counts, mx};
 }
 
-std::vector<Tensor> extract_base_events_fwd(Tensor base_input, double threshold) {
+std::vector<Tensor> extract_base_events_impl(const Tensor& base_input, double threshold, int32_t* max_host) {
     TORCH_CHECK(base_input.is_cuda(), "base_input must be CUDA");
     TORCH_CHECK(base_input.is_contiguous(), "base_input must be contiguous");
     TORCH_CHECK(base_input.dim() == 3, "base_input must be 3-D [B, d_model, L]");
@@ -88,17 +93,21 @@ std::vector<Tensor> extract_base_events_fwd(Tensor base_input, double threshold)
     const int64_t B = base_input.size(0), d_model = base_input.size(1), L = base_input.size(2);
     const float thr = (float)threshold;
     return extract_with(base_input, B * d_model, L,
-                        [&](Tensor& counts, Tensor& cu, Tensor& mx, Tensor& ws, int64_t* E) {
+                        [&](Tensor& counts, Tensor& cu, Tensor& mx, Tensor& ws, int64_t* E, int32_t* mh) {
                             return bcm_extract_base_count(base_input.data_ptr(), dt, B * d_model, L, thr,
                                                           counts.data_ptr<int32_t>(), cu.data_ptr<int32_t>(),
                                                           mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), E,
-                                                          cur_stream());
+                                                          mh, cur_stream());
                         },
-                        "extract_base_events");
+                        "extract_base_events", max_host);
+}
+
+std::vector<Tensor> extract_base_events_fwd(Tensor base_input, double threshold) {
+    return extract_base_events_impl(base_input, threshold, nullptr);
 }
 
 // Same outputs from the (B, L, d_model) layout (no transposed copy).
-std::vector<Tensor> extract_base_events_bld_fwd(Tensor x, double threshold) {
+std::vector<Tensor> extract_base_events_bld_impl(const Tensor& x, double threshold, int32_t* max_host) {
     TORCH_CHECK(x.is_cuda(), "x must be CUDA");
     TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
     TORCH_CHECK(x.dim() == 3, "x must be 3-D [B, L, d_model]");
@@ -106,13 +115,28 @@ std::vector<Tensor> extract_base_events_bld_fwd(Tensor x, double threshold) {
     const int64_t B = x.size(0), L = x.size(1), d_model = x.size(2);
     const float thr = (float)threshold;
     return extract_with(x, B * d_model, L,
-                        [&](Tensor& counts, Tensor& cu, Tensor& mx, Tensor& ws, int64_t* E) {
+                        [&](Tensor& counts, Tensor& cu, Tensor& mx, Tensor& ws, int64_t* E, int32_t* mh) {
                             return bcm_extract_base_count_bld(x.data_ptr(), dt, B, L, d_model, thr,
                                                               counts.data_ptr<int32_t>(), cu.data_ptr<int32_t>(),
                                                               mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), E,
-                                                              cur_stream());
+                                                              mh, cur_stream());
                         },
-                        "extract_base_events_bld");
+                        "extract_base_events_bld", max_host);
+}
+
+std::vector<Tensor> extract_base_events_bld_fwd(Tensor x, double threshold) {
+    return extract_base_events_bld_impl(x, threshold, nullptr);
+}
+
+// The six outputs plus the maximum per-channel count as a host integer (read
+// in the same synchronisation as the event total, so a caller that needs
+// max_seqlen on the host makes no second synchronisation).
+std::tuple<std::vector<Tensor>, int64_t> extract_base_events_host_max(Tensor base_input, double threshold,
+                                                                       bool bld) {
+    int32_t mh = 0;
+    auto r = bld ? extract_base_events_bld_impl(base_input, threshold, &mh)
+                 : extract_base_events_impl(base_input, threshold, &mh);
+    return {r, (int64_t)mh};
 }
 
 std::vector<Tensor> expand_base_events_fwd(Tensor base_ch_ids, Tensor base_t_steps,
@@ -617,6 +641,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("extract_events", &extract_events_fwd, "bool mask -> (ch_ids, t_steps, k_flat, cu_seqlens, max_seqlen, head_flags)");
     m.def("extract_base_events", &extract_base_events_fwd,
           "float base_input + threshold -> (base_ch_ids, base_t_steps, base_k_flat, base_cu_seqlens, base_counts, base_max_seqlen)");
+    m.def("extract_base_events_host_max", &extract_base_events_host_max, py::arg("x"), py::arg("threshold"),
+          py::arg("bld") = false,
+          "extract_base_events (bld: from the (B, L, d_model) layout) -> (6 outputs, max count as a host int)");
     m.def("extract_base_events_bld", &extract_base_events_bld_fwd, py::arg("x"), py::arg("threshold"),
           "extract_base_events from the (B, L, d_model) layout: same 6 outputs, no transposed copy");
     m.def("conv_events_fwd", &conv_events_fwd, py::arg("x"), py::arg("weight"), py::arg("bias"),

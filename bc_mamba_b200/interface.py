@@ -248,12 +248,13 @@ def extract_events_base(base_input, x_conv, threshold: float, expand: int):
     ops = load_ops()
     B, d_model, L = base_input.shape
     with cuda_stage("routing_index_extraction"):
-        bch, bt, bk, bcu, _counts, _bmax = ops.extract_base_events(base_input, threshold)
+        # the maximum count arrives on the host with the event total (one
+        # synchronisation); expansion copies counts, so it is max_seqlen too
+        (bch, bt, bk, bcu, _counts, _bmax), max_seqlen = ops.extract_base_events_host_max(base_input, threshold)
     with cuda_stage("active_token_packing"):
-        ch, ts, kf, cu, mx = ops.expand_base_events(bch, bt, bk, bcu, B, d_model, expand)
-        max_seqlen = int(mx.item())
+        ch, ts, kf, cu, _mx = ops.expand_base_events(bch, bt, bk, bcu, B, d_model, expand)
     x_flat = gather_events(x_conv, ch, ts)
-    return ch, ts, kf, cu, max_seqlen, x_flat
+    return ch, ts, kf, cu, int(max_seqlen), x_flat
 
 
 def extract_events_1d(hidden_states, x_conv, threshold: float, expand: int):
@@ -265,11 +266,12 @@ def extract_events_1d(hidden_states, x_conv, threshold: float, expand: int):
     ops = load_ops()
     B, L, d_model = hidden_states.shape
     with cuda_stage("routing_index_extraction"):
-        # straight from the (B, L, d_model) layout: the reference first makes a
-        # transposed (B, d_model, L) copy (e_model.py:376)
-        bch, bt, bk, bcu, _counts, _bmax = ops.extract_base_events_bld(hidden_states.contiguous(), threshold)
+        # straight from the (B, L, d_model) layout (the reference first makes a
+        # transposed (B, d_model, L) copy, e_model.py:376); the maximum count
+        # comes back with the event total (one synchronisation, no .item())
+        (bch, bt, bk, bcu, _counts, _bmax), max_seqlen = ops.extract_base_events_host_max(
+            hidden_states.contiguous(), threshold, bld=True)
     with cuda_stage("active_token_packing"):
-        ch, ts, kf, cu, mx = ops.expand_base_events(bch, bt, bk, bcu, B, d_model, expand)
-        max_seqlen = int(mx.item())
+        ch, ts, kf, cu, _mx = ops.expand_base_events(bch, bt, bk, bcu, B, d_model, expand)
     x_flat = gather_events(x_conv, ch, ts)
-    return ch, ts, kf, cu, max_seqlen, x_flat
+    return ch, ts, kf, cu, int(max_seqlen), x_flat

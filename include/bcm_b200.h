@@ -67,7 +67,8 @@ BCM_API int bcm_abi_version(void);
  *   1. bcm_extract_base_count thresholds base_input[NCb, L] (strictly
  *      float(x) > threshold), writes counts[NCb], cu_seqlens[NCb+1],
  *      max_seqlen[1] (device, int32) and a bitmask into the workspace, then
- *      copies E_base to *n_events_host (this synchronises `stream`).
+ *      copies E_base to *n_events_host and, when max_seqlen_host is not
+ *      NULL, the maximum count to it (one synchronisation of `stream`).
  *   2. bcm_extract_base_fill writes ch_ids/t_steps/k_flat[E_base] from the
  *      workspace bitmask (k = t - t_prev, first event of a channel k = t + 1).
  * ------------------------------------------------------------------------- */
@@ -79,7 +80,8 @@ BCM_API bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype dtyp
                                   int32_t* counts, int32_t* cu_seqlens,
                                   int32_t* max_seqlen,
                                   void* workspace, size_t workspace_bytes,
-                                  int64_t* n_events_host, cudaStream_t stream);
+                                  int64_t* n_events_host, int32_t* max_seqlen_host,
+                                  cudaStream_t stream);
 
 BCM_API bcm_status bcm_extract_base_fill(int64_t n_base_channels, int64_t seqlen,
                                  const int32_t* cu_seqlens,
@@ -99,7 +101,8 @@ BCM_API bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtype d
                                   int32_t* counts, int32_t* cu_seqlens,
                                   int32_t* max_seqlen,
                                   void* workspace, size_t workspace_bytes,
-                                  int64_t* n_events_host, cudaStream_t stream);
+                                  int64_t* n_events_host, int32_t* max_seqlen_host,
+                                  cudaStream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Expansion of the base stream into `expand` logical replicas per channel

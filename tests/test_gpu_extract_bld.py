@@ -71,3 +71,19 @@ def test_extract_events_1d_matches_transposed_route():
         assert torch.equal(a, r), n
     assert mx == int(e[4])
     assert torch.equal(uf, ops.gather_events_fwd(xc, e[0], e[1])[0])
+
+
+@pytest.mark.parametrize("bld", [False, True])
+def test_host_max_matches_device_outputs(bld):
+    """extract_base_events_host_max: the same six outputs, and the maximum
+    count as a host integer equal to the device max (also for no events)."""
+    ops = load_ops()
+    g = torch.Generator().manual_seed(11)
+    for thr in (0.3, 1e9):
+        x = torch.randn(3, 200, 40, generator=g).to(dev)        # (B, L, d_model)
+        xin = x if bld else x.transpose(1, 2).contiguous()
+        outs, mh = ops.extract_base_events_host_max(xin, thr, bld=bld)
+        ref = ops.extract_base_events_bld(x, thr) if bld else ops.extract_base_events(xin, thr)
+        for a, r, n in zip(outs, ref, NAMES):
+            assert torch.equal(a, r), n
+        assert isinstance(mh, int) and mh == int(ref[5].max())
