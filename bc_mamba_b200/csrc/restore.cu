@@ -92,7 +92,7 @@ template <typename Tin, typename Tout>
 __global__ void __launch_bounds__(kWarpsR * 32)
 restore_fwd_kernel(const Tin* __restrict__ y, const int32_t* __restrict__ ts,
                    const int32_t* __restrict__ cu, int D, int L, int part_len,
-                   int n_dblk, Tout* __restrict__ out) {
+                   int n_dblk, Tout* __restrict__ out, uint32_t* __restrict__ bm) {
     __shared__ float s_val[kDB][kTT + 1];    // event values of the window, in order
     __shared__ uint32_t s_mask[kDB][kMP];
     __shared__ float s_carry[kDB];           // value held at the window start
@@ -176,6 +176,10 @@ restore_fwd_kernel(const Tin* __restrict__ y, const int32_t* __restrict__ ts,
             float cur = e > 0 ? s_val[c][e - 1] : s_carry[c];
             const int tw = t0 + warp * 32;
             Tout* col = out + ((int64_t)b * L + tw) * D + d0 + c;
+            // the event bitmap for the backward: parts are whole 128-row
+            // windows, so every word [b][tw/32][d] is written by one lane
+            if (bm != nullptr && cvalid && tw < wend)
+                bm[((int64_t)b * ((L + 31) >> 5) + (tw >> 5)) * D + d0 + c] = mw;
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 if ((mw >> i) & 1u) cur = s_val[c][e++];
@@ -345,6 +349,141 @@ restore_bwd_kernel(const T* __restrict__ dout, const int32_t* __restrict__ ts,
     if (warp == 0 && my_d < D && open >= 0) dy[open] = open_acc;
 }
 
+// ---- bitmap backward -------------------------------------------------------------
+// A pre-pass marks every addressable event (the first kCap of a channel, at a
+// position in [0, L)) in a bitmap [b][t/32][d]: one warp per channel, its
+// sorted times combined into 32-bit words with a segmented OR over the lanes
+// (a word cut by a 32-event batch is carried to the next), every word written
+// once with a plain store.  The backward then needs no event times: a warp
+// owns one batch row b, 32 features (lane = channel) and a range of
+// positions, and per 32-row window reads one coalesced mask word per lane and
+// the 32 rows (coalesced), closing a channel's interval sum at each set bit
+// (in row order: deterministic); it keeps reading past its range until the
+// intervals it owns have ended.
+constexpr int kBU = 4;   // units (warps) per CTA
+
+__global__ void event_bitmap_kernel(const int32_t* __restrict__ ts, const int32_t* __restrict__ cu,
+                                    int64_t n_ch, int D, int L, int nw, uint32_t* __restrict__ bm) {
+    const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (c >= n_ch) return;
+    const int lane = threadIdx.x & 31;
+    const int64_t b = c / D;
+    const int d = (int)(c % D);
+    const int beg = cu[c];
+    const int n = min(cu[c + 1] - beg, kCap);
+    uint32_t* col = bm + b * nw * (int64_t)D + d;          // word w at col[w * D]
+    int carry_w = -1;
+    uint32_t carry_bits = 0u;
+    constexpr int kPre = 16;                                  // batches whose loads are issued together
+    for (int g0 = 0; g0 < n; g0 += 32 * kPre) {
+    int tpre[kPre];
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) {
+        const int j = g0 + 32 * i + lane;
+        tpre[i] = (j < n) ? ts[beg + j] : -1;
+    }
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) {
+        const int j0 = g0 + 32 * i;
+        if (j0 >= n) break;
+        const int j = j0 + lane;
+        const int t = tpre[i];
+        const bool ok = j < n && t >= 0 && t < L;
+        const int w = ok ? (t >> 5) : -2 - lane;              // invalid lanes form their own segments
+        uint32_t bits = ok ? (1u << (t & 31)) : 0u;
+        if (lane == 0 && carry_w >= 0) {                      // the previous batch's last word
+            if (w == carry_w) bits |= carry_bits;             // continues here
+            else col[(int64_t)carry_w * D] = carry_bits;      // or is complete
+        }
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {              // inclusive segmented OR from the left
+            const uint32_t ob = __shfl_up_sync(kFull, bits, off);
+            const int owd = __shfl_up_sync(kFull, w, off);
+            if (lane >= off && owd == w) bits |= ob;
+        }
+        const int w_next = __shfl_down_sync(kFull, w, 1);
+        const bool last = (lane == 31);
+        if (ok && !last && w_next != w) col[(int64_t)w * D] = bits;
+        carry_w = __shfl_sync(kFull, w, 31);
+        carry_bits = __shfl_sync(kFull, bits, 31);
+        if (carry_w < 0) carry_bits = 0u;
+    }
+    }
+    if (lane == 0 && carry_w >= 0) col[(int64_t)carry_w * D] = carry_bits;
+}
+
+struct BUnit {
+    int64_t b;
+    int d0, t_beg, t_end;
+};
+
+__device__ __forceinline__ BUnit bunit(int64_t unit, int n_dblk, int n_parts, int part_len, int L) {
+    BUnit u;
+    const int part = (int)(unit % n_parts);
+    const int64_t rest = unit / n_parts;
+    u.d0 = (int)(rest % n_dblk) * 32;
+    u.b = rest / n_dblk;
+    u.t_beg = part * part_len;
+    u.t_end = min(L, u.t_beg + part_len);
+    return u;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kBU * 32)
+restore_bwd_bitmap(const T* __restrict__ dout, const int32_t* __restrict__ cu,
+                   const uint32_t* __restrict__ bm, int D, int L, int nw, int part_len, int n_dblk, int n_parts,
+                   int64_t n_units, float* __restrict__ dy) {
+    const int64_t unit = (int64_t)blockIdx.x * kBU + (threadIdx.x >> 5);
+    if (unit >= n_units) return;
+    const int lane = threadIdx.x & 31;
+    const BUnit u = bunit(unit, n_dblk, n_parts, part_len, L);
+    const int d = u.d0 + lane;
+    const bool valid = d < D;
+    int beg = 0, n = 0, n_all = 0;
+    if (valid) {
+        const int64_t c = u.b * D + d;
+        beg = cu[c];
+        n_all = cu[c + 1] - beg;
+        n = min(n_all, kCap);
+    }
+    const uint32_t* mcol = bm + u.b * nw * (int64_t)D + d;
+    // index of the first event at or after t_beg: the marked events before it
+    // (times lie in [0, L), so the bitmap holds exactly the first n events)
+    int p = 0;
+    if (valid) {
+#pragma unroll 8
+        for (int w = 0; w < (u.t_beg >> 5); ++w) p += __popc(mcol[(int64_t)w * D]);
+    }
+    if (u.t_beg == 0)
+        for (int j = kCap; j < n_all; ++j) dy[beg + j] = 0.f;      // past the search cap
+    int e = beg + p;        // next event (global index)
+    int open = -1;          // owned event whose interval is running
+    float acc = 0.f;
+    const T* col = dout + (u.b * L) * D + d;
+    for (int t0 = u.t_beg; t0 < L; t0 += 64) {
+        if (t0 >= u.t_end && !__any_sync(kFull, open >= 0)) break;
+        const uint32_t m0 = valid ? mcol[(int64_t)(t0 >> 5) * D] : 0u;
+        const uint32_t m1 = (valid && t0 + 32 < L) ? mcol[(int64_t)((t0 >> 5) + 1) * D] : 0u;
+        float v[64];
+#pragma unroll
+        for (int r = 0; r < 64; ++r) {
+            const int t = t0 + r;
+            v[r] = (valid && t < L) ? to_f32<T>(col[(int64_t)t * D]) : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < 64; ++r) {
+            if (((r < 32 ? m0 : m1) >> (r & 31)) & 1u) {   // an event starts here: the running interval ends
+                if (open >= 0) dy[open] = acc;
+                open = (t0 + r < u.t_end) ? e : -1;
+                ++e;
+                acc = 0.f;
+            }
+            acc += v[r];
+        }
+    }
+    if (open >= 0) dy[open] = acc;              // the interval runs to L
+}
+
 }  // namespace
 }  // namespace bcm
 
@@ -359,12 +498,10 @@ static int restore_part_len(int64_t n_blocks_2d, int64_t L) {
     return (int)std::min<int64_t>(len, std::max<int64_t>((L + kTT - 1) / kTT * kTT, kTT));
 }
 
-extern "C" bcm_status bcm_restore_dense_fwd(const void* y_flat, bcm_dtype y_dtype,
-                                            const int32_t* time_steps, const int32_t* cu_seqlens,
-                                            int64_t n_events, int64_t n_channels, int64_t dim,
-                                            int64_t seqlen, void* out, bcm_dtype out_dtype,
-                                            cudaStream_t stream) {
-    clear_error();
+static bcm_status restore_fwd_impl(const void* y_flat, bcm_dtype y_dtype, const int32_t* time_steps,
+                                   const int32_t* cu_seqlens, int64_t n_events, int64_t n_channels,
+                                   int64_t dim, int64_t seqlen, void* out, bcm_dtype out_dtype,
+                                   uint32_t* bitmap, cudaStream_t stream) {
     BCM_REQUIRE(dtype_ok(y_dtype) && dtype_ok(out_dtype), "restore_dense_fwd: unsupported dtype");
     BCM_REQUIRE(y_dtype == BCM_F32 || y_dtype == out_dtype,
                 "restore_dense_fwd: 16-bit input only supports the same output dtype");
@@ -385,7 +522,7 @@ extern "C" bcm_status bcm_restore_dense_fwd(const void* y_flat, bcm_dtype y_dtyp
         using Tout = decltype(tout);
         restore_fwd_kernel<Tin, Tout><<<grid, kWarpsR * 32, 0, stream>>>(
             static_cast<const Tin*>(y_flat), time_steps, cu_seqlens, (int)dim, (int)seqlen,
-            part_len, n_dblk, static_cast<Tout*>(out));
+            part_len, n_dblk, static_cast<Tout*>(out), bitmap);
         BCM_LAUNCH_CHECK();
         return BCM_OK;
     };
@@ -398,10 +535,85 @@ extern "C" bcm_status bcm_restore_dense_fwd(const void* y_flat, bcm_dtype y_dtyp
     return launch(__nv_bfloat16{}, __nv_bfloat16{});
 }
 
+extern "C" bcm_status bcm_restore_dense_fwd(const void* y_flat, bcm_dtype y_dtype,
+                                            const int32_t* time_steps, const int32_t* cu_seqlens,
+                                            int64_t n_events, int64_t n_channels, int64_t dim,
+                                            int64_t seqlen, void* out, bcm_dtype out_dtype,
+                                            cudaStream_t stream) {
+    clear_error();
+    return restore_fwd_impl(y_flat, y_dtype, time_steps, cu_seqlens, n_events, n_channels, dim, seqlen,
+                            out, out_dtype, nullptr, stream);
+}
+
+extern "C" bcm_status bcm_restore_dense_fwd_bitmap(const void* y_flat, bcm_dtype y_dtype,
+                                                   const int32_t* time_steps, const int32_t* cu_seqlens,
+                                                   int64_t n_events, int64_t n_channels, int64_t dim,
+                                                   int64_t seqlen, void* out, bcm_dtype out_dtype,
+                                                   uint32_t* event_bitmap, cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(event_bitmap, "restore_dense_fwd_bitmap: null event_bitmap");
+    return restore_fwd_impl(y_flat, y_dtype, time_steps, cu_seqlens, n_events, n_channels, dim, seqlen,
+                            out, out_dtype, event_bitmap, stream);
+}
+
+extern "C" size_t bcm_restore_bitmap_bytes(int64_t n_channels, int64_t seqlen) {
+    if (n_channels < 0 || seqlen < 0) return 0;
+    return (size_t)n_channels * (size_t)((seqlen + 31) / 32) * sizeof(uint32_t);
+}
+
+extern "C" size_t bcm_restore_workspace_bytes(int64_t n_channels, int64_t seqlen) {
+    return align_up(bcm_restore_bitmap_bytes(n_channels, seqlen), 256);
+}
+
+// Bitmap backward layout: warp units of 32 features x part_len positions,
+// enough to cover the SMs ~16 times; parts are whole 32-row windows.
+static void bitmap_layout(int64_t B, int64_t D, int64_t L, int& n_dblk, int& part_len, int& n_parts) {
+    n_dblk = (int)((D + 31) / 32);
+    const int64_t cols = B * n_dblk;
+    const int64_t target = (int64_t)sm_count() * 16;
+    const int64_t parts = std::max<int64_t>(1, (target + cols - 1) / cols);
+    int64_t len = (L + parts - 1) / parts;
+    len = std::max<int64_t>(64, (len + 31) / 32 * 32);
+    part_len = (int)len;
+    n_parts = (int)((L + len - 1) / len);
+}
+
+static bcm_status launch_bwd_bitmap(const void* dout, bcm_dtype dtype, const int32_t* cu_seqlens, int64_t B, int64_t dim, int64_t seqlen,
+                                    const uint32_t* bm, float* dy, cudaStream_t stream) {
+    int bd = 0, bpl = 0, bnp = 0;
+    bitmap_layout(B, dim, seqlen, bd, bpl, bnp);
+    const int64_t bunits = B * bd * bnp;
+    return dispatch_dtype(dtype, [&](auto tag) -> bcm_status {
+        using T = decltype(tag);
+        restore_bwd_bitmap<T><<<(unsigned)((bunits + kBU - 1) / kBU), kBU * 32, 0, stream>>>(
+            static_cast<const T*>(dout), cu_seqlens, bm, (int)dim, (int)seqlen,
+            (int)((seqlen + 31) / 32), bpl, bd, bnp, bunits, dy);
+        BCM_LAUNCH_CHECK();
+        return BCM_OK;
+    });
+}
+
+extern "C" bcm_status bcm_restore_dense_bwd_bitmap(const void* dout, bcm_dtype dtype,
+                                                   const int32_t* time_steps, const int32_t* cu_seqlens,
+                                                   int64_t n_events, int64_t n_channels, int64_t dim,
+                                                   int64_t seqlen, const uint32_t* event_bitmap, float* dy,
+                                                   cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(dtype_ok(dtype), "restore_dense_bwd_bitmap: unsupported dtype");
+    BCM_REQUIRE(dim >= 1 && seqlen >= 1 && n_channels >= 0 && n_events >= 0,
+                "restore_dense_bwd_bitmap: bad sizes");
+    BCM_REQUIRE(n_channels % dim == 0, "restore_dense_bwd_bitmap: n_channels must be divisible by dim");
+    BCM_REQUIRE(seqlen < (1ll << 31) - 2 * kTT, "restore_dense_bwd_bitmap: seqlen too large");
+    if (n_events == 0 || n_channels == 0) return BCM_OK;
+    BCM_REQUIRE(dout && time_steps && cu_seqlens && dy && event_bitmap, "restore_dense_bwd_bitmap: null pointer");
+    return launch_bwd_bitmap(dout, dtype, cu_seqlens, n_channels / dim, dim, seqlen, event_bitmap, dy, stream);
+}
+
 extern "C" bcm_status bcm_restore_dense_bwd(const void* dout, bcm_dtype dtype,
                                             const int32_t* time_steps, const int32_t* cu_seqlens,
                                             int64_t n_events, int64_t n_channels, int64_t dim,
-                                            int64_t seqlen, float* dy, cudaStream_t stream) {
+                                            int64_t seqlen, float* dy, void* workspace,
+                                            size_t workspace_bytes, cudaStream_t stream) {
     clear_error();
     BCM_REQUIRE(dtype_ok(dtype), "restore_dense_bwd: unsupported dtype");
     BCM_REQUIRE(dim >= 1 && seqlen >= 1 && n_channels >= 0 && n_events >= 0,
@@ -416,6 +628,17 @@ extern "C" bcm_status bcm_restore_dense_bwd(const void* dout, bcm_dtype dtype,
     const int part_len = restore_part_len(B * n_dblk, seqlen);
     const int n_parts = ceil_div(seqlen, part_len);
     dim3 grid(n_dblk * n_parts, (unsigned)B);
+    const bool use_bitmap = workspace && workspace_bytes >= bcm_restore_workspace_bytes(n_channels, seqlen);
+    if (use_bitmap) {
+        const int nw = (int)((seqlen + 31) / 32);
+        BCM_CUDA_TRY(cudaMemsetAsync(workspace, 0, (size_t)n_channels * nw * sizeof(uint32_t), stream));
+        event_bitmap_kernel<<<(unsigned)((n_channels + 7) / 8), 256, 0, stream>>>(
+            time_steps, cu_seqlens, n_channels, (int)dim, (int)seqlen, nw, static_cast<uint32_t*>(workspace));
+        BCM_LAUNCH_CHECK();
+    }
+    if (use_bitmap)
+        return launch_bwd_bitmap(dout, dtype, cu_seqlens, B, dim, seqlen,
+                                 static_cast<const uint32_t*>(workspace), dy, stream);
     return dispatch_dtype(dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);
         restore_bwd_kernel<T><<<grid, kWarpsR * 32, 0, stream>>>(

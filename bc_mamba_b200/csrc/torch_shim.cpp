@@ -544,8 +544,10 @@ std::vector<Tensor> dense_scan_unavailable(py::args, py::kwargs) {
 }
 
 // ---------------------------------------------------------------- restore ----
-Tensor restore_dense_fwd(const Tensor& y_flat, const Tensor& time_steps, const Tensor& cu_seqlens,
-                         int64_t dim, int64_t seqlen, const optional<at::ScalarType> out_dtype_opt) {
+// bitmap != nullptr: also returns the event bitmap (int32 [B, ceil(L/32), dim]) for restore_dense_bwd_bitmap
+Tensor restore_fwd_impl(const Tensor& y_flat, const Tensor& time_steps, const Tensor& cu_seqlens,
+                        int64_t dim, int64_t seqlen, const optional<at::ScalarType> out_dtype_opt,
+                        Tensor* bitmap) {
     auto input_type = y_flat.scalar_type();
     TORCH_CHECK(input_type == at::ScalarType::Float || input_type == at::ScalarType::Half ||
                     input_type == at::ScalarType::BFloat16,
@@ -578,6 +580,17 @@ Tensor restore_dense_fwd(const Tensor& y_flat, const Tensor& time_steps, const T
     c10::cuda::CUDAGuard guard(y_flat.device());
     const int64_t B = NC / dim;
     auto out = torch::empty({B, seqlen, dim}, y_flat.options().dtype(out_type));
+    if (bitmap != nullptr) {
+        *bitmap = torch::empty({B, (seqlen + 31) / 32, dim}, y_flat.options().dtype(at::ScalarType::Int));
+        check_status(bcm_restore_dense_fwd_bitmap(y_flat.data_ptr(), to_bcm(input_type, "restore_dense_fwd"),
+                                                  time_steps.data_ptr<int32_t>(), cu_seqlens.data_ptr<int32_t>(),
+                                                  E, NC, dim, seqlen, out.data_ptr(),
+                                                  to_bcm(out_type, "restore_dense_fwd"),
+                                                  reinterpret_cast<uint32_t*>(bitmap->data_ptr<int32_t>()),
+                                                  cur_stream()),
+                     "restore_dense_fwd_bitmap");
+        return out;
+    }
     check_status(bcm_restore_dense_fwd(y_flat.data_ptr(), to_bcm(input_type, "restore_dense_fwd"),
                                        time_steps.data_ptr<int32_t>(), cu_seqlens.data_ptr<int32_t>(),
                                        E, NC, dim, seqlen, out.data_ptr(),
@@ -586,8 +599,21 @@ Tensor restore_dense_fwd(const Tensor& y_flat, const Tensor& time_steps, const T
     return out;
 }
 
+Tensor restore_dense_fwd(const Tensor& y_flat, const Tensor& time_steps, const Tensor& cu_seqlens,
+                         int64_t dim, int64_t seqlen, const optional<at::ScalarType> out_dtype_opt) {
+    return restore_fwd_impl(y_flat, time_steps, cu_seqlens, dim, seqlen, out_dtype_opt, nullptr);
+}
+
+std::vector<Tensor> restore_dense_fwd_bitmap(const Tensor& y_flat, const Tensor& time_steps,
+                                             const Tensor& cu_seqlens, int64_t dim, int64_t seqlen,
+                                             const optional<at::ScalarType> out_dtype_opt) {
+    Tensor bitmap;
+    Tensor out = restore_fwd_impl(y_flat, time_steps, cu_seqlens, dim, seqlen, out_dtype_opt, &bitmap);
+    return {out, bitmap};
+}
+
 Tensor restore_dense_bwd(const Tensor& dout, const Tensor& time_steps, const Tensor& cu_seqlens,
-                         int64_t dim, int64_t seqlen) {
+                         int64_t dim, int64_t seqlen, bool bitmap) {
     auto input_type = dout.scalar_type();
     TORCH_CHECK(input_type == at::ScalarType::Float || input_type == at::ScalarType::Half ||
                     input_type == at::ScalarType::BFloat16,
@@ -609,10 +635,46 @@ Tensor restore_dense_bwd(const Tensor& dout, const Tensor& time_steps, const Ten
     c10::cuda::CUDAGuard guard(dout.device());
     auto dy = torch::empty({E}, dout.options().dtype(at::ScalarType::Float));
     if (E == 0) return dy;
+    Tensor ws = workspace(bitmap ? (int64_t)bcm_restore_workspace_bytes(NC, seqlen) : 0, dout.device());
     check_status(bcm_restore_dense_bwd(dout.data_ptr(), to_bcm(input_type, "restore_dense_bwd"),
                                        time_steps.data_ptr<int32_t>(), cu_seqlens.data_ptr<int32_t>(),
-                                       E, NC, dim, seqlen, dy.data_ptr<float>(), cur_stream()),
+                                       E, NC, dim, seqlen, dy.data_ptr<float>(),
+                                       bitmap ? ws.data_ptr() : nullptr, bitmap ? (size_t)ws.numel() : 0,
+                                       cur_stream()),
                  "restore_dense_bwd");
+    return dy;
+}
+
+Tensor restore_dense_bwd_bitmap(const Tensor& dout, const Tensor& time_steps, const Tensor& cu_seqlens,
+                                const Tensor& bitmap, int64_t dim, int64_t seqlen) {
+    auto input_type = dout.scalar_type();
+    TORCH_CHECK(input_type == at::ScalarType::Float || input_type == at::ScalarType::Half ||
+                    input_type == at::ScalarType::BFloat16,
+                "restore_dense_bwd_bitmap: dout must be fp32/fp16/bf16");
+    TORCH_CHECK(time_steps.scalar_type() == at::ScalarType::Int && cu_seqlens.scalar_type() == at::ScalarType::Int &&
+                    bitmap.scalar_type() == at::ScalarType::Int,
+                "restore_dense_bwd_bitmap: time_steps, cu_seqlens and bitmap must be int32");
+    TORCH_CHECK(dout.is_cuda() && time_steps.is_cuda() && cu_seqlens.is_cuda() && bitmap.is_cuda(),
+                "restore_dense_bwd_bitmap: all tensors must be on CUDA");
+    TORCH_CHECK(dout.is_contiguous() && cu_seqlens.is_contiguous() && bitmap.is_contiguous(),
+                "restore_dense_bwd_bitmap: all tensors must be contiguous");
+    TORCH_CHECK(dim >= 1 && seqlen >= 1, "restore_dense_bwd_bitmap: dim and seqlen must be >= 1");
+    const int64_t NC = cu_seqlens.size(0) - 1;
+    const int64_t E = time_steps.size(0);
+    TORCH_CHECK(dout.dim() == 3 && dout.size(1) == seqlen && dout.size(2) == dim && dout.size(0) * dim == NC,
+                "restore_dense_bwd_bitmap: dout must be (B, seqlen, dim) with B*dim = n_channels");
+    TORCH_CHECK(bitmap.dim() == 3 && bitmap.size(0) == dout.size(0) && bitmap.size(1) == (seqlen + 31) / 32 &&
+                    bitmap.size(2) == dim,
+                "restore_dense_bwd_bitmap: bitmap must be (B, ceil(seqlen/32), dim), from restore_dense_fwd_bitmap");
+    c10::cuda::CUDAGuard guard(dout.device());
+    auto dy = torch::empty({E}, dout.options().dtype(at::ScalarType::Float));
+    if (E == 0) return dy;
+    check_status(bcm_restore_dense_bwd_bitmap(dout.data_ptr(), to_bcm(input_type, "restore_dense_bwd_bitmap"),
+                                              time_steps.data_ptr<int32_t>(), cu_seqlens.data_ptr<int32_t>(),
+                                              E, NC, dim, seqlen,
+                                              reinterpret_cast<const uint32_t*>(bitmap.data_ptr<int32_t>()),
+                                              dy.data_ptr<float>(), cur_stream()),
+                 "restore_dense_bwd_bitmap");
     return dy;
 }
 
@@ -660,7 +722,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("restore_dense_fwd", &restore_dense_fwd, py::arg("y_flat"), py::arg("time_steps"),
           py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"), py::arg("out_dtype") = py::none(),
           "Zero-order-hold restore (B, L, D) from flat events");
+    m.def("restore_dense_fwd_bitmap", &restore_dense_fwd_bitmap, py::arg("y_flat"), py::arg("time_steps"),
+          py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"), py::arg("out_dtype") = py::none(),
+          "restore_dense_fwd that also returns the event bitmap (int32 [B, ceil(L/32), dim]) "
+          "consumed by restore_dense_bwd_bitmap");
+    m.def("restore_dense_bwd_bitmap", &restore_dense_bwd_bitmap, py::arg("dout"), py::arg("time_steps"),
+          py::arg("cu_seqlens"), py::arg("bitmap"), py::arg("dim"), py::arg("seqlen"),
+          "Backward of restore_dense_fwd from the forward's event bitmap; returns dy_flat (float32)");
     m.def("restore_dense_bwd", &restore_dense_bwd, py::arg("dout"), py::arg("time_steps"),
-          py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"),
-          "Backward of restore_dense_fwd; returns dy_flat (float32)");
+          py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"), py::arg("bitmap") = true,
+          "Backward of restore_dense_fwd; returns dy_flat (float32).  bitmap=False runs the "
+          "windowed kernel (no workspace) instead of the event-bitmap one (same result up to fp32 rounding)");
 }

@@ -160,19 +160,21 @@ class RestoreDenseFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, y_flat, time_steps_i32, cu_seqlens, dim: int, seqlen: int):
+        # the forward also writes the event bitmap (one bit per channel and
+        # position) that the backward sweeps instead of the event times
         with cuda_stage("dense_restoration_forward"):
-            out = load_ops().restore_dense_fwd(y_flat, time_steps_i32, cu_seqlens, dim, seqlen)
-        ctx.save_for_backward(time_steps_i32, cu_seqlens)
+            out, bitmap = load_ops().restore_dense_fwd_bitmap(y_flat, time_steps_i32, cu_seqlens, dim, seqlen)
+        ctx.save_for_backward(time_steps_i32, cu_seqlens, bitmap)
         ctx.dim = dim
         ctx.seqlen = seqlen
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        time_steps_i32, cu_seqlens = ctx.saved_tensors
+        time_steps_i32, cu_seqlens, bitmap = ctx.saved_tensors
         with cuda_stage("restore_backward"):
-            dy = load_ops().restore_dense_bwd(dout.contiguous(), time_steps_i32, cu_seqlens,
-                                              ctx.dim, ctx.seqlen)
+            dy = load_ops().restore_dense_bwd_bitmap(dout.contiguous(), time_steps_i32, cu_seqlens, bitmap,
+                                                     ctx.dim, ctx.seqlen)
         return dy, None, None, None, None
 
 

@@ -119,7 +119,7 @@ STAGE_OPS = {
 }
 # kernels each stage launches (all ours): extract 3, expand 2, gather 1,
 # scan fwd 1, restore fwd 1, restore bwd 1, scan bwd 2, gather bwd 4
-KERNELS_PER_STEP = 15
+KERNELS_PER_STEP = 16
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per stage on the
 # c1 workload, summed over the stage's kernels, from one ncu capture of

@@ -301,6 +301,8 @@ BCM_API bcm_status bcm_flat_ch_bwd(const bcm_flat_ch_args* args, cudaStream_t st
  *   restore_dense_fwd_kernel.cuh:38-112, restore_dense_bwd_kernel.cuh:42-113).
  * Event selection follows the reference search exactly: at most the first
  * 4095 events of a channel are addressable (index capped at 4094).
+ * The times of a channel are strictly increasing and lie in [0, seqlen), as
+ * extraction produces them.
  * out (fwd) and dy (bwd) are written in full; no pre-zeroing needed.
  * ------------------------------------------------------------------------- */
 BCM_API bcm_status bcm_restore_dense_fwd(const void* y_flat, bcm_dtype y_dtype,
@@ -311,12 +313,41 @@ BCM_API bcm_status bcm_restore_dense_fwd(const void* y_flat, bcm_dtype y_dtype,
                                  void* out, bcm_dtype out_dtype,
                                  cudaStream_t stream);
 
+/* Forward that also writes the event bitmap (bit t%32 of word
+ * [b][t/32][d] set where channel b*dim+d has an addressable event at t;
+ * bcm_restore_bitmap_bytes bytes, every word written, no pre-zeroing) for
+ * bcm_restore_dense_bwd_bitmap: the autograd pair keeps it between the two
+ * passes so the backward needs neither the event times nor a bitmap pass. */
+BCM_API size_t bcm_restore_bitmap_bytes(int64_t n_channels, int64_t seqlen);
+BCM_API bcm_status bcm_restore_dense_fwd_bitmap(const void* y_flat, bcm_dtype y_dtype,
+                                 const int32_t* time_steps,
+                                 const int32_t* cu_seqlens,
+                                 int64_t n_events, int64_t n_channels,
+                                 int64_t dim, int64_t seqlen,
+                                 void* out, bcm_dtype out_dtype,
+                                 uint32_t* event_bitmap, cudaStream_t stream);
+BCM_API bcm_status bcm_restore_dense_bwd_bitmap(const void* dout, bcm_dtype dtype,
+                                 const int32_t* time_steps,
+                                 const int32_t* cu_seqlens,
+                                 int64_t n_events, int64_t n_channels,
+                                 int64_t dim, int64_t seqlen,
+                                 const uint32_t* event_bitmap, float* dy,
+                                 cudaStream_t stream);
+
+/* The backward's workspace (one bit per channel and position) is optional:
+ * with it an event bitmap is built first and the row sweep needs no event
+ * loads; with NULL the windowed kernel runs.  Both sum each interval in a
+ * fixed order (run-to-run identical); they differ only in fp32 rounding, as
+ * the windowed kernel adds 32-row partials. */
+BCM_API size_t bcm_restore_workspace_bytes(int64_t n_channels, int64_t seqlen);
+
 BCM_API bcm_status bcm_restore_dense_bwd(const void* dout, bcm_dtype dtype,
                                  const int32_t* time_steps,
                                  const int32_t* cu_seqlens,
                                  int64_t n_events, int64_t n_channels,
                                  int64_t dim, int64_t seqlen,
-                                 float* dy, cudaStream_t stream);
+                                 float* dy, void* workspace, size_t workspace_bytes,
+                                 cudaStream_t stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

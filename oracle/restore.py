@@ -51,3 +51,21 @@ def restore_dense_bwd(dout, ts, cu, dim: int, seqlen: int):
         b, d = divmod(ch, dim)
         np.add.at(dy, s + idx[ok], d64[b, ok, d])
     return dy
+
+
+def event_bitmap(ts, cu, dim: int, seqlen: int) -> np.ndarray:
+    """uint32 [B, ceil(L/32), dim]: bit t%32 of word [b, t//32, d] is set where
+    channel b*dim+d has an addressable event (one of its first SEARCH_CAP) at
+    t in [0, L).  The product's restore forward writes this for its backward;
+    the reference has no such array (it searches the times again)."""
+    NC = cu.size - 1
+    B = NC // dim
+    nw = (seqlen + 31) // 32
+    bm = np.zeros((B, nw, dim), dtype=np.uint64)
+    for ch in range(NC):
+        s, e = int(cu[ch]), int(cu[ch + 1])
+        t = np.asarray(ts[s:min(e, s + SEARCH_CAP)], dtype=np.int64)
+        t = t[(t >= 0) & (t < seqlen)]
+        b, d = divmod(ch, dim)
+        np.bitwise_or.at(bm[b, :, d], t >> 5, np.left_shift(np.uint64(1), (t & 31).astype(np.uint64)))
+    return bm.astype(np.uint32)

@@ -35,11 +35,23 @@ def _check(t, cu, dim, L, y_dtype=torch.float32, out_dtype=None, seed=0):
     assert out.dtype == exp_dtype
     ref_t = torch.as_tensor(ref, dtype=torch.float32).to(exp_dtype)
     assert_exact(out, ref_t, "restore fwd")
+    # the forward that also writes the event bitmap for the backward
+    out_b, bm = ops.restore_dense_fwd_bitmap(y.to(dev), ts, cus, dim, L, out_dtype)
+    assert torch.equal(out_b, out)
+    assert bm.dtype == torch.int32 and bm.shape == ((cu.size - 1) // dim, (L + 31) // 32, dim)
+    assert np.array_equal(bm.cpu().numpy().view(np.uint32), rs.event_bitmap(t, cu, dim, L)), "event bitmap"
     B = (cu.size - 1) // dim
     dout = torch.randn(B, L, dim, generator=g).to(y_dtype)
-    dy = ops.restore_dense_bwd(dout.to(dev), ts, cus, dim, L)
-    assert dy.dtype == torch.float32
-    assert_close(dy, rs.restore_dense_bwd(dout.float().numpy(), t, cu, dim, L), 1e-5, "restore bwd")
+    dy_ref = rs.restore_dense_bwd(dout.float().numpy(), t, cu, dim, L)
+    for bitmap in (True, False):
+        dy = ops.restore_dense_bwd(dout.to(dev), ts, cus, dim, L, bitmap)
+        assert dy.dtype == torch.float32
+        assert_close(dy, dy_ref, 1e-5, f"restore bwd (bitmap={bitmap})")
+        # each kernel sums every interval in one fixed order: run to run identical
+        assert torch.equal(dy, ops.restore_dense_bwd(dout.to(dev), ts, cus, dim, L, bitmap))
+        if bitmap:
+            # same sweep from the forward's bitmap: bit-identical
+            assert torch.equal(dy, ops.restore_dense_bwd_bitmap(dout.to(dev), ts, cus, bm, dim, L))
 
 
 @pytest.mark.parametrize("cfg", ["c0", "c1"])
