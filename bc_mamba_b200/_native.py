@@ -36,6 +36,7 @@ ABI_SYMBOLS = (
     "bcm_flat_ch_bwd_workspace_bytes",
     "bcm_flat_ch_fwd",
     "bcm_flat_ch_bwd",
+    "bcm_extract_expand_fill",
     "bcm_restore_workspace_bytes",
     "bcm_restore_bitmap_bytes",
     "bcm_restore_dense_fwd_bitmap",

@@ -112,7 +112,8 @@ constexpr int kScanThreads = 1024;
 
 __global__ void __launch_bounds__(kScanThreads)
 counts_scan_kernel(const int32_t* __restrict__ counts, int64_t n,
-                   int32_t* __restrict__ cu, int32_t* __restrict__ max_out) {
+                   int32_t* __restrict__ cu, int32_t* __restrict__ max_out,
+                   int32_t* __restrict__ summary) {   // {total, max}: one copy to the host
     __shared__ int s_warp_sum[32];
     __shared__ int s_warp_max[32];
     const int tid = threadIdx.x;
@@ -141,7 +142,10 @@ counts_scan_kernel(const int32_t* __restrict__ counts, int64_t n,
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) m = max(m, __shfl_xor_sync(kFull, m, off));
         s_warp_sum[lane] = si - s;  // exclusive
-        if (lane == 0) *max_out = m;
+        if (lane == 0) {
+            *max_out = m;
+            summary[1] = m;
+        }
     }
     __syncthreads();
     int run = s_warp_sum[warp] + incl - local;  // exclusive prefix for this thread
@@ -150,6 +154,7 @@ counts_scan_kernel(const int32_t* __restrict__ counts, int64_t n,
         run += counts[i];
         cu[i + 1] = run;
     }
+    if (tid == kScanThreads - 1) summary[0] = run;   // the last range ends at n: the total
 }
 
 // ---- pass 3: mask words → (ch, t, k) ---------------------------------------
@@ -197,6 +202,62 @@ mask_fill_kernel(const uint32_t* __restrict__ mask, const int32_t* __restrict__ 
         if (lane == 0 && total > 0) st[-1] = st[total - 1];
         __syncwarp();
         pos += total;
+    }
+}
+
+// Pass 3 writing the expanded stream directly (extraction followed by
+// expansion, without the base arrays): base channel c's events are written
+// `expand` times, copy r at s*expand + r*cnt + i as channel c*expand + r (the
+// layout expand_events_kernel produces), and the warp also writes the
+// expanded cu_seqlens entries of its channel.
+__global__ void __launch_bounds__(kFillWarps * 32)
+mask_fill_expand_kernel(const uint32_t* __restrict__ mask, const int32_t* __restrict__ base_cu,
+                        int64_t n_rows, int n_words, int expand,
+                        int32_t* __restrict__ ch_ids, int32_t* __restrict__ t_steps,
+                        int32_t* __restrict__ k_flat, int32_t* __restrict__ cu) {
+    __shared__ int s_t[kFillWarps][1024 + 1];
+    const int lane = lane_id();
+    const int w_in = threadIdx.x >> 5;
+    const int64_t row = (int64_t)blockIdx.x * kFillWarps + w_in;
+    if (row >= n_rows) return;
+    int* st = s_t[w_in] + 1;             // st[-1] holds the previous block's last t
+    const uint32_t* mr = mask + row * (int64_t)n_words;
+    const int s = base_cu[row];
+    const int cnt = base_cu[row + 1] - s;
+    const int64_t out0 = (int64_t)s * expand;
+    for (int r = lane; r < expand; r += 32) cu[row * expand + r] = (int32_t)(out0 + (int64_t)r * cnt);
+    if (row == n_rows - 1 && lane == 0) cu[n_rows * expand] = (int32_t)((int64_t)base_cu[n_rows] * expand);
+    int local = 0;
+    if (lane == 0) st[-1] = -1;
+    for (int w0 = 0; w0 < n_words; w0 += 32) {
+        const int w = w0 + lane;
+        const uint32_t word = (w < n_words) ? mr[w] : 0u;
+        const int c = __popc(word);
+        const int incl = warp_inclusive_sum(c);
+        const int total = __shfl_sync(kFull, incl, 31);
+        int o = incl - c;
+        uint32_t bits = word;
+        while (bits) {
+            const int b = __ffs(bits) - 1;
+            bits &= bits - 1;
+            st[o++] = w * 32 + b;
+        }
+        __syncwarp();
+        for (int i = lane; i < total; i += 32) {
+            const int t = st[i];
+            const int prev = st[i - 1];
+            const int kv = (prev < 0) ? (t + 1) : (t - prev);
+            for (int r = 0; r < expand; ++r) {
+                const int64_t o2 = out0 + (int64_t)r * cnt + local + i;
+                ch_ids[o2] = (int32_t)(row * expand + r);
+                t_steps[o2] = t;
+                k_flat[o2] = kv;
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && total > 0) st[-1] = st[total - 1];
+        __syncwarp();
+        local += total;
     }
 }
 
@@ -364,25 +425,49 @@ using namespace bcm;
 // counts -> cu_seqlens and max on the device, then the event total to the
 // host (the one synchronisation the reference API implies: outputs are sized
 // by it).
+// Bytes of the extraction workspace taken by the event bit mask; the
+// {total, max} summary of the count scan follows it.
+static size_t mask_region_bytes(int64_t n_base_channels, int64_t seqlen) {
+    const int64_t words = (seqlen + 31) / 32;
+    return align_up((size_t)(n_base_channels * words * sizeof(uint32_t)), 256);
+}
+
+// A small pinned host buffer per host thread for the summary copy (a copy to
+// pageable memory is staged by the driver); nullptr if pinning fails.
+static int32_t* pinned_summary() {
+    thread_local int32_t* buf = nullptr;
+    thread_local bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        if (cudaHostAlloc(&p, 2 * sizeof(int32_t), cudaHostAllocPortable) == cudaSuccess)
+            buf = static_cast<int32_t*>(p);
+        else
+            (void)cudaGetLastError();
+    }
+    return buf;
+}
+
 static bcm_status scan_counts_and_sync(const int32_t* counts, int64_t n_base_channels, int32_t* cu_seqlens,
-                                       int32_t* max_seqlen, int64_t* n_events_host, int32_t* max_host,
-                                       cudaStream_t stream) {
-    counts_scan_kernel<<<1, kScanThreads, 0, stream>>>(counts, n_base_channels, cu_seqlens, max_seqlen);
+                                       int32_t* max_seqlen, void* workspace, int64_t seqlen,
+                                       int64_t* n_events_host, int32_t* max_host, cudaStream_t stream) {
+    int32_t* summary = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) +
+                                                  mask_region_bytes(n_base_channels, seqlen));
+    counts_scan_kernel<<<1, kScanThreads, 0, stream>>>(counts, n_base_channels, cu_seqlens, max_seqlen, summary);
     BCM_LAUNCH_CHECK();
-    int32_t e_host = 0;
-    BCM_CUDA_TRY(cudaMemcpyAsync(&e_host, cu_seqlens + n_base_channels, sizeof(int32_t),
-                                 cudaMemcpyDeviceToHost, stream));
-    if (max_host)
-        BCM_CUDA_TRY(cudaMemcpyAsync(max_host, max_seqlen, sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
+    int32_t pageable[2] = {0, 0};
+    int32_t* host = pinned_summary();
+    if (host == nullptr) host = pageable;
+    BCM_CUDA_TRY(cudaMemcpyAsync(host, summary, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
     BCM_CUDA_TRY(cudaStreamSynchronize(stream));
-    *n_events_host = e_host;
+    *n_events_host = host[0];
+    if (max_host) *max_host = host[1];
     return BCM_OK;
 }
 
 extern "C" size_t bcm_extract_workspace_bytes(int64_t n_base_channels, int64_t seqlen) {
     if (n_base_channels < 0 || seqlen < 0) return 0;
-    const int64_t words = (seqlen + 31) / 32;
-    return align_up((size_t)(n_base_channels * words * sizeof(uint32_t)), 256);
+    return mask_region_bytes(n_base_channels, seqlen) + 256;
 }
 
 extern "C" bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype dtype,
@@ -404,8 +489,8 @@ extern "C" bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype d
                   workspace_bytes, need);
         return BCM_ERR_WORKSPACE;
     }
-    BCM_CUDA_TRY(cudaMemsetAsync(max_seqlen, 0, sizeof(int32_t), stream));
     if (n_base_channels == 0) {
+        BCM_CUDA_TRY(cudaMemsetAsync(max_seqlen, 0, sizeof(int32_t), stream));
         BCM_CUDA_TRY(cudaMemsetAsync(cu_seqlens, 0, sizeof(int32_t), stream));
         BCM_CUDA_TRY(cudaStreamSynchronize(stream));
         *n_events_host = 0;
@@ -430,8 +515,8 @@ extern "C" bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype d
         });
         if (st != BCM_OK) return st;
     }
-    return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, n_events_host, max_seqlen_host,
-                                stream);
+    return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, workspace, seqlen,
+                                n_events_host, max_seqlen_host, stream);
 }
 
 extern "C" bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtype dtype, int64_t batch,
@@ -452,8 +537,8 @@ extern "C" bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtyp
         set_error("extract_base_events_bld: workspace of %zu bytes < required %zu", workspace_bytes, need);
         return BCM_ERR_WORKSPACE;
     }
-    BCM_CUDA_TRY(cudaMemsetAsync(max_seqlen, 0, sizeof(int32_t), stream));
     if (n_base_channels == 0) {
+        BCM_CUDA_TRY(cudaMemsetAsync(max_seqlen, 0, sizeof(int32_t), stream));
         BCM_CUDA_TRY(cudaMemsetAsync(cu_seqlens, 0, sizeof(int32_t), stream));
         BCM_CUDA_TRY(cudaStreamSynchronize(stream));
         *n_events_host = 0;
@@ -480,8 +565,8 @@ extern "C" bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtyp
         });
         if (st != BCM_OK) return st;
     }
-    return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, n_events_host, max_seqlen_host,
-                                stream);
+    return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, workspace, seqlen,
+                                n_events_host, max_seqlen_host, stream);
 }
 
 extern "C" bcm_status bcm_extract_base_fill(int64_t n_base_channels, int64_t seqlen,
@@ -505,6 +590,32 @@ extern "C" bcm_status bcm_extract_base_fill(int64_t n_base_channels, int64_t seq
     mask_fill_kernel<<<grid, kFillWarps * 32, 0, stream>>>(
         static_cast<const uint32_t*>(workspace), cu_seqlens, n_base_channels, L, n_words,
         ch_ids, t_steps, k_flat);
+    BCM_LAUNCH_CHECK();
+    return BCM_OK;
+}
+
+extern "C" bcm_status bcm_extract_expand_fill(int64_t n_base_channels, int64_t seqlen,
+                                              const int32_t* base_cu_seqlens, const void* workspace,
+                                              size_t workspace_bytes, int64_t expand, int32_t* ch_ids,
+                                              int32_t* t_steps, int32_t* k_flat, int32_t* cu_seqlens,
+                                              cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(n_base_channels >= 0 && seqlen >= 0, "extract_expand_fill: negative size");
+    BCM_REQUIRE(expand >= 1 && n_base_channels * expand < (1ll << 31), "extract_expand_fill: bad expand");
+    if (n_base_channels == 0) return BCM_OK;
+    BCM_REQUIRE(base_cu_seqlens && cu_seqlens, "extract_expand_fill: null pointer");
+    const size_t need = bcm_extract_workspace_bytes(n_base_channels, seqlen);
+    if (workspace_bytes < need || !workspace) {
+        set_error("extract_expand_fill: workspace of %zu bytes < required %zu", workspace_bytes, need);
+        return BCM_ERR_WORKSPACE;
+    }
+    BCM_REQUIRE(seqlen == 0 || (ch_ids && t_steps && k_flat), "extract_expand_fill: null pointer");
+    const int L = (int)seqlen;
+    const int n_words = (L + 31) / 32;
+    const int grid = ceil_div(n_base_channels, kFillWarps);
+    mask_fill_expand_kernel<<<grid, kFillWarps * 32, 0, stream>>>(
+        static_cast<const uint32_t*>(workspace), base_cu_seqlens, n_base_channels, n_words, (int)expand,
+        ch_ids, t_steps, k_flat, cu_seqlens);
     BCM_LAUNCH_CHECK();
     return BCM_OK;
 }

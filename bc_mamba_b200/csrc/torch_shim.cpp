@@ -57,9 +57,11 @@ Tensor workspace(int64_t bytes, const at::Device& dev) {
 // ---------------------------------------------------------------- extract ----
 // count pass (the given call) + fill, shared by both input layouts; the
 // count call also brings the maximum per-channel count to the host (max_host)
+// expand > 0: the fill writes the expanded stream directly (ch, ts, kf,
+// expanded cu, max) instead of the base stream (ch, ts, kf, cu, counts, max)
 template <typename CountFn>
 std::vector<Tensor> extract_with(const Tensor& like, int64_t NCb, int64_t L, CountFn count, const char* what,
-                                 int32_t* max_host = nullptr) {
+                                 int32_t* max_host = nullptr, int64_t expand = 0) {
     c10::cuda::CUDAGuard guard(like.device());
     auto opt_i = torch::TensorOptions().dtype(torch::kInt32).device(like.device());
     auto counts = torch::empty({NCb}, opt_i);
@@ -70,6 +72,22 @@ std::vector<Tensor> extract_with(const Tensor& like, int64_t NCb, int64_t L, Cou
     int32_t mh = 0;
     check_status(count(counts, cu, mx, ws, &E, &mh), what);
     if (max_host) *max_host = mh;
+    if (expand > 0) {
+        TORCH_CHECK(E * expand < (1ll << 31) && NCb * expand < (1ll << 31), what, ": expanded sizes exceed int32");
+        auto ch = torch::empty({E * expand}, opt_i);
+        auto ts = torch::empty({E * expand}, opt_i);
+        auto kf = torch::empty({E * expand}, opt_i);
+        auto cu_x = torch::empty({NCb * expand + 1}, opt_i);
+        if (E == 0) {
+            cu_x.zero_();
+            return {ch, ts, kf, cu_x, torch::zeros({1}, opt_i)};
+        }
+        check_status(bcm_extract_expand_fill(NCb, L, cu.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), expand,
+                                             ch.data_ptr<int32_t>(), ts.data_ptr<int32_t>(),
+                                             kf.data_ptr<int32_t>(), cu_x.data_ptr<int32_t>(), cur_stream()),
+                     what);
+        return {ch, ts, kf, cu_x, mx};
+    }
     if (E == 0) {
         auto ei = torch::zeros({0}, opt_i);
         auto ms = torch::zeros({1}, opt_i);
@@ -85,7 +103,8 @@ std::vector<Tensor> extract_with(const Tensor& like, int64_t NCb, int64_t L, Cou
     return {ch, ts, kf, cu, counts, mx};
 }
 
-std::vector<Tensor> extract_base_events_impl(const Tensor& base_input, double threshold, int32_t* max_host) {
+std::vector<Tensor> extract_base_events_impl(const Tensor& base_input, double threshold, int32_t* max_host,
+                                             int64_t expand = 0) {
     TORCH_CHECK(base_input.is_cuda(), "base_input must be CUDA");
     TORCH_CHECK(base_input.is_contiguous(), "base_input must be contiguous");
     TORCH_CHECK(base_input.dim() == 3, "base_input must be 3-D [B, d_model, L]");
@@ -99,7 +118,7 @@ std::vector<Tensor> extract_base_events_impl(const Tensor& base_input, double th
                                                           mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), E,
                                                           mh, cur_stream());
                         },
-                        "extract_base_events", max_host);
+                        "extract_base_events", max_host, expand);
 }
 
 std::vector<Tensor> extract_base_events_fwd(Tensor base_input, double threshold) {
@@ -107,7 +126,8 @@ std::vector<Tensor> extract_base_events_fwd(Tensor base_input, double threshold)
 }
 
 // Same outputs from the (B, L, d_model) layout (no transposed copy).
-std::vector<Tensor> extract_base_events_bld_impl(const Tensor& x, double threshold, int32_t* max_host) {
+std::vector<Tensor> extract_base_events_bld_impl(const Tensor& x, double threshold, int32_t* max_host,
+                                                 int64_t expand = 0) {
     TORCH_CHECK(x.is_cuda(), "x must be CUDA");
     TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
     TORCH_CHECK(x.dim() == 3, "x must be 3-D [B, L, d_model]");
@@ -121,7 +141,7 @@ std::vector<Tensor> extract_base_events_bld_impl(const Tensor& x, double thresho
                                                               mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), E,
                                                               mh, cur_stream());
                         },
-                        "extract_base_events_bld", max_host);
+                        "extract_base_events_bld", max_host, expand);
 }
 
 std::vector<Tensor> extract_base_events_bld_fwd(Tensor x, double threshold) {
@@ -136,6 +156,19 @@ std::tuple<std::vector<Tensor>, int64_t> extract_base_events_host_max(Tensor bas
     int32_t mh = 0;
     auto r = bld ? extract_base_events_bld_impl(base_input, threshold, &mh)
                  : extract_base_events_impl(base_input, threshold, &mh);
+    return {r, (int64_t)mh};
+}
+
+// Extraction + expansion in one fill pass: the outputs of
+// expand_base_events(*extract_base_events(x, threshold)[:4], B, d_model,
+// expand) and the maximum per-channel count as a host integer (the one
+// synchronisation of the count pass); bld selects the (B, L, d_model) layout.
+std::tuple<std::vector<Tensor>, int64_t> extract_expanded_events(Tensor x, double threshold, int64_t expand,
+                                                                  bool bld) {
+    TORCH_CHECK(expand >= 1, "extract_expanded_events: expand must be >= 1");
+    int32_t mh = 0;
+    auto r = bld ? extract_base_events_bld_impl(x, threshold, &mh, expand)
+                 : extract_base_events_impl(x, threshold, &mh, expand);
     return {r, (int64_t)mh};
 }
 
@@ -706,6 +739,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("extract_base_events_host_max", &extract_base_events_host_max, py::arg("x"), py::arg("threshold"),
           py::arg("bld") = false,
           "extract_base_events (bld: from the (B, L, d_model) layout) -> (6 outputs, max count as a host int)");
+    m.def("extract_expanded_events", &extract_expanded_events, py::arg("x"), py::arg("threshold"),
+          py::arg("expand"), py::arg("bld") = false,
+          "extract_base_events then expand_base_events in one fill pass -> ((ch, t, k, cu, max), "
+          "max count as a host int); bld: from the (B, L, d_model) layout");
     m.def("extract_base_events_bld", &extract_base_events_bld_fwd, py::arg("x"), py::arg("threshold"),
           "extract_base_events from the (B, L, d_model) layout: same 6 outputs, no transposed copy");
     m.def("conv_events_fwd", &conv_events_fwd, py::arg("x"), py::arg("weight"), py::arg("bias"),

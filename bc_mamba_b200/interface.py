@@ -120,11 +120,15 @@ class SelectiveScanFlatChFn(torch.autograd.Function):
             saved += [pw_B, pw_C]
         ctx.save_for_backward(*saved)
         ctx.mark_non_differentiable(x)
+        # x takes no gradient: without this autograd fills a zero tensor for it
+        ctx.set_materialize_grads(False)
         return (res[2] if ctx.has_z else out), x
 
     @staticmethod
     def backward(ctx, dout, _dx):
         ops = load_ops()
+        if dout is None:        # the output was not used in the loss
+            return (None,) * 16
         if dout.stride(-1) != 1:
             dout = dout.contiguous()
         it = iter(ctx.saved_tensors)
@@ -250,11 +254,11 @@ def extract_events_base(base_input, x_conv, threshold: float, expand: int):
     ops = load_ops()
     B, d_model, L = base_input.shape
     with cuda_stage("routing_index_extraction"):
-        # the maximum count arrives on the host with the event total (one
-        # synchronisation); expansion copies counts, so it is max_seqlen too
-        (bch, bt, bk, bcu, _counts, _bmax), max_seqlen = ops.extract_base_events_host_max(base_input, threshold)
-    with cuda_stage("active_token_packing"):
-        ch, ts, kf, cu, _mx = ops.expand_base_events(bch, bt, bk, bcu, B, d_model, expand)
+        # extraction and expansion in one fill pass (the base stream is never
+        # written); the maximum count arrives on the host with the event total
+        # (one synchronisation), and expansion copies counts, so it is
+        # max_seqlen of the expanded stream too
+        (ch, ts, kf, cu, _mx), max_seqlen = ops.extract_expanded_events(base_input, threshold, expand)
     x_flat = gather_events(x_conv, ch, ts)
     return ch, ts, kf, cu, int(max_seqlen), x_flat
 
@@ -269,11 +273,10 @@ def extract_events_1d(hidden_states, x_conv, threshold: float, expand: int):
     B, L, d_model = hidden_states.shape
     with cuda_stage("routing_index_extraction"):
         # straight from the (B, L, d_model) layout (the reference first makes a
-        # transposed (B, d_model, L) copy, e_model.py:376); the maximum count
-        # comes back with the event total (one synchronisation, no .item())
-        (bch, bt, bk, bcu, _counts, _bmax), max_seqlen = ops.extract_base_events_host_max(
-            hidden_states.contiguous(), threshold, bld=True)
-    with cuda_stage("active_token_packing"):
-        ch, ts, kf, cu, _mx = ops.expand_base_events(bch, bt, bk, bcu, B, d_model, expand)
+        # transposed (B, d_model, L) copy, e_model.py:376), extraction and
+        # expansion in one fill pass; the maximum count comes back with the
+        # event total (one synchronisation, no .item())
+        (ch, ts, kf, cu, _mx), max_seqlen = ops.extract_expanded_events(
+            hidden_states.contiguous(), threshold, expand, bld=True)
     x_flat = gather_events(x_conv, ch, ts)
     return ch, ts, kf, cu, int(max_seqlen), x_flat

@@ -122,6 +122,20 @@ BCM_API bcm_status bcm_expand_base_events(const int32_t* base_ch_ids,
                                   int32_t* k_flat, int32_t* cu_seqlens,
                                   int32_t* max_seqlen, cudaStream_t stream);
 
+/* Extraction fill and expansion in one pass: after bcm_extract_base_count (or
+ * _bld) on the same workspace, writes the stream bcm_expand_base_events would
+ * make from the base stream — ch_ids/t_steps/k_flat[E_base*expand] and
+ * cu_seqlens[NCb*expand+1] — without writing the base stream; the maximum
+ * per-channel count is the count pass's.  Interface path of
+ * Mamba.extract_events_1d (reference spike_mamba/e_model.py:371-390), which
+ * keeps only the expanded stream. */
+BCM_API bcm_status bcm_extract_expand_fill(int64_t n_base_channels, int64_t seqlen,
+                                  const int32_t* base_cu_seqlens,
+                                  const void* workspace, size_t workspace_bytes,
+                                  int64_t expand, int32_t* ch_ids,
+                                  int32_t* t_steps, int32_t* k_flat,
+                                  int32_t* cu_seqlens, cudaStream_t stream);
+
 /* ------------------------------------------------------------------------- *
  * Event gather of x[NC, L] at (channel_ids, time_steps) and its transpose.
  * Replaces extract_events_cuda.gather_events_fwd / gather_events_bwd

@@ -42,7 +42,12 @@ def test_workspace_queries_without_gpu():
     lib = bc_mamba_b200.load_library()
     lib.bcm_extract_workspace_bytes.restype = ctypes.c_size_t
     lib.bcm_extract_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
-    assert lib.bcm_extract_workspace_bytes(4096, 2048) == 4096 * 64 * 4
+    # one bit per base channel and position, plus a 256-byte {total, max} slot
+    assert lib.bcm_extract_workspace_bytes(4096, 2048) == 4096 * 64 * 4 + 256
+    lib.bcm_restore_bitmap_bytes.restype = ctypes.c_size_t
+    lib.bcm_restore_bitmap_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    assert lib.bcm_restore_bitmap_bytes(8192, 2048) == 8192 * 64 * 4
+    assert lib.bcm_restore_bitmap_bytes(3, 33) == 3 * 2 * 4
 
 
 def test_shim_exports_reference_entry_points():
@@ -52,6 +57,10 @@ def test_shim_exports_reference_entry_points():
     for name in ["fwd", "bwd", "fwd_flat_ch", "bwd_flat_ch", "extract_events", "extract_base_events",
                  "expand_base_events", "gather_events_fwd", "gather_events_bwd", "restore_dense_fwd",
                  "restore_dense_bwd"]:
+        assert callable(getattr(ops, name)), name
+    # the product's own fused entry points beside them
+    for name in ["extract_expanded_events", "extract_base_events_host_max", "restore_dense_fwd_bitmap",
+                 "restore_dense_bwd_bitmap", "conv_events_fwd", "conv_events_bwd"]:
         assert callable(getattr(ops, name)), name
     doc = ops.fwd_flat_ch.__doc__
     for arg in ["u_flat", "k_flat", "cu_seqlens", "max_seqlen", "dt_idle", "dt_active", "tile_offsets",
