@@ -88,114 +88,6 @@ __device__ __forceinline__ int stage_channel(const int32_t* ts, const Tin* y, in
     return taken;
 }
 
-template <typename Tin, typename Tout>
-__global__ void __launch_bounds__(kWarpsR * 32)
-restore_fwd_kernel(const Tin* __restrict__ y, const int32_t* __restrict__ ts,
-                   const int32_t* __restrict__ cu, int D, int L, int part_len,
-                   int n_dblk, Tout* __restrict__ out, uint32_t* __restrict__ bm) {
-    __shared__ float s_val[kDB][kTT + 1];    // event values of the window, in order
-    __shared__ uint32_t s_mask[kDB][kMP];
-    __shared__ float s_carry[kDB];           // value held at the window start
-    __shared__ int s_p[kDB];
-    const int dblk = blockIdx.x % n_dblk;
-    const int part = blockIdx.x / n_dblk;
-    const int b = blockIdx.y;
-    const int d0 = dblk * kDB;
-    const int t_beg = part * part_len;
-    const int t_end = min(L, t_beg + part_len);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-
-    int c_beg[kChPerWarp], c_n[kChPerWarp];
-#pragma unroll
-    for (int ci = 0; ci < kChPerWarp; ++ci) {
-        const int d = d0 + warp * kChPerWarp + ci;
-        c_beg[ci] = 0; c_n[ci] = 0;
-        if (d < D) {
-            const int ch = b * D + d;
-            c_beg[ci] = cu[ch];
-            c_n[ci] = min(cu[ch + 1] - c_beg[ci], kCap);
-        }
-    }
-    if (lane < kChPerWarp) {
-        int beg = 0, n = 0;
-#pragma unroll
-        for (int ci = 0; ci < kChPerWarp; ++ci)
-            if (ci == lane) { beg = c_beg[ci]; n = c_n[ci]; }
-        const int p = lower_bound_i32(ts + beg, n, t_beg);
-        s_p[warp * kChPerWarp + lane] = p;
-        s_carry[warp * kChPerWarp + lane] = (p > 0) ? to_f32<Tin>(y[beg + p - 1]) : 0.f;
-    }
-    __syncwarp();
-    // first 32 events of every channel of the next window, loaded ahead
-    float v_pre[kChPerWarp];
-    int t_pre[kChPerWarp];
-    auto prefetch = [&](const int (&pp)[kChPerWarp]) {
-#pragma unroll
-        for (int ci = 0; ci < kChPerWarp; ++ci) {
-            const int j = pp[ci] + lane;
-            const bool in = j < c_n[ci];
-            t_pre[ci] = in ? ts[c_beg[ci] + j] : INT_MAX;
-            v_pre[ci] = in ? to_f32<Tin>(y[c_beg[ci] + j]) : 0.f;
-        }
-    };
-    {
-        int p0[kChPerWarp];
-#pragma unroll
-        for (int ci = 0; ci < kChPerWarp; ++ci) p0[ci] = s_p[warp * kChPerWarp + ci];
-        prefetch(p0);
-    }
-    const bool cvalid = d0 + lane < D;
-
-    for (int t0 = t_beg; t0 < t_end; t0 += kTT) {
-        const int wend = min(t0 + kTT, t_end);
-        // 1. staging of this warp's 8 channels
-        float carry_new[kChPerWarp];
-        int p_new[kChPerWarp];
-#pragma unroll
-        for (int ci = 0; ci < kChPerWarp; ++ci) {
-            const int c = warp * kChPerWarp + ci;
-            const int p = s_p[c];
-            float last = s_carry[c];
-            const int taken = stage_channel<Tin, true>(ts, y, c_beg[ci], c_n[ci], p, t0, wend, s_mask[c],
-                                                       s_val[c], lane, last, t_pre[ci], v_pre[ci]);
-            carry_new[ci] = last;
-            p_new[ci] = p + taken;
-        }
-        if (t0 + kTT < t_end) prefetch(p_new);   // in flight during the sweep
-        __syncthreads();
-        // 2. sweep: lane = channel, this warp's 32 positions, each a coalesced
-        //    row of 32 features stored straight to (B, L, D)
-        {
-            const int c = lane;
-            uint32_t before = 0;
-#pragma unroll
-            for (int w = 0; w < kMW; ++w)
-                if (w < warp) before += __popc(s_mask[c][w]);
-            const uint32_t mw = s_mask[c][warp];
-            int e = (int)before;
-            float cur = e > 0 ? s_val[c][e - 1] : s_carry[c];
-            const int tw = t0 + warp * 32;
-            Tout* col = out + ((int64_t)b * L + tw) * D + d0 + c;
-            // the event bitmap for the backward: parts are whole 128-row
-            // windows, so every word [b][tw/32][d] is written by one lane
-            if (bm != nullptr && cvalid && tw < wend)
-                bm[((int64_t)b * ((L + 31) >> 5) + (tw >> 5)) * D + d0 + c] = mw;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                if ((mw >> i) & 1u) cur = s_val[c][e++];
-                if (cvalid && tw + i < wend) col[(int64_t)i * D] = from_f32<Tout>(cur);
-            }
-        }
-        __syncthreads();
-        // advance the channel state (each warp updates its own 8 channels)
-        if (lane < kChPerWarp) {
-#pragma unroll
-            for (int ci = 0; ci < kChPerWarp; ++ci)
-                if (ci == lane) { s_p[warp * kChPerWarp + ci] = p_new[ci]; s_carry[warp * kChPerWarp + ci] = carry_new[ci]; }
-        }
-        __syncwarp();
-    }
-}
 
 template <typename T>
 __global__ void __launch_bounds__(kWarpsR * 32)
@@ -428,29 +320,172 @@ __device__ __forceinline__ BUnit bunit(int64_t unit, int n_dblk, int n_parts, in
     return u;
 }
 
+// k-ary lower bound: first index in [0, n) with a[i] >= key (n if none);
+// each round issues 7 independent probes, so n <= 4096 takes 4 load rounds.
+__device__ __forceinline__ int lower_bound8(const int32_t* __restrict__ a, int n, int key) {
+    int lo = 0, hi = n;   // the answer lies in [lo, hi]
+    while (hi - lo > 8) {
+        const int step = (hi - lo + 7) >> 3;
+        int c = 0;
+#pragma unroll
+        for (int k = 1; k < 8; ++k) {
+            const int p = lo + step * k;
+            c += (p < hi && a[p] < key) ? 1 : 0;
+        }
+        const int nhi = lo + step * (c + 1);
+        lo = (c > 0) ? lo + step * c + 1 : lo;
+        hi = min(hi, nhi);
+    }
+    int c = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) c += (lo + k < hi && a[lo + k] < key) ? 1 : 0;
+    return lo + c;
+}
+
+// ---- tile forward --------------------------------------------------------------
+// A warp owns one batch row b, 32 features (lane = channel) and a range of
+// positions (whole 64-row windows).  Per window the events of its 32 channels
+// are loaded coalesced, channel by channel (32 events per load, lane = event),
+// and scattered into a shared-memory tile of (value, flag) pairs
+// [row][channel] (pitch 33: the scatter of one channel's rows and the row
+// reads are conflict-free); the sweep then reads its row of the tile (lane =
+// channel), holds or replaces the value, stores the 32 features of the row
+// with one coalesced store, clears the slot and collects the event bits into
+// the bitmap words.  The first load of the next window's events is issued
+// before the sweep.  Per unit it also records the local index of its first
+// event for the backward.
+constexpr int kFW = 2;        // warps (units) per CTA
+constexpr int kTW = 64;       // rows per window
+constexpr int kTP = 33;       // tile pitch (float2 slots)
+constexpr int kSweepWarpsPerSM = 12;
+
+struct SweepLayout {
+    int n_dblk, part_len, n_parts;
+    int64_t n_units;
+};
+
+template <typename Tin, typename Tout>
+__global__ void __launch_bounds__(kFW * 32)
+restore_fwd_tile(const Tin* __restrict__ y, const int32_t* __restrict__ ts, const int32_t* __restrict__ cu,
+                 int D, int L, int nw, int part_len, int n_dblk, int n_parts, int64_t n_units,
+                 Tout* __restrict__ out, uint32_t* __restrict__ bm, int32_t* __restrict__ e_start) {
+    __shared__ float2 s_tile[kFW][kTW * kTP];
+    __shared__ int s_e[kFW][32];    // next unconsumed event of each channel (global index)
+    __shared__ int s_end[kFW][32];  // end of each channel's addressable events (global index)
+    const int w_in = threadIdx.x >> 5;
+    const int64_t unit = (int64_t)blockIdx.x * kFW + w_in;
+    if (unit >= n_units) return;   // warp-uniform; the kernel has no block barrier
+    const int lane = threadIdx.x & 31;
+    float2* tile = s_tile[w_in];
+    int* se = s_e[w_in];
+    int* send = s_end[w_in];
+    const BUnit u = bunit(unit, n_dblk, n_parts, part_len, L);
+    const int d = u.d0 + lane;
+    const bool valid = d < D;
+    int beg = 0, n = 0;
+    if (valid) {
+        const int64_t c = u.b * D + d;
+        beg = cu[c];
+        n = min(cu[c + 1] - beg, kCap);
+    }
+    const int p = (u.t_beg == 0) ? 0 : lower_bound8(ts + beg, n, u.t_beg);
+    float cur = (p > 0) ? to_f32<Tin>(y[beg + p - 1]) : 0.f;
+    if (e_start != nullptr) e_start[unit * 32 + lane] = p;
+    se[lane] = beg + p;
+    send[lane] = beg + n;
+    for (int i = lane; i < kTW * kTP; i += 32) tile[i] = make_float2(0.f, 0.f);
+    __syncwarp();
+
+    // first 32 events of every channel from its next unconsumed event
+    int pt[32];
+    float pv[32];
+    auto prefetch = [&]() {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+            const int j = se[c] + lane;
+            const bool in = j < send[c];
+            pt[c] = in ? ts[j] : INT_MAX;
+            pv[c] = in ? to_f32<Tin>(y[j]) : 0.f;
+        }
+    };
+    prefetch();
+    Tout* col = out + (u.b * L + u.t_beg) * (int64_t)D + (valid ? d : 0);
+    uint32_t* mcol = (bm != nullptr) ? bm + (u.b * nw + (u.t_beg >> 5)) * (int64_t)D + d : nullptr;
+    for (int t0 = u.t_beg; t0 < u.t_end; t0 += kTW) {
+        const int wend = min(t0 + kTW, u.t_end);
+        // 1. scatter this window's events into the tile (channel by channel)
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+            const bool in = pt[c] < wend;
+            if (in) tile[(pt[c] - t0) * kTP + c] = make_float2(pv[c], 1.f);
+            int taken = __popc(__ballot_sync(kFull, in));
+            if (taken == 32) {   // a dense window: more events of this channel
+                int e = se[c] + 32;
+                const int end = send[c];
+                while (true) {
+                    const int j = e + lane;
+                    const int tt = j < end ? ts[j] : INT_MAX;
+                    const bool in2 = tt < wend;
+                    if (in2) tile[(tt - t0) * kTP + c] = make_float2(to_f32<Tin>(y[j]), 1.f);
+                    const int k2 = __popc(__ballot_sync(kFull, in2));
+                    taken += k2;
+                    e += 32;
+                    if (k2 < 32) break;
+                }
+            }
+            if (lane == 0) se[c] += taken;
+        }
+        __syncwarp();
+        if (t0 + kTW < u.t_end) prefetch();   // next window's first loads, in flight during the sweep
+        // 2. sweep: lane = channel, one coalesced row store per position
+        uint32_t m = 0u;
+#pragma unroll
+        for (int r = 0; r < kTW; ++r) {
+            const int t = t0 + r;
+            float2* slot = tile + r * kTP + lane;
+            const float2 sv = *slot;
+            *slot = make_float2(0.f, 0.f);
+            const bool hit = sv.y != 0.f;
+            cur = hit ? sv.x : cur;
+            m |= (hit ? 1u : 0u) << (r & 31);
+            if (valid && t < wend) col[(int64_t)r * D] = from_f32<Tout>(cur);
+            if ((r & 31) == 31) {
+                if (mcol != nullptr && valid && t - 31 < wend) mcol[(int64_t)(r >> 5) * D] = m;
+                m = 0u;
+            }
+        }
+        __syncwarp();
+        col += (int64_t)kTW * D;
+        if (mcol != nullptr) mcol += (int64_t)(kTW / 32) * D;
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kBU * 32)
-restore_bwd_bitmap(const T* __restrict__ dout, const int32_t* __restrict__ cu,
-                   const uint32_t* __restrict__ bm, int D, int L, int nw, int part_len, int n_dblk, int n_parts,
-                   int64_t n_units, float* __restrict__ dy) {
+restore_bwd_bitmap(const T* __restrict__ dout, const int32_t* __restrict__ cu, const uint32_t* __restrict__ bm,
+                   const int32_t* __restrict__ e_start, int D, int L, int nw, int part_len, int n_dblk,
+                   int n_parts, int64_t n_units, float* __restrict__ dy) {
     const int64_t unit = (int64_t)blockIdx.x * kBU + (threadIdx.x >> 5);
     if (unit >= n_units) return;
     const int lane = threadIdx.x & 31;
     const BUnit u = bunit(unit, n_dblk, n_parts, part_len, L);
     const int d = u.d0 + lane;
     const bool valid = d < D;
-    int beg = 0, n = 0, n_all = 0;
+    const int dc = valid ? d : D - 1;   // lanes past D read a real column and use none of it
+    int beg = 0, n_all = 0;
     if (valid) {
         const int64_t c = u.b * D + d;
         beg = cu[c];
         n_all = cu[c + 1] - beg;
-        n = min(n_all, kCap);
     }
-    const uint32_t* mcol = bm + u.b * nw * (int64_t)D + d;
-    // index of the first event at or after t_beg: the marked events before it
-    // (times lie in [0, L), so the bitmap holds exactly the first n events)
+    const uint32_t* mcol = bm + u.b * nw * (int64_t)D + dc;
+    // local index of the first event at or after t_beg: recorded by the
+    // forward, else the marked events before t_beg (times lie in [0, L), so
+    // the bitmap holds exactly the first min(n, kCap) events)
     int p = 0;
-    if (valid) {
+    if (e_start != nullptr) {
+        p = valid ? e_start[unit * 32 + lane] : 0;
+    } else if (valid) {
 #pragma unroll 8
         for (int w = 0; w < (u.t_beg >> 5); ++w) p += __popc(mcol[(int64_t)w * D]);
     }
@@ -459,26 +494,27 @@ restore_bwd_bitmap(const T* __restrict__ dout, const int32_t* __restrict__ cu,
     int e = beg + p;        // next event (global index)
     int open = -1;          // owned event whose interval is running
     float acc = 0.f;
-    const T* col = dout + (u.b * L) * D + d;
+    const T* col = dout + (u.b * L + u.t_beg) * (int64_t)D + dc;
     for (int t0 = u.t_beg; t0 < L; t0 += 64) {
         if (t0 >= u.t_end && !__any_sync(kFull, open >= 0)) break;
         const uint32_t m0 = valid ? mcol[(int64_t)(t0 >> 5) * D] : 0u;
         const uint32_t m1 = (valid && t0 + 32 < L) ? mcol[(int64_t)((t0 >> 5) + 1) * D] : 0u;
         float v[64];
+        if (t0 + 64 <= L) {
 #pragma unroll
-        for (int r = 0; r < 64; ++r) {
-            const int t = t0 + r;
-            v[r] = (valid && t < L) ? to_f32<T>(col[(int64_t)t * D]) : 0.f;
+            for (int r = 0; r < 64; ++r) v[r] = to_f32<T>(col[(int64_t)r * D]);
+        } else {
+#pragma unroll
+            for (int r = 0; r < 64; ++r) v[r] = (t0 + r < L) ? to_f32<T>(col[(int64_t)r * D]) : 0.f;
         }
+        col += (int64_t)64 * D;
 #pragma unroll
         for (int r = 0; r < 64; ++r) {
-            if (((r < 32 ? m0 : m1) >> (r & 31)) & 1u) {   // an event starts here: the running interval ends
-                if (open >= 0) dy[open] = acc;
-                open = (t0 + r < u.t_end) ? e : -1;
-                ++e;
-                acc = 0.f;
-            }
-            acc += v[r];
+            const bool hit = (((r < 32 ? m0 : m1) >> (r & 31)) & 1u) != 0u;
+            if (hit && open >= 0) dy[open] = acc;   // an event starts here: the running interval ends
+            open = hit ? ((t0 + r < u.t_end) ? e : -1) : open;
+            e += hit ? 1 : 0;
+            acc = (hit ? 0.f : acc) + v[r];
         }
     }
     if (open >= 0) dy[open] = acc;              // the interval runs to L
@@ -498,6 +534,29 @@ static int restore_part_len(int64_t n_blocks_2d, int64_t L) {
     return (int)std::min<int64_t>(len, std::max<int64_t>((L + kTT - 1) / kTT * kTT, kTT));
 }
 
+// Unit layout of the tile forward and the bitmap backward (shared, so that
+// the backward can read the forward's per-unit start indices): warp units of
+// 32 features x part_len positions (whole 64-row windows), as many as the SMs
+// hold at once (kSweepWarpsPerSM warps each), more only when the batch rows
+// alone exceed that.
+static SweepLayout sweep_layout(int64_t B, int64_t D, int64_t L) {
+    SweepLayout s;
+    s.n_dblk = (int)((D + 31) / 32);
+    const int64_t cols = B * s.n_dblk;
+    const int64_t cap = (int64_t)sm_count() * kSweepWarpsPerSM;
+    const int64_t parts = std::max<int64_t>(1, cap / std::max<int64_t>(1, cols));
+    int64_t len = (L + parts - 1) / parts;
+    len = std::max<int64_t>(kTW, (len + kTW - 1) / kTW * kTW);
+    s.part_len = (int)len;
+    s.n_parts = (int)((L + len - 1) / len);
+    s.n_units = cols * s.n_parts;
+    return s;
+}
+
+static size_t bitmap_words_bytes(int64_t n_channels, int64_t seqlen) {
+    return (size_t)n_channels * (size_t)((seqlen + 31) / 32) * sizeof(uint32_t);
+}
+
 static bcm_status restore_fwd_impl(const void* y_flat, bcm_dtype y_dtype, const int32_t* time_steps,
                                    const int32_t* cu_seqlens, int64_t n_events, int64_t n_channels,
                                    int64_t dim, int64_t seqlen, void* out, bcm_dtype out_dtype,
@@ -512,17 +571,19 @@ static bcm_status restore_fwd_impl(const void* y_flat, bcm_dtype y_dtype, const 
     BCM_REQUIRE(out && cu_seqlens && (n_events == 0 || (y_flat && time_steps)),
                 "restore_dense_fwd: null pointer");
     const int64_t B = n_channels / dim;
-    const int n_dblk = ceil_div(dim, kDB);
-    const int part_len = restore_part_len(B * n_dblk, seqlen);
-    const int n_parts = ceil_div(seqlen, part_len);
-    BCM_REQUIRE(B < 65536, "restore_dense_fwd: batch too large");
-    dim3 grid(n_dblk * n_parts, (unsigned)B);
+    const SweepLayout lay = sweep_layout(B, dim, seqlen);
+    BCM_REQUIRE((lay.n_units + kFW - 1) / kFW < (1ll << 31), "restore_dense_fwd: too many units");
+    const int nw = (int)((seqlen + 31) / 32);
+    // the per-unit start indices follow the bitmap words
+    int32_t* e_start = bitmap ? reinterpret_cast<int32_t*>(reinterpret_cast<char*>(bitmap) +
+                                                           bitmap_words_bytes(n_channels, seqlen))
+                              : nullptr;
     auto launch = [&](auto tin, auto tout) -> bcm_status {
         using Tin = decltype(tin);
         using Tout = decltype(tout);
-        restore_fwd_kernel<Tin, Tout><<<grid, kWarpsR * 32, 0, stream>>>(
-            static_cast<const Tin*>(y_flat), time_steps, cu_seqlens, (int)dim, (int)seqlen,
-            part_len, n_dblk, static_cast<Tout*>(out), bitmap);
+        restore_fwd_tile<Tin, Tout><<<(unsigned)((lay.n_units + kFW - 1) / kFW), kFW * 32, 0, stream>>>(
+            static_cast<const Tin*>(y_flat), time_steps, cu_seqlens, (int)dim, (int)seqlen, nw, lay.part_len,
+            lay.n_dblk, lay.n_parts, lay.n_units, static_cast<Tout*>(out), bitmap, e_start);
         BCM_LAUNCH_CHECK();
         return BCM_OK;
     };
@@ -556,38 +617,27 @@ extern "C" bcm_status bcm_restore_dense_fwd_bitmap(const void* y_flat, bcm_dtype
                             out, out_dtype, event_bitmap, stream);
 }
 
-extern "C" size_t bcm_restore_bitmap_bytes(int64_t n_channels, int64_t seqlen) {
-    if (n_channels < 0 || seqlen < 0) return 0;
-    return (size_t)n_channels * (size_t)((seqlen + 31) / 32) * sizeof(uint32_t);
+extern "C" size_t bcm_restore_bitmap_bytes(int64_t n_channels, int64_t dim, int64_t seqlen) {
+    if (n_channels < 0 || dim < 1 || seqlen < 1 || n_channels % dim != 0) return 0;
+    const SweepLayout lay = sweep_layout(n_channels / dim, dim, seqlen);
+    return bitmap_words_bytes(n_channels, seqlen) + (size_t)lay.n_units * 32 * sizeof(int32_t);
 }
 
 extern "C" size_t bcm_restore_workspace_bytes(int64_t n_channels, int64_t seqlen) {
-    return align_up(bcm_restore_bitmap_bytes(n_channels, seqlen), 256);
+    if (n_channels < 0 || seqlen < 0) return 0;
+    return align_up(bitmap_words_bytes(n_channels, seqlen), 256);
 }
 
-// Bitmap backward layout: warp units of 32 features x part_len positions,
-// enough to cover the SMs ~16 times; parts are whole 32-row windows.
-static void bitmap_layout(int64_t B, int64_t D, int64_t L, int& n_dblk, int& part_len, int& n_parts) {
-    n_dblk = (int)((D + 31) / 32);
-    const int64_t cols = B * n_dblk;
-    const int64_t target = (int64_t)sm_count() * 16;
-    const int64_t parts = std::max<int64_t>(1, (target + cols - 1) / cols);
-    int64_t len = (L + parts - 1) / parts;
-    len = std::max<int64_t>(64, (len + 31) / 32 * 32);
-    part_len = (int)len;
-    n_parts = (int)((L + len - 1) / len);
-}
 
-static bcm_status launch_bwd_bitmap(const void* dout, bcm_dtype dtype, const int32_t* cu_seqlens, int64_t B, int64_t dim, int64_t seqlen,
-                                    const uint32_t* bm, float* dy, cudaStream_t stream) {
-    int bd = 0, bpl = 0, bnp = 0;
-    bitmap_layout(B, dim, seqlen, bd, bpl, bnp);
-    const int64_t bunits = B * bd * bnp;
+static bcm_status launch_bwd_bitmap(const void* dout, bcm_dtype dtype, const int32_t* cu_seqlens, int64_t B,
+                                    int64_t dim, int64_t seqlen, const uint32_t* bm, const int32_t* e_start,
+                                    float* dy, cudaStream_t stream) {
+    const SweepLayout lay = sweep_layout(B, dim, seqlen);
     return dispatch_dtype(dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);
-        restore_bwd_bitmap<T><<<(unsigned)((bunits + kBU - 1) / kBU), kBU * 32, 0, stream>>>(
-            static_cast<const T*>(dout), cu_seqlens, bm, (int)dim, (int)seqlen,
-            (int)((seqlen + 31) / 32), bpl, bd, bnp, bunits, dy);
+        restore_bwd_bitmap<T><<<(unsigned)((lay.n_units + kBU - 1) / kBU), kBU * 32, 0, stream>>>(
+            static_cast<const T*>(dout), cu_seqlens, bm, e_start, (int)dim, (int)seqlen,
+            (int)((seqlen + 31) / 32), lay.part_len, lay.n_dblk, lay.n_parts, lay.n_units, dy);
         BCM_LAUNCH_CHECK();
         return BCM_OK;
     });
@@ -606,7 +656,10 @@ extern "C" bcm_status bcm_restore_dense_bwd_bitmap(const void* dout, bcm_dtype d
     BCM_REQUIRE(seqlen < (1ll << 31) - 2 * kTT, "restore_dense_bwd_bitmap: seqlen too large");
     if (n_events == 0 || n_channels == 0) return BCM_OK;
     BCM_REQUIRE(dout && time_steps && cu_seqlens && dy && event_bitmap, "restore_dense_bwd_bitmap: null pointer");
-    return launch_bwd_bitmap(dout, dtype, cu_seqlens, n_channels / dim, dim, seqlen, event_bitmap, dy, stream);
+    const int32_t* e_start = reinterpret_cast<const int32_t*>(reinterpret_cast<const char*>(event_bitmap) +
+                                                              bitmap_words_bytes(n_channels, seqlen));
+    return launch_bwd_bitmap(dout, dtype, cu_seqlens, n_channels / dim, dim, seqlen, event_bitmap, e_start, dy,
+                             stream);
 }
 
 extern "C" bcm_status bcm_restore_dense_bwd(const void* dout, bcm_dtype dtype,
@@ -638,7 +691,7 @@ extern "C" bcm_status bcm_restore_dense_bwd(const void* dout, bcm_dtype dtype,
     }
     if (use_bitmap)
         return launch_bwd_bitmap(dout, dtype, cu_seqlens, B, dim, seqlen,
-                                 static_cast<const uint32_t*>(workspace), dy, stream);
+                                 static_cast<const uint32_t*>(workspace), nullptr, dy, stream);
     return dispatch_dtype(dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);
         restore_bwd_kernel<T><<<grid, kWarpsR * 32, 0, stream>>>(

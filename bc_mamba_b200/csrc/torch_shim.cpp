@@ -577,7 +577,8 @@ std::vector<Tensor> dense_scan_unavailable(py::args, py::kwargs) {
 }
 
 // ---------------------------------------------------------------- restore ----
-// bitmap != nullptr: also returns the event bitmap (int32 [B, ceil(L/32), dim]) for restore_dense_bwd_bitmap
+// bitmap != nullptr: also returns the event bitmap words ([B, ceil(L/32), dim]) and the sweep's
+// per-unit start indices, one flat int32 buffer for restore_dense_bwd_bitmap
 Tensor restore_fwd_impl(const Tensor& y_flat, const Tensor& time_steps, const Tensor& cu_seqlens,
                         int64_t dim, int64_t seqlen, const optional<at::ScalarType> out_dtype_opt,
                         Tensor* bitmap) {
@@ -614,7 +615,9 @@ Tensor restore_fwd_impl(const Tensor& y_flat, const Tensor& time_steps, const Te
     const int64_t B = NC / dim;
     auto out = torch::empty({B, seqlen, dim}, y_flat.options().dtype(out_type));
     if (bitmap != nullptr) {
-        *bitmap = torch::empty({B, (seqlen + 31) / 32, dim}, y_flat.options().dtype(at::ScalarType::Int));
+        const int64_t words = (int64_t)bcm_restore_bitmap_bytes(NC, dim, seqlen) / 4;
+        TORCH_CHECK(words > 0, "restore_dense_fwd_bitmap: bad sizes");
+        *bitmap = torch::empty({words}, y_flat.options().dtype(at::ScalarType::Int));
         check_status(bcm_restore_dense_fwd_bitmap(y_flat.data_ptr(), to_bcm(input_type, "restore_dense_fwd"),
                                                   time_steps.data_ptr<int32_t>(), cu_seqlens.data_ptr<int32_t>(),
                                                   E, NC, dim, seqlen, out.data_ptr(),
@@ -696,9 +699,9 @@ Tensor restore_dense_bwd_bitmap(const Tensor& dout, const Tensor& time_steps, co
     const int64_t E = time_steps.size(0);
     TORCH_CHECK(dout.dim() == 3 && dout.size(1) == seqlen && dout.size(2) == dim && dout.size(0) * dim == NC,
                 "restore_dense_bwd_bitmap: dout must be (B, seqlen, dim) with B*dim = n_channels");
-    TORCH_CHECK(bitmap.dim() == 3 && bitmap.size(0) == dout.size(0) && bitmap.size(1) == (seqlen + 31) / 32 &&
-                    bitmap.size(2) == dim,
-                "restore_dense_bwd_bitmap: bitmap must be (B, ceil(seqlen/32), dim), from restore_dense_fwd_bitmap");
+    TORCH_CHECK(bitmap.dim() == 1 && bitmap.numel() * 4 == (int64_t)bcm_restore_bitmap_bytes(NC, dim, seqlen),
+                "restore_dense_bwd_bitmap: bitmap must be the buffer restore_dense_fwd_bitmap returned for these "
+                "sizes on this device");
     c10::cuda::CUDAGuard guard(dout.device());
     auto dy = torch::empty({E}, dout.options().dtype(at::ScalarType::Float));
     if (E == 0) return dy;
@@ -761,8 +764,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "Zero-order-hold restore (B, L, D) from flat events");
     m.def("restore_dense_fwd_bitmap", &restore_dense_fwd_bitmap, py::arg("y_flat"), py::arg("time_steps"),
           py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"), py::arg("out_dtype") = py::none(),
-          "restore_dense_fwd that also returns the event bitmap (int32 [B, ceil(L/32), dim]) "
-          "consumed by restore_dense_bwd_bitmap");
+          "restore_dense_fwd that also returns the event bitmap (the first B*ceil(L/32)*dim int32 words, "
+          "layout [B, ceil(L/32), dim]) and the sweep's start indices, consumed by restore_dense_bwd_bitmap");
     m.def("restore_dense_bwd_bitmap", &restore_dense_bwd_bitmap, py::arg("dout"), py::arg("time_steps"),
           py::arg("cu_seqlens"), py::arg("bitmap"), py::arg("dim"), py::arg("seqlen"),
           "Backward of restore_dense_fwd from the forward's event bitmap; returns dy_flat (float32)");

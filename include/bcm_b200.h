@@ -327,12 +327,14 @@ BCM_API bcm_status bcm_restore_dense_fwd(const void* y_flat, bcm_dtype y_dtype,
                                  void* out, bcm_dtype out_dtype,
                                  cudaStream_t stream);
 
-/* Forward that also writes the event bitmap (bit t%32 of word
- * [b][t/32][d] set where channel b*dim+d has an addressable event at t;
- * bcm_restore_bitmap_bytes bytes, every word written, no pre-zeroing) for
- * bcm_restore_dense_bwd_bitmap: the autograd pair keeps it between the two
- * passes so the backward needs neither the event times nor a bitmap pass. */
-BCM_API size_t bcm_restore_bitmap_bytes(int64_t n_channels, int64_t seqlen);
+/* Forward that also writes, for bcm_restore_dense_bwd_bitmap, the event
+ * bitmap (uint32 words [b][t/32][d], bit t%32 set where channel b*dim+d has
+ * an addressable event at t) followed by the local index of the first event
+ * of each work unit of the sweep (int32, one per unit and lane); the buffer
+ * is bcm_restore_bitmap_bytes bytes for the current device, every byte
+ * written, no pre-zeroing.  The autograd pair keeps it between the two
+ * passes so the backward needs neither the event times nor a search. */
+BCM_API size_t bcm_restore_bitmap_bytes(int64_t n_channels, int64_t dim, int64_t seqlen);
 BCM_API bcm_status bcm_restore_dense_fwd_bitmap(const void* y_flat, bcm_dtype y_dtype,
                                  const int32_t* time_steps,
                                  const int32_t* cu_seqlens,

@@ -44,10 +44,10 @@ def test_workspace_queries_without_gpu():
     lib.bcm_extract_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
     # one bit per base channel and position, plus a 256-byte {total, max} slot
     assert lib.bcm_extract_workspace_bytes(4096, 2048) == 4096 * 64 * 4 + 256
-    lib.bcm_restore_bitmap_bytes.restype = ctypes.c_size_t
-    lib.bcm_restore_bitmap_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
-    assert lib.bcm_restore_bitmap_bytes(8192, 2048) == 8192 * 64 * 4
-    assert lib.bcm_restore_bitmap_bytes(3, 33) == 3 * 2 * 4
+    lib.bcm_restore_workspace_bytes.restype = ctypes.c_size_t
+    lib.bcm_restore_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    assert lib.bcm_restore_workspace_bytes(8192, 2048) == 8192 * 64 * 4
+    assert lib.bcm_restore_workspace_bytes(3, 33) == 256
 
 
 def test_shim_exports_reference_entry_points():
