@@ -32,11 +32,13 @@ ABI_SYMBOLS = (
     "bcm_conv_events_fwd",
     "bcm_conv_events_bwd_workspace_bytes",
     "bcm_conv_events_bwd",
+    "bcm_flat_ch_ckpt_bytes",
     "bcm_flat_ch_fwd_workspace_bytes",
     "bcm_flat_ch_bwd_workspace_bytes",
     "bcm_flat_ch_fwd",
     "bcm_flat_ch_bwd",
     "bcm_extract_expand_fill",
+    "bcm_gather_events_bwd_rows",
     "bcm_restore_workspace_bytes",
     "bcm_restore_bitmap_bytes",
     "bcm_restore_dense_fwd_bitmap",

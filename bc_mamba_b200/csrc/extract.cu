@@ -209,12 +209,16 @@ mask_fill_kernel(const uint32_t* __restrict__ mask, const int32_t* __restrict__ 
 // expansion, without the base arrays): base channel c's events are written
 // `expand` times, copy r at s*expand + r*cnt + i as channel c*expand + r (the
 // layout expand_events_kernel produces), and the warp also writes the
-// expanded cu_seqlens entries of its channel.
+// expanded cu_seqlens entries of its channel.  With x (B, D, L) given it also
+// gathers x at every expanded event (x_flat[o] = x[channel][t], what
+// gather_kernel computes from the finished stream).
+template <typename T>
 __global__ void __launch_bounds__(kFillWarps * 32)
 mask_fill_expand_kernel(const uint32_t* __restrict__ mask, const int32_t* __restrict__ base_cu,
                         int64_t n_rows, int n_words, int expand,
                         int32_t* __restrict__ ch_ids, int32_t* __restrict__ t_steps,
-                        int32_t* __restrict__ k_flat, int32_t* __restrict__ cu) {
+                        int32_t* __restrict__ k_flat, int32_t* __restrict__ cu,
+                        const T* __restrict__ x, int L, T* __restrict__ x_flat) {
     __shared__ int s_t[kFillWarps][1024 + 1];
     const int lane = lane_id();
     const int w_in = threadIdx.x >> 5;
@@ -249,9 +253,11 @@ mask_fill_expand_kernel(const uint32_t* __restrict__ mask, const int32_t* __rest
             const int kv = (prev < 0) ? (t + 1) : (t - prev);
             for (int r = 0; r < expand; ++r) {
                 const int64_t o2 = out0 + (int64_t)r * cnt + local + i;
-                ch_ids[o2] = (int32_t)(row * expand + r);
+                const int64_t c2 = row * expand + r;
+                ch_ids[o2] = (int32_t)c2;
                 t_steps[o2] = t;
                 k_flat[o2] = kv;
+                if (x != nullptr) x_flat[o2] = x[c2 * L + t];
             }
         }
         __syncwarp();
@@ -346,7 +352,7 @@ dense_rows_kernel(const T* __restrict__ g, const int32_t* __restrict__ ts,
     constexpr int V = 16 / sizeof(T);
     constexpr int CH = 32 * V;             // positions per chunk
     __shared__ __align__(16) T s_chunk[4][CH];
-    if (*flag) return;
+    if (flag != nullptr && *flag) return;   // null: no bounds pass ran (rows from cu_seqlens)
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t r = (int64_t)blockIdx.x * 4 + w;
     if (r >= n_ch) return;
@@ -388,6 +394,79 @@ dense_rows_kernel(const T* __restrict__ g, const int32_t* __restrict__ ts,
     if (lane == 0 && e != e_end) atomicExch(flag_out, 1);  // events at t >= L
 }
 
+// Pass B for rows that fit in shared memory (the usual case): one warp per
+// row holds the whole row: it zeroes it, scatters all of the row's events
+// (coalesced 32-event loads, independent of one another, so their latencies
+// overlap) and writes the row out with 16-byte stores.  Same flag rule.
+constexpr int kRowWarps = 4;
+constexpr size_t kRowSmemMax = 48 * 1024;   // dynamic shared memory per CTA without opt-in
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kRowWarps * 32)
+dense_rows_smem_kernel(const T* __restrict__ g, const int32_t* __restrict__ ts,
+                       const int32_t* __restrict__ row_start, const int32_t* __restrict__ flag_in,
+                       int64_t n_ch, int L, int row_elems, T* __restrict__ dx, int32_t* __restrict__ flag_out) {
+    extern __shared__ __align__(16) unsigned char s_rows[];
+    constexpr int V = 16 / sizeof(T);
+    if (flag_in != nullptr && *flag_in) return;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + w;
+    if (r >= n_ch) return;
+    T* buf = reinterpret_cast<T*>(s_rows) + (size_t)w * row_elems;
+    for (int p = lane * V; p < row_elems; p += 32 * V) *reinterpret_cast<uint4*>(buf + p) = make_uint4(0, 0, 0, 0);
+    __syncwarp();
+    const int e_beg = row_start[r];
+    const int e_end = row_start[r + 1];
+    bool bad = false;
+    int prev = -1;   // last time of the previous 32 events (order check across steps)
+#pragma unroll 4
+    for (int j0 = e_beg; j0 < e_end; j0 += 32) {
+        const int j = j0 + lane;
+        const bool in = j < e_end;
+        const int t = in ? ts[j] : INT_MAX;
+        const T v = in ? g[j] : from_f32<T>(0.f);
+        int tp = __shfl_up_sync(kFull, t, 1);
+        if (lane == 0) tp = prev;
+        prev = __shfl_sync(kFull, t, 31);
+        if (in) {
+            if (t < 0 || t >= L || t <= tp) bad = true;
+            else buf[t] = v;
+        }
+    }
+    if (__any_sync(kFull, bad) && lane == 0) atomicExch(flag_out, 1);
+    __syncwarp();
+    T* row = dx + r * (int64_t)L;
+    if (VEC) {
+        for (int p = lane * V; p < L; p += 32 * V)
+            *reinterpret_cast<uint4*>(row + p) = *reinterpret_cast<const uint4*>(buf + p);
+    } else {
+        for (int p = lane; p < L; p += 32) row[p] = buf[p];
+    }
+}
+
+// Fallback of the rows variant (channel of an event given by cu_seqlens, not
+// channel_ids; runs only when *flag is set): every row is zeroed and its
+// events are written in stream order.
+template <typename T>
+__global__ void rows_fallback_kernel(const int32_t* __restrict__ flag, const T* __restrict__ g,
+                                     const int32_t* __restrict__ ts, const int32_t* __restrict__ row_start,
+                                     int64_t n_ch, int L, T* __restrict__ dx) {
+    if (!*flag) return;
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n_ch; r += warps) {
+        T* row = dx + r * (int64_t)L;
+        for (int p = lane; p < L; p += 32) row[p] = from_f32<T>(0.f);
+        __syncwarp();
+        if (lane == 0)
+            for (int j = row_start[r]; j < row_start[r + 1]; ++j) {
+                const int t = ts[j];
+                if (t >= 0 && t < L) row[t] = g[j];
+            }
+        __syncwarp();
+    }
+}
+
 // Fallback for any other event order (runs only when *flag is set):
 // zero-fill, then scatter in stream order (reference
 // extract_events_cuda.cu:649-662, 731).
@@ -409,6 +488,38 @@ __global__ void fallback_scatter_kernel(const int32_t* __restrict__ flag, const 
         const int c = ch[e], t = ts[e];
         if (c >= 0 && c < n_ch && t >= 0 && t < L) dx[(int64_t)c * L + t] = g[e];
     }
+}
+
+// Pass B launch: whole rows in shared memory when a row fits (kRowSmemMax per
+// CTA), else the chunked kernel.
+template <typename T>
+bcm_status launch_dense_rows(const T* g, const int32_t* ts, const int32_t* row_start, const int32_t* flag_in,
+                             int64_t n_ch, int64_t L, T* dx, int32_t* flag_out, cudaStream_t stream) {
+    constexpr int V = 16 / sizeof(T);
+    const bool vec = (L % V == 0) && (reinterpret_cast<uintptr_t>(dx) % 16 == 0);
+    const int64_t row_elems = (L + V - 1) / V * V;
+    const size_t row_bytes = (size_t)row_elems * sizeof(T);
+    if (row_bytes <= kRowSmemMax) {
+        const int warps = (int)std::min<size_t>(kRowWarps, kRowSmemMax / row_bytes);
+        const unsigned grid = (unsigned)((n_ch + warps - 1) / warps);
+        const size_t smem = row_bytes * warps;
+        if (vec)
+            dense_rows_smem_kernel<T, true><<<grid, warps * 32, smem, stream>>>(
+                g, ts, row_start, flag_in, n_ch, (int)L, (int)row_elems, dx, flag_out);
+        else
+            dense_rows_smem_kernel<T, false><<<grid, warps * 32, smem, stream>>>(
+                g, ts, row_start, flag_in, n_ch, (int)L, (int)row_elems, dx, flag_out);
+    } else {
+        const int rows_grid = ceil_div(n_ch, 4);
+        if (vec)
+            dense_rows_kernel<T, true><<<rows_grid, 128, 0, stream>>>(g, ts, row_start, flag_in, n_ch, (int)L,
+                                                                      dx, flag_out);
+        else
+            dense_rows_kernel<T, false><<<rows_grid, 128, 0, stream>>>(g, ts, row_start, flag_in, n_ch, (int)L,
+                                                                       dx, flag_out);
+    }
+    BCM_LAUNCH_CHECK();
+    return BCM_OK;
 }
 
 inline int grid_for(int64_t n, int threads) {
@@ -598,6 +709,7 @@ extern "C" bcm_status bcm_extract_expand_fill(int64_t n_base_channels, int64_t s
                                               const int32_t* base_cu_seqlens, const void* workspace,
                                               size_t workspace_bytes, int64_t expand, int32_t* ch_ids,
                                               int32_t* t_steps, int32_t* k_flat, int32_t* cu_seqlens,
+                                              const void* x, bcm_dtype x_dtype, void* x_flat,
                                               cudaStream_t stream) {
     clear_error();
     BCM_REQUIRE(n_base_channels >= 0 && seqlen >= 0, "extract_expand_fill: negative size");
@@ -610,14 +722,26 @@ extern "C" bcm_status bcm_extract_expand_fill(int64_t n_base_channels, int64_t s
         return BCM_ERR_WORKSPACE;
     }
     BCM_REQUIRE(seqlen == 0 || (ch_ids && t_steps && k_flat), "extract_expand_fill: null pointer");
+    BCM_REQUIRE((x == nullptr) == (x_flat == nullptr), "extract_expand_fill: x and x_flat go together");
     const int L = (int)seqlen;
     const int n_words = (L + 31) / 32;
     const int grid = ceil_div(n_base_channels, kFillWarps);
-    mask_fill_expand_kernel<<<grid, kFillWarps * 32, 0, stream>>>(
-        static_cast<const uint32_t*>(workspace), base_cu_seqlens, n_base_channels, n_words, (int)expand,
-        ch_ids, t_steps, k_flat, cu_seqlens);
-    BCM_LAUNCH_CHECK();
-    return BCM_OK;
+    if (x == nullptr) {
+        mask_fill_expand_kernel<float><<<grid, kFillWarps * 32, 0, stream>>>(
+            static_cast<const uint32_t*>(workspace), base_cu_seqlens, n_base_channels, n_words, (int)expand,
+            ch_ids, t_steps, k_flat, cu_seqlens, nullptr, L, nullptr);
+        BCM_LAUNCH_CHECK();
+        return BCM_OK;
+    }
+    BCM_REQUIRE(dtype_ok64(x_dtype), "extract_expand_fill: unsupported x dtype %d", (int)x_dtype);
+    return dispatch_dtype64(x_dtype, [&](auto tag) -> bcm_status {
+        using T = decltype(tag);
+        mask_fill_expand_kernel<T><<<grid, kFillWarps * 32, 0, stream>>>(
+            static_cast<const uint32_t*>(workspace), base_cu_seqlens, n_base_channels, n_words, (int)expand,
+            ch_ids, t_steps, k_flat, cu_seqlens, static_cast<const T*>(x), L, static_cast<T*>(x_flat));
+        BCM_LAUNCH_CHECK();
+        return BCM_OK;
+    });
 }
 
 extern "C" bcm_status bcm_expand_base_events(const int32_t* base_ch_ids,
@@ -720,18 +844,9 @@ extern "C" bcm_status bcm_gather_events_bwd(const void* grad, bcm_dtype dtype,
     BCM_LAUNCH_CHECK();
     return dispatch_dtype64(dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);
-        constexpr int V = 16 / sizeof(T);
-        const bool vec = (seqlen % V == 0) && (reinterpret_cast<uintptr_t>(dx) % 16 == 0);
-        const int rows_grid = ceil_div(n_channels, 4);
-        if (vec)
-            dense_rows_kernel<T, true><<<rows_grid, 128, 0, stream>>>(
-                static_cast<const T*>(grad), time_steps, row_start, flag, n_channels, (int)seqlen,
-                static_cast<T*>(dx), flag);
-        else
-            dense_rows_kernel<T, false><<<rows_grid, 128, 0, stream>>>(
-                static_cast<const T*>(grad), time_steps, row_start, flag, n_channels, (int)seqlen,
-                static_cast<T*>(dx), flag);
-        BCM_LAUNCH_CHECK();
+        const bcm_status st = launch_dense_rows<T>(static_cast<const T*>(grad), time_steps, row_start, flag,
+                                                   n_channels, seqlen, static_cast<T*>(dx), flag, stream);
+        if (st != BCM_OK) return st;
         const int fb_grid = sm_count() * 2;
         fallback_zero_kernel<T><<<fb_grid, threads, 0, stream>>>(flag, static_cast<T*>(dx),
                                                                  (int64_t)n_channels * seqlen);
@@ -739,6 +854,43 @@ extern "C" bcm_status bcm_gather_events_bwd(const void* grad, bcm_dtype dtype,
         fallback_scatter_kernel<T><<<fb_grid, threads, 0, stream>>>(
             flag, static_cast<const T*>(grad), channel_ids, time_steps, n_events, n_channels,
             (int)seqlen, static_cast<T*>(dx));
+        BCM_LAUNCH_CHECK();
+        return BCM_OK;
+    });
+}
+
+extern "C" bcm_status bcm_gather_events_bwd_rows(const void* grad, bcm_dtype dtype,
+                                                 const int32_t* time_steps, const int32_t* cu_seqlens,
+                                                 int64_t n_events, int64_t n_channels, int64_t seqlen,
+                                                 void* dx, void* workspace, size_t workspace_bytes,
+                                                 cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(dtype_ok64(dtype), "gather_events_bwd_rows: unsupported dtype %d", (int)dtype);
+    BCM_REQUIRE(n_events >= 0 && n_channels >= 0 && seqlen >= 0, "gather_events_bwd_rows: negative size");
+    BCM_REQUIRE(n_events < (1ll << 31) && seqlen < (1ll << 31), "gather_events_bwd_rows: sizes exceed int32");
+    const size_t bytes = (size_t)n_channels * (size_t)seqlen * dtype_size(dtype);
+    if (bytes == 0) return BCM_OK;
+    BCM_REQUIRE(dx, "gather_events_bwd_rows: null dx");
+    if (n_events == 0) {
+        BCM_CUDA_TRY(cudaMemsetAsync(dx, 0, bytes, stream));
+        return BCM_OK;
+    }
+    BCM_REQUIRE(grad && time_steps && cu_seqlens, "gather_events_bwd_rows: null pointer");
+    if (!workspace || workspace_bytes < (size_t)BCM_GATHER_BWD_ROWS_WORKSPACE) {
+        set_error("gather_events_bwd_rows: workspace of %zu bytes < required %zu", workspace_bytes,
+                  (size_t)BCM_GATHER_BWD_ROWS_WORKSPACE);
+        return BCM_ERR_WORKSPACE;
+    }
+    int32_t* flag = static_cast<int32_t*>(workspace);
+    BCM_CUDA_TRY(cudaMemsetAsync(flag, 0, sizeof(int32_t), stream));
+    return dispatch_dtype64(dtype, [&](auto tag) -> bcm_status {
+        using T = decltype(tag);
+        const bcm_status st = launch_dense_rows<T>(static_cast<const T*>(grad), time_steps, cu_seqlens, nullptr,
+                                                   n_channels, seqlen, static_cast<T*>(dx), flag, stream);
+        if (st != BCM_OK) return st;
+        rows_fallback_kernel<T><<<sm_count() * 2, 256, 0, stream>>>(flag, static_cast<const T*>(grad), time_steps,
+                                                                     cu_seqlens, n_channels, (int)seqlen,
+                                                                     static_cast<T*>(dx));
         BCM_LAUNCH_CHECK();
         return BCM_OK;
     });

@@ -32,6 +32,8 @@ struct ScanArgs {
     void* du; float* dB_ev; float* dC_ev;  // per-event dB/dC (flat variable / tiled)
     void* dz;
     float* ws_ckpt;   // backward: recompute checkpoints
+    float* ckpt;      // staged kernels: the forward writes the checkpoints here and the
+                      // backward reads them instead of recomputing (nullable)
     float* ws_part;   // backward: per-channel parameter-gradient partials
     int part_stride;  // floats per channel in ws_part
 };
@@ -132,5 +134,10 @@ bcm_status dw_fast_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStre
 // of one feature fill whole warps; dw_fast_launch prefers them.
 bool v3_supported(const ScanArgs& a, bool bwd);
 bcm_status v3_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t st);
+// Floats per checkpoint slot of the staged kernels (dstate padded), and the
+// checkpoint buffer size shared by their forward and backward (0 when either
+// does not apply, in which case ScanArgs::ckpt must be null).
+int v3_ckpt_np(int dstate);
+size_t v3_ckpt_bytes(const ScanArgs& a);
 
 }  // namespace bcm

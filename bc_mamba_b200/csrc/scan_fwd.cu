@@ -285,6 +285,8 @@ void scan_fill_args(const bcm_flat_ch_args* p, ScanArgs& a) {
     a.dout = p->dout; a.out_fwd = p->out_fwd;
     a.du = p->du; a.dB_ev = nullptr; a.dC_ev = nullptr; a.dz = p->dz;
     a.ws_ckpt = nullptr; a.ws_part = nullptr; a.part_stride = 0;
+    a.ckpt = nullptr;
+    if (p->ckpt != nullptr && v3_ckpt_bytes(a) > 0) a.ckpt = p->ckpt;   // else ignored
 }
 
 bcm_status scan_launch_pw_mix(const bcm_flat_ch_args* p, float* WB_eff, float* WC_eff,
@@ -307,6 +309,13 @@ using namespace bcm;
 extern "C" size_t bcm_flat_ch_fwd_workspace_bytes(const bcm_flat_ch_args* p) {
     if (!p || p->pw_B == nullptr) return 0;
     return align_up((size_t)(2 * p->dim * p->dstate * sizeof(float)), 256);
+}
+
+extern "C" size_t bcm_flat_ch_ckpt_bytes(const bcm_flat_ch_args* p) {
+    if (!p || p->n_events <= 0 || p->n_channels <= 0 || p->dim <= 0 || p->dstate <= 0) return 0;
+    ScanArgs a;
+    scan_fill_args(p, a);
+    return v3_ckpt_bytes(a);
 }
 
 extern "C" bcm_status bcm_flat_ch_fwd(const bcm_flat_ch_args* p, cudaStream_t stream) {

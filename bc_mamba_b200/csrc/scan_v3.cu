@@ -242,7 +242,10 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
     const float Dv = a.D ? a.D[d] : 0.f;
     const T* u = static_cast<const T*>(a.u);
     const T* dout = static_cast<const T*>(a.dout);
-    float* ck = a.ws_ckpt + ((int64_t)(beg >> 3) + ch) * NP + q * G;
+    // checkpoints: the forward's (slots by event index over the whole
+    // channel), else this kernel's pass 1 (slots by index inside the chunk)
+    const bool fwd_ck = a.ckpt != nullptr;
+    float* const ck0 = (fwd_ck ? a.ckpt : a.ws_ckpt) + ((int64_t)(beg >> 3) + ch) * NP + q * G;
 
     // decays of one event: table row (row 0 = identity for padding slots);
     // EXACT batches send real events outside the table to exp2 in double
@@ -286,9 +289,10 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
 #pragma unroll
         for (int g = 0; g < G; ++g) SA[g] = SB[g] = QE[g] = 0.f;
         float c_ddi = 0.f, c_dda = 0.f, c_dD = 0.f;
+        float* const ck = fwd_ck ? ck0 + (int64_t)(cs >> 3) * NP : ck0;
 
         // ---- pass 1: checkpoints of the chunk -----------------------------
-        {
+        if (!fwd_ck) {
             float eta[G];
 #pragma unroll
             for (int g = 0; g < G; ++g) {
@@ -641,6 +645,13 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
 #pragma unroll
     for (int c = 0; c < CPW; ++c) sd[c] = 0.f;
 
+    // checkpoints for the backward: the state entering events 0, 8, 16, ...
+    // of the channel (slot j/8 of the channel's region)
+    float* ckb = nullptr;
+    if (a.ckpt != nullptr) {
+        ckb = a.ckpt + ((int64_t)(s_beg[grp] >> 3) + ch) * NP + s0;
+        if (n > 0) sts_vec<G>(ckb, eta);
+    }
     const T* u = static_cast<const T*>(a.u);
     float pu[CPW];
     int pk[CPW];
@@ -685,6 +696,8 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
 #pragma unroll
                 for (int g = 0; g < G; ++g) eta[g] = fmaf(dec[g], eta[g], w0);
                 sts_vec<G>(erow + i * EP, eta);
+                if (ckb != nullptr && (i & 7) == 7 && j0 + i + 1 < n)
+                    sts_vec<G>(ckb + (int64_t)((j0 + i + 1) >> 3) * NP, eta);
 #pragma unroll
                 for (int g = 0; g < G; ++g) dec[g] = dn[g];
                 w0 = w1;
@@ -713,6 +726,8 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
 #pragma unroll
                 for (int g = 0; g < G; ++g) eta[g] = fmaf(dec[g], eta[g], w);
                 sts_vec<G>(erow + i * EP, eta);
+                if (ckb != nullptr && (i & 7) == 7 && j0 + i + 1 < n)
+                    sts_vec<G>(ckb + (int64_t)((j0 + i + 1) >> 3) * NP, eta);
             }
         }
         // chunk state after a chunk end or after the channel's last event
@@ -856,6 +871,15 @@ bool v3_supported(const ScanArgs& a, bool bwd) {
     static const int mode = env_int("BCM_SCAN_V3", 1);
     if (mode == 0 || a.dstate > 64 || a.dim <= 0 || a.n_channels % a.dim != 0) return false;
     return (a.n_channels / a.dim) % channels_per_warp(a.dstate, bwd) == 0;
+}
+
+int v3_ckpt_np(int dstate) { return padded_states(dstate); }
+
+size_t v3_ckpt_bytes(const ScanArgs& a) {
+    if (a.bc_mode != BCM_BC_DEPTHWISE || a.n_events <= 0 || !v3_supported(a, false) || !v3_supported(a, true))
+        return 0;
+    const size_t slots = (size_t)(a.n_events >> 3) + (size_t)a.n_channels + 1;
+    return slots * (size_t)padded_states(a.dstate) * sizeof(float);
 }
 
 bcm_status v3_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t st) {

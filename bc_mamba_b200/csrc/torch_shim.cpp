@@ -58,10 +58,12 @@ Tensor workspace(int64_t bytes, const at::Device& dev) {
 // count pass (the given call) + fill, shared by both input layouts; the
 // count call also brings the maximum per-channel count to the host (max_host)
 // expand > 0: the fill writes the expanded stream directly (ch, ts, kf,
-// expanded cu, max) instead of the base stream (ch, ts, kf, cu, counts, max)
+// expanded cu, max) instead of the base stream (ch, ts, kf, cu, counts, max),
+// and with x_conv (B, D, L) also the gather of x_conv at it (sixth output)
 template <typename CountFn>
 std::vector<Tensor> extract_with(const Tensor& like, int64_t NCb, int64_t L, CountFn count, const char* what,
-                                 int32_t* max_host = nullptr, int64_t expand = 0) {
+                                 int32_t* max_host = nullptr, int64_t expand = 0,
+                                 const Tensor* x_conv = nullptr) {
     c10::cuda::CUDAGuard guard(like.device());
     auto opt_i = torch::TensorOptions().dtype(torch::kInt32).device(like.device());
     auto counts = torch::empty({NCb}, opt_i);
@@ -78,14 +80,21 @@ std::vector<Tensor> extract_with(const Tensor& like, int64_t NCb, int64_t L, Cou
         auto ts = torch::empty({E * expand}, opt_i);
         auto kf = torch::empty({E * expand}, opt_i);
         auto cu_x = torch::empty({NCb * expand + 1}, opt_i);
+        Tensor x_flat;
+        if (x_conv != nullptr) x_flat = torch::empty({E * expand}, x_conv->options());
         if (E == 0) {
             cu_x.zero_();
+            if (x_conv != nullptr) return {ch, ts, kf, cu_x, torch::zeros({1}, opt_i), x_flat};
             return {ch, ts, kf, cu_x, torch::zeros({1}, opt_i)};
         }
         check_status(bcm_extract_expand_fill(NCb, L, cu.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), expand,
                                              ch.data_ptr<int32_t>(), ts.data_ptr<int32_t>(),
-                                             kf.data_ptr<int32_t>(), cu_x.data_ptr<int32_t>(), cur_stream()),
+                                             kf.data_ptr<int32_t>(), cu_x.data_ptr<int32_t>(),
+                                             x_conv ? x_conv->data_ptr() : nullptr,
+                                             x_conv ? to_bcm(x_conv->scalar_type(), what) : BCM_F32,
+                                             x_conv ? x_flat.data_ptr() : nullptr, cur_stream()),
                      what);
+        if (x_conv != nullptr) return {ch, ts, kf, cu_x, mx, x_flat};
         return {ch, ts, kf, cu_x, mx};
     }
     if (E == 0) {
@@ -104,7 +113,7 @@ std::vector<Tensor> extract_with(const Tensor& like, int64_t NCb, int64_t L, Cou
 }
 
 std::vector<Tensor> extract_base_events_impl(const Tensor& base_input, double threshold, int32_t* max_host,
-                                             int64_t expand = 0) {
+                                             int64_t expand = 0, const Tensor* x_conv = nullptr) {
     TORCH_CHECK(base_input.is_cuda(), "base_input must be CUDA");
     TORCH_CHECK(base_input.is_contiguous(), "base_input must be contiguous");
     TORCH_CHECK(base_input.dim() == 3, "base_input must be 3-D [B, d_model, L]");
@@ -118,7 +127,7 @@ std::vector<Tensor> extract_base_events_impl(const Tensor& base_input, double th
                                                           mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), E,
                                                           mh, cur_stream());
                         },
-                        "extract_base_events", max_host, expand);
+                        "extract_base_events", max_host, expand, x_conv);
 }
 
 std::vector<Tensor> extract_base_events_fwd(Tensor base_input, double threshold) {
@@ -127,7 +136,7 @@ std::vector<Tensor> extract_base_events_fwd(Tensor base_input, double threshold)
 
 // Same outputs from the (B, L, d_model) layout (no transposed copy).
 std::vector<Tensor> extract_base_events_bld_impl(const Tensor& x, double threshold, int32_t* max_host,
-                                                 int64_t expand = 0) {
+                                                 int64_t expand = 0, const Tensor* x_conv = nullptr) {
     TORCH_CHECK(x.is_cuda(), "x must be CUDA");
     TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
     TORCH_CHECK(x.dim() == 3, "x must be 3-D [B, L, d_model]");
@@ -141,7 +150,7 @@ std::vector<Tensor> extract_base_events_bld_impl(const Tensor& x, double thresho
                                                               mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), E,
                                                               mh, cur_stream());
                         },
-                        "extract_base_events_bld", max_host, expand);
+                        "extract_base_events_bld", max_host, expand, x_conv);
 }
 
 std::vector<Tensor> extract_base_events_bld_fwd(Tensor x, double threshold) {
@@ -164,11 +173,22 @@ std::tuple<std::vector<Tensor>, int64_t> extract_base_events_host_max(Tensor bas
 // expand) and the maximum per-channel count as a host integer (the one
 // synchronisation of the count pass); bld selects the (B, L, d_model) layout.
 std::tuple<std::vector<Tensor>, int64_t> extract_expanded_events(Tensor x, double threshold, int64_t expand,
-                                                                  bool bld) {
+                                                                  bool bld, const optional<Tensor>& x_conv) {
     TORCH_CHECK(expand >= 1, "extract_expanded_events: expand must be >= 1");
+    const Tensor* xc = nullptr;
+    if (x_conv.has_value() && x_conv->defined()) {
+        const Tensor& v = *x_conv;
+        TORCH_CHECK(v.is_cuda() && v.is_contiguous() && v.dim() == 3,
+                    "extract_expanded_events: x_conv must be a contiguous CUDA (B, D, L) tensor");
+        TORCH_CHECK(x.dim() == 3 && v.device() == x.device(), "extract_expanded_events: x_conv on x's device");
+        const int64_t B = x.size(0), L = bld ? x.size(1) : x.size(2), d_model = bld ? x.size(2) : x.size(1);
+        TORCH_CHECK(v.size(0) == B && v.size(1) == d_model * expand && v.size(2) == L,
+                    "extract_expanded_events: x_conv must be (B, d_model*expand, L)");
+        xc = &v;
+    }
     int32_t mh = 0;
-    auto r = bld ? extract_base_events_bld_impl(x, threshold, &mh, expand)
-                 : extract_base_events_impl(x, threshold, &mh, expand);
+    auto r = bld ? extract_base_events_bld_impl(x, threshold, &mh, expand, xc)
+                 : extract_base_events_impl(x, threshold, &mh, expand, xc);
     return {r, (int64_t)mh};
 }
 
@@ -246,6 +266,26 @@ std::vector<Tensor> gather_events_bwd(Tensor grad_x, Tensor channel_ids, Tensor 
                                        NC, L, dx.data_ptr(), ws.data_ptr(), ws.numel(), cur_stream()),
                  "gather_events_bwd");
     return {dx};
+}
+
+// dx[NC, L] from a stream in extraction order and its cu_seqlens (no
+// channel_ids pass): the gather autograd function's backward.
+Tensor gather_events_bwd_rows(Tensor grad_x, Tensor time_steps, Tensor cu_seqlens, int64_t NC, int64_t L) {
+    TORCH_CHECK(grad_x.is_cuda(), "gather_events_bwd_rows: grad tensor must be CUDA");
+    TORCH_CHECK(time_steps.scalar_type() == torch::kInt32 && cu_seqlens.scalar_type() == torch::kInt32,
+                "gather_events_bwd_rows: time_steps / cu_seqlens must be int32");
+    TORCH_CHECK(cu_seqlens.numel() == NC + 1, "gather_events_bwd_rows: cu_seqlens must have NC + 1 entries");
+    c10::cuda::CUDAGuard guard(grad_x.device());
+    auto g = grad_x.contiguous();
+    auto dx = torch::empty({NC, L}, g.options());
+    auto ts = time_steps.contiguous();
+    auto cu = cu_seqlens.contiguous();
+    Tensor ws = workspace(BCM_GATHER_BWD_ROWS_WORKSPACE, g.device());
+    check_status(bcm_gather_events_bwd_rows(g.data_ptr(), to_bcm(g.scalar_type(), "gather_events_bwd_rows"),
+                                            ts.data_ptr<int32_t>(), cu.data_ptr<int32_t>(), g.size(0), NC, L,
+                                            dx.data_ptr(), ws.data_ptr(), ws.numel(), cur_stream()),
+                 "gather_events_bwd_rows");
+    return dx;
 }
 
 // ------------------------------------------------------------- conv at events
@@ -457,12 +497,14 @@ void prep_scan(ScanPrep& P, const char* fn, const Tensor& u_flat, const Tensor& 
     a.pw_C = P.has_pw ? P.pwC.data_ptr<float>() : nullptr;
 }
 
-std::vector<Tensor> selective_scan_fwd_flat_ch(
+// with_ckpt: the result gets one more entry, the state checkpoints for the
+// backward (empty where the staged kernels do not run)
+std::vector<Tensor> selective_scan_fwd_flat_ch_impl(
     const Tensor& u_flat, const Tensor& k_flat, const Tensor& cu_seqlens, const int64_t max_seqlen,
     const Tensor& dt_idle, const Tensor& dt_active, const Tensor& A, const Tensor& B,
     const Tensor& C, const optional<Tensor>& D_, const optional<Tensor>& z_,
     const optional<Tensor>& tile_offsets_, const int64_t tile_chunk_size, const bool is_depthwise_bc,
-    const optional<Tensor>& pw_B_, const optional<Tensor>& pw_C_) {
+    const optional<Tensor>& pw_B_, const optional<Tensor>& pw_C_, bool with_ckpt) {
     (void)tile_chunk_size;  // the kernel derives the tile stride from max_seqlen, as the reference
     ScanPrep P;
     prep_scan(P, "selective_scan_fwd_flat_ch", u_flat, k_flat, cu_seqlens, max_seqlen, dt_idle,
@@ -482,10 +524,39 @@ std::vector<Tensor> selective_scan_fwd_flat_ch(
     Tensor ws = workspace((int64_t)bcm_flat_ch_fwd_workspace_bytes(&a), u_flat.device());
     a.workspace = ws.data_ptr();
     a.workspace_bytes = ws.numel();
+    Tensor ckpt;
+    if (with_ckpt) {
+        const int64_t ck_bytes = (int64_t)bcm_flat_ch_ckpt_bytes(&a);
+        ckpt = torch::empty({ck_bytes / 4}, u_flat.options().dtype(torch::kFloat32));
+        a.ckpt = ck_bytes > 0 ? ckpt.data_ptr<float>() : nullptr;
+    }
     check_status(bcm_flat_ch_fwd(&a, cur_stream()), "selective_scan_fwd_flat_ch");
     std::vector<Tensor> result = {out, x};
     if (P.has_z) result.push_back(out_z);
+    if (with_ckpt) result.push_back(ckpt);
     return result;
+}
+
+std::vector<Tensor> selective_scan_fwd_flat_ch(
+    const Tensor& u_flat, const Tensor& k_flat, const Tensor& cu_seqlens, const int64_t max_seqlen,
+    const Tensor& dt_idle, const Tensor& dt_active, const Tensor& A, const Tensor& B,
+    const Tensor& C, const optional<Tensor>& D_, const optional<Tensor>& z_,
+    const optional<Tensor>& tile_offsets_, const int64_t tile_chunk_size, const bool is_depthwise_bc,
+    const optional<Tensor>& pw_B_, const optional<Tensor>& pw_C_) {
+    return selective_scan_fwd_flat_ch_impl(u_flat, k_flat, cu_seqlens, max_seqlen, dt_idle, dt_active, A, B, C,
+                                           D_, z_, tile_offsets_, tile_chunk_size, is_depthwise_bc, pw_B_, pw_C_,
+                                           false);
+}
+
+std::vector<Tensor> selective_scan_fwd_flat_ch_ckpt(
+    const Tensor& u_flat, const Tensor& k_flat, const Tensor& cu_seqlens, const int64_t max_seqlen,
+    const Tensor& dt_idle, const Tensor& dt_active, const Tensor& A, const Tensor& B,
+    const Tensor& C, const optional<Tensor>& D_, const optional<Tensor>& z_,
+    const optional<Tensor>& tile_offsets_, const int64_t tile_chunk_size, const bool is_depthwise_bc,
+    const optional<Tensor>& pw_B_, const optional<Tensor>& pw_C_) {
+    return selective_scan_fwd_flat_ch_impl(u_flat, k_flat, cu_seqlens, max_seqlen, dt_idle, dt_active, A, B, C,
+                                           D_, z_, tile_offsets_, tile_chunk_size, is_depthwise_bc, pw_B_, pw_C_,
+                                           true);
 }
 
 std::vector<Tensor> selective_scan_bwd_flat_ch(
@@ -494,7 +565,7 @@ std::vector<Tensor> selective_scan_bwd_flat_ch(
     const Tensor& C, const Tensor& dout_flat, const Tensor& x, const optional<Tensor>& D_,
     const optional<Tensor>& z_, const optional<Tensor>& out_, const optional<Tensor>& tile_offsets_,
     const int64_t tile_chunk_size, const bool is_depthwise_bc, const optional<Tensor>& pw_B_,
-    const optional<Tensor>& pw_C_) {
+    const optional<Tensor>& pw_C_, const optional<Tensor>& ckpt_) {
     (void)tile_chunk_size;
     const char* fn = "selective_scan_bwd_flat_ch";
     TORCH_CHECK(dout_flat.scalar_type() == u_flat.scalar_type(), fn, ": dout_flat must match u_flat dtype");
@@ -558,6 +629,13 @@ std::vector<Tensor> selective_scan_bwd_flat_ch(
     Tensor ws = workspace((int64_t)bcm_flat_ch_bwd_workspace_bytes(&a), u_flat.device());
     a.workspace = ws.data_ptr();
     a.workspace_bytes = ws.numel();
+    if (ckpt_.has_value() && ckpt_->defined() && ckpt_->numel() > 0) {
+        const Tensor& ck = *ckpt_;
+        TORCH_CHECK(ck.is_cuda() && ck.scalar_type() == at::ScalarType::Float && ck.is_contiguous() &&
+                        ck.numel() * 4 == (int64_t)bcm_flat_ch_ckpt_bytes(&a),
+                    fn, ": ckpt must be the checkpoints fwd_flat_ch_ckpt returned for these inputs");
+        a.ckpt = ck.data_ptr<float>();
+    }
     check_status(bcm_flat_ch_bwd(&a, cur_stream()), fn);
     std::vector<Tensor> result = {du, dA, dB, dC, ddt_idle, ddt_active};
     if (D_.has_value()) result.push_back(dD);
@@ -728,13 +806,23 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("tile_chunk_size") = 0, py::arg("is_depthwise_bc") = false,
           py::arg("pw_B") = py::none(), py::arg("pw_C") = py::none(),
           "Selective scan forward (flat per-channel, jagged layout)");
+    m.def("fwd_flat_ch_ckpt", &selective_scan_fwd_flat_ch_ckpt, py::arg("u_flat"), py::arg("k_flat"),
+          py::arg("cu_seqlens"), py::arg("max_seqlen"), py::arg("dt_idle"), py::arg("dt_active"),
+          py::arg("A"), py::arg("B"), py::arg("C"), py::arg("D") = py::none(),
+          py::arg("z") = py::none(), py::arg("tile_offsets") = py::none(),
+          py::arg("tile_chunk_size") = 0, py::arg("is_depthwise_bc") = false,
+          py::arg("pw_B") = py::none(), py::arg("pw_C") = py::none(),
+          "fwd_flat_ch whose result ends with the state checkpoints for bwd_flat_ch(ckpt=...) "
+          "(an empty tensor where they do not apply)");
     m.def("bwd_flat_ch", &selective_scan_bwd_flat_ch, py::arg("u_flat"), py::arg("k_flat"),
           py::arg("cu_seqlens"), py::arg("max_seqlen"), py::arg("dt_idle"), py::arg("dt_active"),
           py::arg("A"), py::arg("B"), py::arg("C"), py::arg("dout_flat"), py::arg("x"),
           py::arg("D") = py::none(), py::arg("z") = py::none(), py::arg("out") = py::none(),
           py::arg("tile_offsets") = py::none(), py::arg("tile_chunk_size") = 0,
           py::arg("is_depthwise_bc") = false, py::arg("pw_B") = py::none(),
-          py::arg("pw_C") = py::none(), "Selective scan backward (flat per-channel, jagged layout)");
+          py::arg("pw_C") = py::none(), py::arg("ckpt") = py::none(),
+          "Selective scan backward (flat per-channel, jagged layout); ckpt: the checkpoints "
+          "fwd_flat_ch_ckpt returned for the same inputs");
     // extract_events_cuda
     m.def("extract_events", &extract_events_fwd, "bool mask -> (ch_ids, t_steps, k_flat, cu_seqlens, max_seqlen, head_flags)");
     m.def("extract_base_events", &extract_base_events_fwd,
@@ -743,9 +831,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("bld") = false,
           "extract_base_events (bld: from the (B, L, d_model) layout) -> (6 outputs, max count as a host int)");
     m.def("extract_expanded_events", &extract_expanded_events, py::arg("x"), py::arg("threshold"),
-          py::arg("expand"), py::arg("bld") = false,
-          "extract_base_events then expand_base_events in one fill pass -> ((ch, t, k, cu, max), "
-          "max count as a host int); bld: from the (B, L, d_model) layout");
+          py::arg("expand"), py::arg("bld") = false, py::arg("x_conv") = py::none(),
+          "extract_base_events then expand_base_events in one fill pass -> ((ch, t, k, cu, max[, x_flat]), "
+          "max count as a host int); bld: from the (B, L, d_model) layout; x_conv (B, d_model*expand, L): "
+          "also gather_events_fwd of it at the stream (x_flat)");
     m.def("extract_base_events_bld", &extract_base_events_bld_fwd, py::arg("x"), py::arg("threshold"),
           "extract_base_events from the (B, L, d_model) layout: same 6 outputs, no transposed copy");
     m.def("conv_events_fwd", &conv_events_fwd, py::arg("x"), py::arg("weight"), py::arg("bias"),
@@ -762,6 +851,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("restore_dense_fwd", &restore_dense_fwd, py::arg("y_flat"), py::arg("time_steps"),
           py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"), py::arg("out_dtype") = py::none(),
           "Zero-order-hold restore (B, L, D) from flat events");
+    m.def("gather_events_bwd_rows", &gather_events_bwd_rows, py::arg("grad_x"), py::arg("time_steps"),
+          py::arg("cu_seqlens"), py::arg("n_channels"), py::arg("seqlen"),
+          "gather_events_bwd for a stream in extraction order, rows from cu_seqlens -> dx [NC, L]");
     m.def("restore_dense_fwd_bitmap", &restore_dense_fwd_bitmap, py::arg("y_flat"), py::arg("time_steps"),
           py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"), py::arg("out_dtype") = py::none(),
           "restore_dense_fwd that also returns the event bitmap (the first B*ceil(L/32)*dim int32 words, "

@@ -98,10 +98,12 @@ class SelectiveScanFlatChFn(torch.autograd.Function):
         pw_B = pw_B.contiguous() if pw_B is not None else None
         pw_C = pw_C.contiguous() if pw_C is not None else None
         with cuda_stage("sparse_scan_forward"):
-            res = ops.fwd_flat_ch(u_flat, k_flat, cu_seqlens, max_seqlen, dt_idle, dt_active,
-                                  A, B, C, D, z, tile_offsets, tile_chunk_size,
-                                  is_depthwise_bc, pw_B, pw_C)
-        out, x = res[0], res[1]
+            # the forward also keeps the state every 8 events (where the
+            # staged kernels run) so the backward does not re-run the recurrence
+            res = ops.fwd_flat_ch_ckpt(u_flat, k_flat, cu_seqlens, max_seqlen, dt_idle, dt_active,
+                                       A, B, C, D, z, tile_offsets, tile_chunk_size,
+                                       is_depthwise_bc, pw_B, pw_C)
+        out, x, ckpt = res[0], res[1], res[-1]
         ctx.has_D = D is not None
         ctx.has_z = z is not None
         ctx.has_tiles = tile_offsets is not None
@@ -118,6 +120,7 @@ class SelectiveScanFlatChFn(torch.autograd.Function):
             saved.append(tile_offsets)
         if ctx.has_pw:
             saved += [pw_B, pw_C]
+        saved.append(ckpt)
         ctx.save_for_backward(*saved)
         ctx.mark_non_differentiable(x)
         # x takes no gradient: without this autograd fills a zero tensor for it
@@ -137,10 +140,12 @@ class SelectiveScanFlatChFn(torch.autograd.Function):
         z, out = (next(it), next(it)) if ctx.has_z else (None, None)
         tile_offsets = next(it) if ctx.has_tiles else None
         pw_B, pw_C = (next(it), next(it)) if ctx.has_pw else (None, None)
+        ckpt = next(it)
         with cuda_stage("sparse_scan_backward"):
             res = ops.bwd_flat_ch(u_flat, k_flat, cu_seqlens, ctx.max_seqlen, dt_idle, dt_active,
                                   A, B, C, dout, x, D, z, out, tile_offsets,
-                                  ctx.tile_chunk_size, ctx.is_depthwise_bc, pw_B, pw_C)
+                                  ctx.tile_chunk_size, ctx.is_depthwise_bc, pw_B, pw_C,
+                                  ckpt if ckpt.numel() > 0 else None)
         du, dA, dB, dC, ddt_idle, ddt_active = res[:6]
         rest = iter(res[6:])
         dD = next(rest) if ctx.has_D else None
@@ -190,22 +195,31 @@ class GatherEventsFn(torch.autograd.Function):
     """u_flat[e] = x_conv[b, d, t] at (channel_ids[e] = b*D + d, time_steps[e])."""
 
     @staticmethod
-    def forward(ctx, x_conv, channel_ids_i32, time_steps_i32):
+    def forward(ctx, x_conv, channel_ids_i32, time_steps_i32, cu_seqlens=None):
         x_c = x_conv.contiguous()
         with cuda_stage("active_gather_forward"):
             out_x = load_ops().gather_events_fwd(x_c, channel_ids_i32, time_steps_i32)[0]
-        ctx.save_for_backward(channel_ids_i32, time_steps_i32)
+        # with the extraction's cu_seqlens the backward reads each channel's
+        # rows from it instead of recovering them from channel_ids
+        if cu_seqlens is not None:
+            ctx.save_for_backward(channel_ids_i32, time_steps_i32, cu_seqlens)
+        else:
+            ctx.save_for_backward(channel_ids_i32, time_steps_i32)
         ctx.shape = x_c.shape
         return out_x
 
     @staticmethod
     def backward(ctx, grad_x):
-        channel_ids_i32, time_steps_i32 = ctx.saved_tensors
+        saved = ctx.saved_tensors
+        channel_ids_i32, time_steps_i32 = saved[0], saved[1]
         B, D, L = ctx.shape
         with cuda_stage("gather_scatter_backward"):
-            dx = load_ops().gather_events_bwd(grad_x.contiguous(), channel_ids_i32,
-                                              time_steps_i32, B * D, L)[0]
-        return dx.view(B, D, L), None, None
+            if len(saved) == 3:
+                dx = load_ops().gather_events_bwd_rows(grad_x.contiguous(), time_steps_i32, saved[2], B * D, L)
+            else:
+                dx = load_ops().gather_events_bwd(grad_x.contiguous(), channel_ids_i32,
+                                                  time_steps_i32, B * D, L)[0]
+        return dx.view(B, D, L), None, None, None
 
 
 class ConvEventsFn(torch.autograd.Function):
@@ -240,8 +254,44 @@ def conv_events(x, weight, bias, channel_ids_i32, time_steps_i32, cu_seqlens):
     return ConvEventsFn.apply(x, weight, bias, channel_ids_i32, time_steps_i32, cu_seqlens)
 
 
-def gather_events(x_conv, channel_ids_i32, time_steps_i32):
-    return GatherEventsFn.apply(x_conv, channel_ids_i32, time_steps_i32)
+class ExtractGatherFn(torch.autograd.Function):
+    """Extraction + expansion + gather of x_conv in one fill pass: the
+    forward of extract_base_events -> expand_base_events -> GatherEventsFn
+    (reference spike_mamba/e_model.py:371-390, 167-193) with the same outputs;
+    only x_flat is differentiable (w.r.t. x_conv), and its backward is the
+    gather backward from the stream's rows."""
+
+    @staticmethod
+    def forward(ctx, x_conv, spikes, threshold, expand, bld, max_out):
+        x_c = x_conv.contiguous()
+        with cuda_stage("routing_index_extraction"):
+            # the maximum count arrives on the host with the event total (one
+            # synchronisation); expansion copies counts, so it is max_seqlen
+            # of the expanded stream too
+            (ch, ts, kf, cu, _mx, x_flat), max_seqlen = load_ops().extract_expanded_events(
+                spikes, threshold, expand, bld=bld, x_conv=x_c)
+        max_out.append(int(max_seqlen))
+        ctx.save_for_backward(ts, cu)
+        ctx.shape = x_c.shape
+        ctx.mark_non_differentiable(ch, ts, kf, cu)
+        ctx.set_materialize_grads(False)
+        return x_flat, ch, ts, kf, cu
+
+    @staticmethod
+    def backward(ctx, grad_x, *_):
+        if grad_x is None:
+            return (None,) * 6
+        ts, cu = ctx.saved_tensors
+        B, D, L = ctx.shape
+        with cuda_stage("gather_scatter_backward"):
+            dx = load_ops().gather_events_bwd_rows(grad_x.contiguous(), ts, cu, B * D, L)
+        return dx.view(B, D, L), None, None, None, None, None
+
+
+def gather_events(x_conv, channel_ids_i32, time_steps_i32, cu_seqlens=None):
+    """cu_seqlens (optional): the stream's channel offsets when it is in
+    extraction order, as extraction returns it."""
+    return GatherEventsFn.apply(x_conv, channel_ids_i32, time_steps_i32, cu_seqlens)
 
 
 def extract_events_base(base_input, x_conv, threshold: float, expand: int):
@@ -251,16 +301,12 @@ def extract_events_base(base_input, x_conv, threshold: float, expand: int):
 
     Returns (channel_ids, time_steps, k_flat, cu_seqlens, max_seqlen, x_conv_flat).
     """
-    ops = load_ops()
-    B, d_model, L = base_input.shape
-    with cuda_stage("routing_index_extraction"):
-        # extraction and expansion in one fill pass (the base stream is never
-        # written); the maximum count arrives on the host with the event total
-        # (one synchronisation), and expansion copies counts, so it is
-        # max_seqlen of the expanded stream too
-        (ch, ts, kf, cu, _mx), max_seqlen = ops.extract_expanded_events(base_input, threshold, expand)
-    x_flat = gather_events(x_conv, ch, ts)
-    return ch, ts, kf, cu, int(max_seqlen), x_flat
+    # extraction, expansion and the gather of x_conv in one fill pass (the
+    # base stream is never written)
+    mx = []
+    x_flat, ch, ts, kf, cu = ExtractGatherFn.apply(x_conv, base_input.contiguous(), float(threshold), int(expand),
+                                                   False, mx)
+    return ch, ts, kf, cu, mx[0], x_flat
 
 
 def extract_events_1d(hidden_states, x_conv, threshold: float, expand: int):
@@ -269,14 +315,11 @@ def extract_events_1d(hidden_states, x_conv, threshold: float, expand: int):
 
     Returns (channel_ids, time_steps, k_flat, cu_seqlens, max_seqlen, x_conv_flat).
     """
-    ops = load_ops()
-    B, L, d_model = hidden_states.shape
-    with cuda_stage("routing_index_extraction"):
-        # straight from the (B, L, d_model) layout (the reference first makes a
-        # transposed (B, d_model, L) copy, e_model.py:376), extraction and
-        # expansion in one fill pass; the maximum count comes back with the
-        # event total (one synchronisation, no .item())
-        (ch, ts, kf, cu, _mx), max_seqlen = ops.extract_expanded_events(
-            hidden_states.contiguous(), threshold, expand, bld=True)
-    x_flat = gather_events(x_conv, ch, ts)
-    return ch, ts, kf, cu, int(max_seqlen), x_flat
+    # straight from the (B, L, d_model) layout (the reference first makes a
+    # transposed (B, d_model, L) copy, e_model.py:376); extraction, expansion
+    # and the gather of x_conv in one fill pass, the maximum count back with
+    # the event total (one synchronisation, no .item())
+    mx = []
+    x_flat, ch, ts, kf, cu = ExtractGatherFn.apply(x_conv, hidden_states.contiguous(), float(threshold),
+                                                   int(expand), True, mx)
+    return ch, ts, kf, cu, mx[0], x_flat

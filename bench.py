@@ -1,6 +1,6 @@
 """Benchmark of the BC_mamba event hot path on B200: fwd+bwd events/s.
 
-One step = extract (threshold -> expanded events) -> gather -> sparse
+One step = extract (threshold -> expanded events, gather of x_conv) -> sparse
 selective scan forward -> ZOH restore forward, then the backward of all of
 them (restore bwd -> scan bwd -> gather bwd), through the reference-facing
 autograd Functions (bc_mamba_b200.interface), followed by the all-reduce of
@@ -112,14 +112,15 @@ class ClockSampler:
 
 # the API stages of one step (interface.cuda_stage names) -> op keys
 STAGE_OPS = {
-    "routing_index_extraction": "extract", "active_gather_forward": "gather_fwd", "sparse_scan_forward": "scan_fwd",
+    "routing_index_extraction": "extract", "sparse_scan_forward": "scan_fwd",
     "dense_restoration_forward": "restore_fwd", "restore_backward": "restore_bwd",
     "sparse_scan_backward": "scan_bwd", "gather_scatter_backward": "gather_bwd",
 }
 # kernels each stage launches (all ours): extract 3 (threshold + count,
-# count scan, fill of the expanded stream), gather 1, scan fwd 1, restore fwd
-# 1, restore bwd 1, scan bwd 2, gather bwd 4
-KERNELS_PER_STEP = 13
+# count scan, fill of the expanded stream with the gather of x_conv), scan fwd
+# 1, restore fwd 1, restore bwd 1, scan bwd 2, gather bwd 2 (row writer, idle
+# fallback)
+KERNELS_PER_STEP = 10
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per stage on the
 # c1 workload, summed over the stage's kernels, from one ncu capture of
@@ -127,7 +128,7 @@ KERNELS_PER_STEP = 13
 # profiles/dram_traffic_c1.txt).  Writes that stay in the 126 MB L2 when a
 # kernel ends are not counted.  Re-measured whenever a kernel changes.
 NCU_TRAFFIC_C1 = {
-    "extract": None, "gather_fwd": 95.40e6, "scan_fwd": 26.97e6,
+    "extract": None, "scan_fwd": 26.97e6,
     "restore_fwd": 36.77e6, "restore_bwd": 81.28e6, "scan_bwd": 46.16e6, "gather_bwd": 49.22e6,
 }
 
@@ -140,8 +141,7 @@ def algorithmic_bytes(cfg, E, NC, n_chunks):
     NCb = NC // cfg.expand
     L, N = cfg.L, cfg.N
     b = {
-        "extract": NCb * L * sv + 12 * E + 4 * NC,
-        "gather_fwd": (8 + 2 * s) * E,
+        "extract": NCb * L * sv + 12 * E + 4 * NC + 2 * s * E,
         "scan_fwd": (2 * s + 4) * E + 8 * N * NC * n_chunks,
         "restore_fwd": (4 + s) * E + NC * L * s,
         "restore_bwd": NC * L * s + 8 * E,

@@ -126,15 +126,20 @@ BCM_API bcm_status bcm_expand_base_events(const int32_t* base_ch_ids,
  * _bld) on the same workspace, writes the stream bcm_expand_base_events would
  * make from the base stream — ch_ids/t_steps/k_flat[E_base*expand] and
  * cu_seqlens[NCb*expand+1] — without writing the base stream; the maximum
- * per-channel count is the count pass's.  Interface path of
- * Mamba.extract_events_1d (reference spike_mamba/e_model.py:371-390), which
- * keeps only the expanded stream. */
+ * per-channel count is the count pass's.  With x (B, NCb*expand/B, seqlen)
+ * in x_dtype (fp32/fp16/bf16/fp64) it also writes x_flat[E_base*expand] =
+ * bcm_gather_events_fwd of x at that stream; x and x_flat are both NULL
+ * otherwise.  Interface path of Mamba.extract_events_1d (reference
+ * spike_mamba/e_model.py:371-390, 167-193), which keeps only the expanded
+ * stream and the gathered x_conv. */
 BCM_API bcm_status bcm_extract_expand_fill(int64_t n_base_channels, int64_t seqlen,
                                   const int32_t* base_cu_seqlens,
                                   const void* workspace, size_t workspace_bytes,
                                   int64_t expand, int32_t* ch_ids,
                                   int32_t* t_steps, int32_t* k_flat,
-                                  int32_t* cu_seqlens, cudaStream_t stream);
+                                  int32_t* cu_seqlens,
+                                  const void* x, bcm_dtype x_dtype, void* x_flat,
+                                  cudaStream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Event gather of x[NC, L] at (channel_ids, time_steps) and its transpose.
@@ -157,6 +162,24 @@ BCM_API size_t bcm_gather_bwd_workspace_bytes(int64_t n_channels);
 BCM_API bcm_status bcm_gather_events_bwd(const void* grad, bcm_dtype dtype,
                                  const int32_t* channel_ids,
                                  const int32_t* time_steps, int64_t n_events,
+                                 int64_t n_channels, int64_t seqlen,
+                                 void* dx, void* workspace, size_t workspace_bytes,
+                                 cudaStream_t stream);
+
+/* Gather backward of a stream in extraction order with its cu_seqlens: the
+ * events of channel c are [cu_seqlens[c], cu_seqlens[c+1]) (channel_ids is
+ * not read), so the row-bounds pass of bcm_gather_events_bwd is skipped.
+ * Results equal bcm_gather_events_bwd's for such streams; if a channel's
+ * times are not strictly increasing inside [0, seqlen) every row is rewritten
+ * by a fallback (zeros, then that row's events in stream order).  Workspace:
+ * BCM_GATHER_BWD_ROWS_WORKSPACE bytes.  Used by the interface's gather
+ * autograd function (reference GatherEventsFn.backward,
+ * spike_mamba/e_model.py:179-193), which holds cu_seqlens from extraction. */
+#define BCM_GATHER_BWD_ROWS_WORKSPACE 256
+
+BCM_API bcm_status bcm_gather_events_bwd_rows(const void* grad, bcm_dtype dtype,
+                                 const int32_t* time_steps,
+                                 const int32_t* cu_seqlens, int64_t n_events,
                                  int64_t n_channels, int64_t seqlen,
                                  void* dx, void* workspace, size_t workspace_bytes,
                                  cudaStream_t stream);
@@ -300,8 +323,17 @@ typedef struct bcm_flat_ch_args {
     /* scratch */
     void* workspace;
     size_t workspace_bytes;
+    /* nullable: state checkpoints (the normalised state entering every 8th
+     * event of a channel), bcm_flat_ch_ckpt_bytes(args) bytes.  The forward
+     * writes them, a backward given the same buffer reads them instead of
+     * re-running the forward recurrence; ignored when that size is 0. */
+    float* ckpt;
 } bcm_flat_ch_args;
 
+/* Bytes of the checkpoint buffer for these arguments: nonzero for the
+ * depthwise shapes the staged kernels run (dstate <= 64, the batch rows of
+ * a feature filling whole warps), 0 where the buffer would not be used. */
+BCM_API size_t bcm_flat_ch_ckpt_bytes(const bcm_flat_ch_args* args);
 BCM_API size_t bcm_flat_ch_fwd_workspace_bytes(const bcm_flat_ch_args* args);
 BCM_API size_t bcm_flat_ch_bwd_workspace_bytes(const bcm_flat_ch_args* args);
 BCM_API bcm_status bcm_flat_ch_fwd(const bcm_flat_ch_args* args, cudaStream_t stream);

@@ -3,7 +3,9 @@ the fill pass writing the expanded stream directly): its outputs equal
 ``expand_base_events`` applied to ``extract_base_events`` bit for bit, and the
 oracle's expansion, for both input layouts, expand 1..3, ragged shapes, 16-bit
 and float64 inputs, and the empty and all-events edge cases; the host-side
-maximum equals the device maximum."""
+maximum equals the device maximum; with x_conv the fused gather equals
+``gather_events_fwd`` at the same stream, and the autograd function built on
+it gives the gather's gradient."""
 import numpy as np
 import pytest
 import torch
@@ -35,6 +37,16 @@ def _check(x_bdl, thr, expand):
         for g, r, n in zip(got[:4], ref[:4], NAMES):
             assert_exact(g, r, n)
         assert mx_host == int(np.asarray(ref[4]).reshape(-1)[0]) == int(got[4].reshape(-1)[0].item())
+        # with x_conv: the same stream and the gather of x_conv at it
+        xc = torch.randn(B, dm * expand, L, generator=torch.Generator().manual_seed(L + dm)).to(
+            x_bdl.dtype if x_bdl.dtype in (torch.float16, torch.bfloat16, torch.float64) else torch.float32).to(dev)
+        got_x, mx2 = ops.extract_expanded_events(x_in.to(dev), thr, expand, bld=bld, x_conv=xc)
+        assert len(got_x) == 6 and mx2 == mx_host
+        for g, v in zip(got_x[:5], got):
+            assert torch.equal(g.reshape(-1), v.reshape(-1))
+        assert got_x[5].dtype == xc.dtype and got_x[5].numel() == got[0].numel()
+        if got[0].numel():
+            assert torch.equal(got_x[5], ops.gather_events_fwd(xc, got[0], got[1])[0])
     return got
 
 
@@ -65,3 +77,26 @@ def test_no_events_and_all_events():
     assert got[0].numel() == 0 and got[3].numel() == 2 * 9 * 2 + 1
     assert not got[3].any()
     _check(x, -1e9, 2)
+
+
+def test_extract_gather_autograd():
+    """interface.extract_events_base / extract_events_1d (fused fill + gather)
+    against the unfused ops: same stream, same x_flat, same d x_conv."""
+    from bc_mamba_b200 import interface as itf
+    ops = load_ops()
+    g = torch.Generator().manual_seed(11)
+    B, dm, L, expand = 3, 40, 300, 2
+    v = torch.randn(B, dm, L, generator=g).to(dev)
+    xc = torch.randn(B, dm * expand, L, generator=g).to(dev)
+    for fn, spikes in ((itf.extract_events_base, v), (itf.extract_events_1d, v.transpose(1, 2).contiguous())):
+        x_leaf = xc.clone().requires_grad_(True)
+        ch, ts, kf, cu, mx, x_flat = fn(spikes, x_leaf, 0.3, expand)
+        base = ops.extract_base_events(v, 0.3)
+        ref = ops.expand_base_events(*base[:4], B, dm, expand)
+        for a, b in zip((ch, ts, kf, cu), ref[:4]):
+            assert torch.equal(a, b)
+        assert mx == int(ref[4].reshape(-1)[0].item())
+        assert torch.equal(x_flat.detach(), ops.gather_events_fwd(xc, ch, ts)[0])
+        w = torch.randn(x_flat.shape, generator=g).to(dev)
+        (x_flat * w).sum().backward()
+        assert torch.equal(x_leaf.grad, ops.gather_events_bwd(w, ch, ts, B * dm * expand, L)[0].view(B, -1, L))

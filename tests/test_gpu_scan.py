@@ -94,6 +94,24 @@ def _run_and_check(u, k, cu, mx, dti, dta, A, B, C, D=None, z=None, toff=None, d
     assert len(gr) == len(ref) == len(names)
     for a, b, n in zip(gr, ref, names):
         assert_close(a, b, tol, n)
+    # the forward that also keeps the state checkpoints, and the backward that
+    # reads them instead of re-running the recurrence (staged kernels only)
+    res_ck = ops.fwd_flat_ch_ckpt(*args, Dt, None if zt is None else zt.to(dev),
+                                  None if toff is None else T(toff), 0, dw,
+                                  None if pwB is None else T(pwB), None if pwC is None else T(pwC))
+    assert len(res_ck) == len(res) + 1
+    for a, b in zip(res_ck[:-1], res):
+        assert torch.equal(a, b)
+    ck = res_ck[-1]
+    if ck.numel() > 0:
+        gr_ck = ops.bwd_flat_ch(*args, dout.to(dev), res[1], Dt, None if zt is None else zt.to(dev),
+                                res[0] if z is not None else None, None if toff is None else T(toff), 0, dw,
+                                None if pwB is None else T(pwB), None if pwC is None else T(pwC), ck)
+        for a, b, n in zip(gr_ck, ref, names):
+            assert_close(a, b, tol, n + " (forward checkpoints)")
+        if mx <= 2048:   # one chunk: the same states as the recomputation, bit for bit
+            for a, b, n in zip(gr_ck, gr, names):
+                assert torch.equal(a, b), n
     return res, gr
 
 
