@@ -340,108 +340,63 @@ __global__ void row_bounds_kernel(const int32_t* __restrict__ ch, int64_t n_even
     }
 }
 
-// Pass B: one warp per row writes the whole row of dx (zeros and the event
-// values) in chunks of 32*V positions with vector stores; the row's events are
-// staged 32 at a time into a shared chunk buffer.  Rows whose times are not
-// strictly increasing inside [0, L) raise *flag.
-template <typename T, bool VEC>
-__global__ void __launch_bounds__(128)
-dense_rows_kernel(const T* __restrict__ g, const int32_t* __restrict__ ts,
-                  const int32_t* __restrict__ row_start, const int32_t* __restrict__ flag,
-                  int64_t n_ch, int L, T* __restrict__ dx, int32_t* __restrict__ flag_out) {
-    constexpr int V = 16 / sizeof(T);
-    constexpr int CH = 32 * V;             // positions per chunk
-    __shared__ __align__(16) T s_chunk[4][CH];
-    if (flag != nullptr && *flag) return;   // null: no bounds pass ran (rows from cu_seqlens)
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int64_t r = (int64_t)blockIdx.x * 4 + w;
-    if (r >= n_ch) return;
-    T* row = dx + r * (int64_t)L;
-    T* buf = s_chunk[w];
-    int e = row_start[r];
-    const int e_end = row_start[r + 1];
-    int prev_t = -1;
-    for (int c0 = 0; c0 < L; c0 += CH) {
-        const int cend = min(c0 + CH, L);
-#pragma unroll
-        for (int v = 0; v < V; ++v) buf[lane * V + v] = from_f32<T>(0.f);
-        __syncwarp();
-        while (e < e_end) {
-            const int j = e + lane;
-            const int t = (j < e_end) ? ts[j] : INT_MAX;
-            const bool in = t < cend;
-            const unsigned m = __ballot_sync(kFull, in);
-            const int cnt = __popc(m);
-            // order check: strictly increasing times inside [0, L)
-            int tp = __shfl_up_sync(kFull, t, 1);
-            if (lane == 0) tp = prev_t;
-            if (in && (t <= tp || t < c0)) atomicExch(flag_out, 1);
-            if (in) buf[t - c0 < 0 ? 0 : t - c0] = g[j];
-            if (cnt > 0) prev_t = __shfl_sync(kFull, t, cnt - 1);
-            e += cnt;
-            if (cnt < 32) break;
-        }
-        __syncwarp();
-        if (VEC) {
-            const int pos = c0 + lane * V;
-            if (pos < cend)
-                *reinterpret_cast<uint4*>(row + pos) = *reinterpret_cast<const uint4*>(buf + lane * V);
-        } else {
-            for (int p = lane; p < cend - c0; p += 32) row[c0 + p] = buf[p];
-        }
-        __syncwarp();
-    }
-    if (lane == 0 && e != e_end) atomicExch(flag_out, 1);  // events at t >= L
-}
-
-// Pass B for rows that fit in shared memory (the usual case): one warp per
-// row holds the whole row: it zeroes it, scatters all of the row's events
-// (coalesced 32-event loads, independent of one another, so their latencies
-// overlap) and writes the row out with 16-byte stores.  Same flag rule.
-constexpr int kRowWarps = 4;
-constexpr size_t kRowSmemMax = 48 * 1024;   // dynamic shared memory per CTA without opt-in
+// Pass B: one warp per row.  The row's events are loaded first (coalesced,
+// up to kRowPre*32 at a time, all loads independent), the row is zeroed with
+// 16-byte stores while they are in flight, and the events are then written
+// into it (same warp, ordered after the zeros by __syncwarp; L2 merges the
+// writes, so the row reaches DRAM once).  Rows whose times are not strictly
+// increasing inside [0, L) raise *flag_out and are rewritten by the fallback.
+constexpr int kRowWarps = 8;
+constexpr int kRowPre = 16;
 
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(kRowWarps * 32)
-dense_rows_smem_kernel(const T* __restrict__ g, const int32_t* __restrict__ ts,
-                       const int32_t* __restrict__ row_start, const int32_t* __restrict__ flag_in,
-                       int64_t n_ch, int L, int row_elems, T* __restrict__ dx, int32_t* __restrict__ flag_out) {
-    extern __shared__ __align__(16) unsigned char s_rows[];
+dense_rows_direct_kernel(const T* __restrict__ g, const int32_t* __restrict__ ts,
+                         const int32_t* __restrict__ row_start, const int32_t* __restrict__ flag_in,
+                         int64_t n_ch, int L, T* __restrict__ dx, int32_t* __restrict__ flag_out) {
     constexpr int V = 16 / sizeof(T);
     if (flag_in != nullptr && *flag_in) return;
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + w;
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
     if (r >= n_ch) return;
-    T* buf = reinterpret_cast<T*>(s_rows) + (size_t)w * row_elems;
-    for (int p = lane * V; p < row_elems; p += 32 * V) *reinterpret_cast<uint4*>(buf + p) = make_uint4(0, 0, 0, 0);
-    __syncwarp();
+    T* row = dx + r * (int64_t)L;
     const int e_beg = row_start[r];
     const int e_end = row_start[r + 1];
     bool bad = false;
-    int prev = -1;   // last time of the previous 32 events (order check across steps)
-#pragma unroll 4
-    for (int j0 = e_beg; j0 < e_end; j0 += 32) {
-        const int j = j0 + lane;
-        const bool in = j < e_end;
-        const int t = in ? ts[j] : INT_MAX;
-        const T v = in ? g[j] : from_f32<T>(0.f);
-        int tp = __shfl_up_sync(kFull, t, 1);
-        if (lane == 0) tp = prev;
-        prev = __shfl_sync(kFull, t, 31);
-        if (in) {
-            if (t < 0 || t >= L || t <= tp) bad = true;
-            else buf[t] = v;
+    int prev = -1;   // time of the last event of the previous 32 (order check)
+    bool zeroed = false;
+    for (int b0 = e_beg; b0 < e_end || !zeroed; b0 += kRowPre * 32) {
+        int t[kRowPre];
+        T v[kRowPre];
+#pragma unroll
+        for (int i = 0; i < kRowPre; ++i) {
+            const int j = b0 + i * 32 + lane;
+            const bool in = j < e_end;
+            t[i] = in ? ts[j] : INT_MAX;
+            v[i] = in ? g[j] : from_f32<T>(0.f);
+        }
+        if (!zeroed) {
+            if (VEC) {
+                for (int p = lane * V; p < L; p += 32 * V) *reinterpret_cast<uint4*>(row + p) = make_uint4(0, 0, 0, 0);
+            } else {
+                for (int p = lane; p < L; p += 32) row[p] = from_f32<T>(0.f);
+            }
+            zeroed = true;
+            __syncwarp();
+        }
+#pragma unroll
+        for (int i = 0; i < kRowPre; ++i) {
+            const int j = b0 + i * 32 + lane;
+            int tp = __shfl_up_sync(kFull, t[i], 1);
+            if (lane == 0) tp = prev;
+            prev = __shfl_sync(kFull, t[i], 31);
+            if (j < e_end) {
+                if (t[i] < 0 || t[i] >= L || t[i] <= tp) bad = true;
+                else row[t[i]] = v[i];
+            }
         }
     }
     if (__any_sync(kFull, bad) && lane == 0) atomicExch(flag_out, 1);
-    __syncwarp();
-    T* row = dx + r * (int64_t)L;
-    if (VEC) {
-        for (int p = lane * V; p < L; p += 32 * V)
-            *reinterpret_cast<uint4*>(row + p) = *reinterpret_cast<const uint4*>(buf + p);
-    } else {
-        for (int p = lane; p < L; p += 32) row[p] = buf[p];
-    }
 }
 
 // Fallback of the rows variant (channel of an event given by cu_seqlens, not
@@ -490,34 +445,20 @@ __global__ void fallback_scatter_kernel(const int32_t* __restrict__ flag, const 
     }
 }
 
-// Pass B launch: whole rows in shared memory when a row fits (kRowSmemMax per
-// CTA), else the chunked kernel.
+// Pass B launch (16-byte row stores when L and dx allow).
 template <typename T>
 bcm_status launch_dense_rows(const T* g, const int32_t* ts, const int32_t* row_start, const int32_t* flag_in,
                              int64_t n_ch, int64_t L, T* dx, int32_t* flag_out, cudaStream_t stream) {
     constexpr int V = 16 / sizeof(T);
     const bool vec = (L % V == 0) && (reinterpret_cast<uintptr_t>(dx) % 16 == 0);
-    const int64_t row_elems = (L + V - 1) / V * V;
-    const size_t row_bytes = (size_t)row_elems * sizeof(T);
-    if (row_bytes <= kRowSmemMax) {
-        const int warps = (int)std::min<size_t>(kRowWarps, kRowSmemMax / row_bytes);
-        const unsigned grid = (unsigned)((n_ch + warps - 1) / warps);
-        const size_t smem = row_bytes * warps;
-        if (vec)
-            dense_rows_smem_kernel<T, true><<<grid, warps * 32, smem, stream>>>(
-                g, ts, row_start, flag_in, n_ch, (int)L, (int)row_elems, dx, flag_out);
-        else
-            dense_rows_smem_kernel<T, false><<<grid, warps * 32, smem, stream>>>(
-                g, ts, row_start, flag_in, n_ch, (int)L, (int)row_elems, dx, flag_out);
-    } else {
-        const int rows_grid = ceil_div(n_ch, 4);
-        if (vec)
-            dense_rows_kernel<T, true><<<rows_grid, 128, 0, stream>>>(g, ts, row_start, flag_in, n_ch, (int)L,
-                                                                      dx, flag_out);
-        else
-            dense_rows_kernel<T, false><<<rows_grid, 128, 0, stream>>>(g, ts, row_start, flag_in, n_ch, (int)L,
-                                                                       dx, flag_out);
-    }
+    const int64_t grid = (n_ch + kRowWarps - 1) / kRowWarps;
+    BCM_REQUIRE(grid < (1ll << 31), "gather_events_bwd: too many rows");
+    if (vec)
+        dense_rows_direct_kernel<T, true><<<(unsigned)grid, kRowWarps * 32, 0, stream>>>(
+            g, ts, row_start, flag_in, n_ch, (int)L, dx, flag_out);
+    else
+        dense_rows_direct_kernel<T, false><<<(unsigned)grid, kRowWarps * 32, 0, stream>>>(
+            g, ts, row_start, flag_in, n_ch, (int)L, dx, flag_out);
     BCM_LAUNCH_CHECK();
     return BCM_OK;
 }
