@@ -38,6 +38,7 @@ ABI_SYMBOLS = (
     "bcm_flat_ch_fwd",
     "bcm_flat_ch_bwd",
     "bcm_extract_expand_fill",
+    "bcm_extract_expanded",
     "bcm_gather_events_bwd_rows",
     "bcm_restore_workspace_bytes",
     "bcm_restore_bitmap_bytes",

@@ -218,7 +218,7 @@ mask_fill_expand_kernel(const uint32_t* __restrict__ mask, const int32_t* __rest
                         int64_t n_rows, int n_words, int expand,
                         int32_t* __restrict__ ch_ids, int32_t* __restrict__ t_steps,
                         int32_t* __restrict__ k_flat, int32_t* __restrict__ cu,
-                        const T* __restrict__ x, int L, T* __restrict__ x_flat) {
+                        const T* __restrict__ x, int L, T* __restrict__ x_flat, int64_t cap) {
     __shared__ int s_t[kFillWarps][1024 + 1];
     const int lane = lane_id();
     const int w_in = threadIdx.x >> 5;
@@ -254,6 +254,7 @@ mask_fill_expand_kernel(const uint32_t* __restrict__ mask, const int32_t* __rest
             for (int r = 0; r < expand; ++r) {
                 const int64_t o2 = out0 + (int64_t)r * cnt + local + i;
                 const int64_t c2 = row * expand + r;
+                if (o2 >= cap) continue;   // outputs sized below the total: the caller fills again
                 ch_ids[o2] = (int32_t)c2;
                 t_steps[o2] = t;
                 k_flat[o2] = kv;
@@ -500,9 +501,30 @@ static int32_t* pinned_summary() {
     return buf;
 }
 
+// A timing-free event per host thread and device marking the summary copy.
+static cudaError_t summary_event(cudaEvent_t* out) {
+    constexpr int kDev = 64;
+    thread_local cudaEvent_t ev[kDev] = {};
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    if (dev < 0 || dev >= kDev) return cudaErrorInvalidDevice;
+    if (ev[dev] == nullptr) {
+        err = cudaEventCreateWithFlags(&ev[dev], cudaEventDisableTiming);
+        if (err != cudaSuccess) return err;
+    }
+    *out = ev[dev];
+    return cudaSuccess;
+}
+
+// `before_sync` enqueues more work after the summary copy (work that needs
+// cu_seqlens on the device but not the total on the host); the host then
+// waits for the copy only, so the GPU keeps running that work meanwhile.
+template <typename Hook>
 static bcm_status scan_counts_and_sync(const int32_t* counts, int64_t n_base_channels, int32_t* cu_seqlens,
                                        int32_t* max_seqlen, void* workspace, int64_t seqlen,
-                                       int64_t* n_events_host, int32_t* max_host, cudaStream_t stream) {
+                                       int64_t* n_events_host, int32_t* max_host, cudaStream_t stream,
+                                       Hook&& before_sync) {
     int32_t* summary = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) +
                                                   mask_region_bytes(n_base_channels, seqlen));
     counts_scan_kernel<<<1, kScanThreads, 0, stream>>>(counts, n_base_channels, cu_seqlens, max_seqlen, summary);
@@ -511,7 +533,12 @@ static bcm_status scan_counts_and_sync(const int32_t* counts, int64_t n_base_cha
     int32_t* host = pinned_summary();
     if (host == nullptr) host = pageable;
     BCM_CUDA_TRY(cudaMemcpyAsync(host, summary, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
-    BCM_CUDA_TRY(cudaStreamSynchronize(stream));
+    cudaEvent_t copied = nullptr;
+    BCM_CUDA_TRY(summary_event(&copied));
+    BCM_CUDA_TRY(cudaEventRecord(copied, stream));
+    const bcm_status hs = before_sync();
+    if (hs != BCM_OK) return hs;
+    BCM_CUDA_TRY(cudaEventSynchronize(copied));
     *n_events_host = host[0];
     if (max_host) *max_host = host[1];
     return BCM_OK;
@@ -522,14 +549,12 @@ extern "C" size_t bcm_extract_workspace_bytes(int64_t n_base_channels, int64_t s
     return mask_region_bytes(n_base_channels, seqlen) + 256;
 }
 
-extern "C" bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype dtype,
-                                             int64_t n_base_channels, int64_t seqlen,
-                                             float threshold, int32_t* counts,
-                                             int32_t* cu_seqlens, int32_t* max_seqlen,
-                                             void* workspace, size_t workspace_bytes,
-                                             int64_t* n_events_host, int32_t* max_seqlen_host,
-                                             cudaStream_t stream) {
-    clear_error();
+template <typename Hook>
+static bcm_status count_base_impl(const void* base_input, bcm_dtype dtype, int64_t n_base_channels,
+                                  int64_t seqlen, float threshold, int32_t* counts, int32_t* cu_seqlens,
+                                  int32_t* max_seqlen, void* workspace, size_t workspace_bytes,
+                                  int64_t* n_events_host, int32_t* max_seqlen_host, cudaStream_t stream,
+                                  Hook&& before_sync) {
     BCM_REQUIRE(dtype_ok64(dtype), "extract_base_events: unsupported dtype %d", (int)dtype);
     BCM_REQUIRE(n_base_channels >= 0 && seqlen >= 0, "extract_base_events: negative size");
     BCM_REQUIRE(seqlen < (1ll << 31) && n_base_channels * seqlen < (1ll << 31) * 64,
@@ -568,16 +593,15 @@ extern "C" bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype d
         if (st != BCM_OK) return st;
     }
     return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, workspace, seqlen,
-                                n_events_host, max_seqlen_host, stream);
+                                n_events_host, max_seqlen_host, stream, before_sync);
 }
 
-extern "C" bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtype dtype, int64_t batch,
-                                                 int64_t seqlen, int64_t d_model, float threshold,
-                                                 int32_t* counts, int32_t* cu_seqlens, int32_t* max_seqlen,
-                                                 void* workspace, size_t workspace_bytes,
-                                                 int64_t* n_events_host, int32_t* max_seqlen_host,
-                                                 cudaStream_t stream) {
-    clear_error();
+template <typename Hook>
+static bcm_status count_bld_impl(const void* input_bld, bcm_dtype dtype, int64_t batch, int64_t seqlen,
+                                 int64_t d_model, float threshold, int32_t* counts, int32_t* cu_seqlens,
+                                 int32_t* max_seqlen, void* workspace, size_t workspace_bytes,
+                                 int64_t* n_events_host, int32_t* max_seqlen_host, cudaStream_t stream,
+                                 Hook&& before_sync) {
     BCM_REQUIRE(dtype_ok64(dtype), "extract_base_events_bld: unsupported dtype %d", (int)dtype);
     BCM_REQUIRE(batch >= 0 && seqlen >= 0 && d_model >= 0, "extract_base_events_bld: negative size");
     const int64_t n_base_channels = batch * d_model;
@@ -618,7 +642,32 @@ extern "C" bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtyp
         if (st != BCM_OK) return st;
     }
     return scan_counts_and_sync(counts, n_base_channels, cu_seqlens, max_seqlen, workspace, seqlen,
-                                n_events_host, max_seqlen_host, stream);
+                                n_events_host, max_seqlen_host, stream, before_sync);
+}
+
+static bcm_status no_hook() { return BCM_OK; }
+
+extern "C" bcm_status bcm_extract_base_count(const void* base_input, bcm_dtype dtype,
+                                             int64_t n_base_channels, int64_t seqlen,
+                                             float threshold, int32_t* counts,
+                                             int32_t* cu_seqlens, int32_t* max_seqlen,
+                                             void* workspace, size_t workspace_bytes,
+                                             int64_t* n_events_host, int32_t* max_seqlen_host,
+                                             cudaStream_t stream) {
+    clear_error();
+    return count_base_impl(base_input, dtype, n_base_channels, seqlen, threshold, counts, cu_seqlens, max_seqlen,
+                           workspace, workspace_bytes, n_events_host, max_seqlen_host, stream, no_hook);
+}
+
+extern "C" bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtype dtype, int64_t batch,
+                                                 int64_t seqlen, int64_t d_model, float threshold,
+                                                 int32_t* counts, int32_t* cu_seqlens, int32_t* max_seqlen,
+                                                 void* workspace, size_t workspace_bytes,
+                                                 int64_t* n_events_host, int32_t* max_seqlen_host,
+                                                 cudaStream_t stream) {
+    clear_error();
+    return count_bld_impl(input_bld, dtype, batch, seqlen, d_model, threshold, counts, cu_seqlens, max_seqlen,
+                          workspace, workspace_bytes, n_events_host, max_seqlen_host, stream, no_hook);
 }
 
 extern "C" bcm_status bcm_extract_base_fill(int64_t n_base_channels, int64_t seqlen,
@@ -646,6 +695,31 @@ extern "C" bcm_status bcm_extract_base_fill(int64_t n_base_channels, int64_t seq
     return BCM_OK;
 }
 
+static bcm_status launch_expand_fill(int64_t n_base_channels, int64_t seqlen, const int32_t* base_cu,
+                                     const void* workspace, int64_t expand, int32_t* ch_ids, int32_t* t_steps,
+                                     int32_t* k_flat, int32_t* cu_seqlens, const void* x, bcm_dtype x_dtype,
+                                     void* x_flat, int64_t cap, cudaStream_t stream) {
+    const int L = (int)seqlen;
+    const int n_words = (L + 31) / 32;
+    const int grid = ceil_div(n_base_channels, kFillWarps);
+    if (x == nullptr) {
+        mask_fill_expand_kernel<float><<<grid, kFillWarps * 32, 0, stream>>>(
+            static_cast<const uint32_t*>(workspace), base_cu, n_base_channels, n_words, (int)expand,
+            ch_ids, t_steps, k_flat, cu_seqlens, nullptr, L, nullptr, cap);
+        BCM_LAUNCH_CHECK();
+        return BCM_OK;
+    }
+    BCM_REQUIRE(dtype_ok64(x_dtype), "extract_expand_fill: unsupported x dtype %d", (int)x_dtype);
+    return dispatch_dtype64(x_dtype, [&](auto tag) -> bcm_status {
+        using T = decltype(tag);
+        mask_fill_expand_kernel<T><<<grid, kFillWarps * 32, 0, stream>>>(
+            static_cast<const uint32_t*>(workspace), base_cu, n_base_channels, n_words, (int)expand,
+            ch_ids, t_steps, k_flat, cu_seqlens, static_cast<const T*>(x), L, static_cast<T*>(x_flat), cap);
+        BCM_LAUNCH_CHECK();
+        return BCM_OK;
+    });
+}
+
 extern "C" bcm_status bcm_extract_expand_fill(int64_t n_base_channels, int64_t seqlen,
                                               const int32_t* base_cu_seqlens, const void* workspace,
                                               size_t workspace_bytes, int64_t expand, int32_t* ch_ids,
@@ -664,25 +738,45 @@ extern "C" bcm_status bcm_extract_expand_fill(int64_t n_base_channels, int64_t s
     }
     BCM_REQUIRE(seqlen == 0 || (ch_ids && t_steps && k_flat), "extract_expand_fill: null pointer");
     BCM_REQUIRE((x == nullptr) == (x_flat == nullptr), "extract_expand_fill: x and x_flat go together");
-    const int L = (int)seqlen;
-    const int n_words = (L + 31) / 32;
-    const int grid = ceil_div(n_base_channels, kFillWarps);
-    if (x == nullptr) {
-        mask_fill_expand_kernel<float><<<grid, kFillWarps * 32, 0, stream>>>(
-            static_cast<const uint32_t*>(workspace), base_cu_seqlens, n_base_channels, n_words, (int)expand,
-            ch_ids, t_steps, k_flat, cu_seqlens, nullptr, L, nullptr);
-        BCM_LAUNCH_CHECK();
+    return launch_expand_fill(n_base_channels, seqlen, base_cu_seqlens, workspace, expand, ch_ids, t_steps, k_flat,
+                              cu_seqlens, x, x_dtype, x_flat, INT64_MAX, stream);
+}
+
+extern "C" bcm_status bcm_extract_expanded(const void* input, bcm_dtype dtype, int32_t input_layout,
+                                           int64_t batch, int64_t d_model, int64_t seqlen, float threshold,
+                                           int64_t expand, int32_t* counts, int32_t* base_cu_seqlens,
+                                           int32_t* max_seqlen, void* workspace, size_t workspace_bytes,
+                                           int64_t capacity, int32_t* ch_ids, int32_t* t_steps, int32_t* k_flat,
+                                           int32_t* cu_seqlens, const void* x, bcm_dtype x_dtype, void* x_flat,
+                                           int64_t* n_events_host, int32_t* max_seqlen_host,
+                                           cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(input_layout == 0 || input_layout == 1, "extract_expanded: input_layout must be 0 or 1");
+    BCM_REQUIRE(batch >= 0 && d_model >= 0 && seqlen >= 0 && capacity >= 0, "extract_expanded: negative size");
+    BCM_REQUIRE(expand >= 1 && batch * d_model * expand < (1ll << 31), "extract_expanded: bad expand");
+    BCM_REQUIRE(cu_seqlens && n_events_host, "extract_expanded: null output");
+    BCM_REQUIRE((x == nullptr) == (x_flat == nullptr), "extract_expanded: x and x_flat go together");
+    BCM_REQUIRE(capacity == 0 || (ch_ids && t_steps && k_flat), "extract_expanded: null stream outputs");
+    const int64_t NCb = batch * d_model;
+    if (NCb == 0) {
+        BCM_CUDA_TRY(cudaMemsetAsync(cu_seqlens, 0, sizeof(int32_t), stream));
+        if (max_seqlen) BCM_CUDA_TRY(cudaMemsetAsync(max_seqlen, 0, sizeof(int32_t), stream));
+        BCM_CUDA_TRY(cudaStreamSynchronize(stream));
+        *n_events_host = 0;
+        if (max_seqlen_host) *max_seqlen_host = 0;
         return BCM_OK;
     }
-    BCM_REQUIRE(dtype_ok64(x_dtype), "extract_expand_fill: unsupported x dtype %d", (int)x_dtype);
-    return dispatch_dtype64(x_dtype, [&](auto tag) -> bcm_status {
-        using T = decltype(tag);
-        mask_fill_expand_kernel<T><<<grid, kFillWarps * 32, 0, stream>>>(
-            static_cast<const uint32_t*>(workspace), base_cu_seqlens, n_base_channels, n_words, (int)expand,
-            ch_ids, t_steps, k_flat, cu_seqlens, static_cast<const T*>(x), L, static_cast<T*>(x_flat));
-        BCM_LAUNCH_CHECK();
-        return BCM_OK;
-    });
+    // the fill goes in before the host waits: it needs the offsets on the
+    // device, not the total on the host
+    auto fill = [&]() -> bcm_status {
+        return launch_expand_fill(NCb, seqlen, base_cu_seqlens, workspace, expand, ch_ids, t_steps, k_flat,
+                                  cu_seqlens, x, x_dtype, x_flat, capacity, stream);
+    };
+    if (input_layout == 0)
+        return count_base_impl(input, dtype, NCb, seqlen, threshold, counts, base_cu_seqlens, max_seqlen, workspace,
+                               workspace_bytes, n_events_host, max_seqlen_host, stream, fill);
+    return count_bld_impl(input, dtype, batch, seqlen, d_model, threshold, counts, base_cu_seqlens, max_seqlen,
+                          workspace, workspace_bytes, n_events_host, max_seqlen_host, stream, fill);
 }
 
 extern "C" bcm_status bcm_expand_base_events(const int32_t* base_ch_ids,

@@ -337,9 +337,15 @@ extern "C" bcm_status bcm_flat_ch_fwd(const bcm_flat_ch_args* p, cudaStream_t st
         a.B = WB_eff;
         a.C = WC_eff;
     }
-    if (p->n_events == 0) return BCM_OK;
     const bool dw = p->bc_mode == BCM_BC_DEPTHWISE;
     const bool has_z = p->z != nullptr;
+    // x is written in full: the staged forward writes every slot itself,
+    // every other path writes the chunks that exist onto zeros
+    const bool staged = p->n_events > 0 && dw && dw_fast_supported(a.dstate) && v3_supported(a, false);
+    if (!staged)
+        BCM_CUDA_TRY(cudaMemsetAsync(p->x, 0, (size_t)a.n_channels * a.n_chunks * 2 * a.dstate * sizeof(float),
+                                     stream));
+    if (p->n_events == 0) return BCM_OK;
     if (dw && dw_fast_supported(a.dstate)) return dw_fast_launch(a, p->dtype, false, stream);
     return dispatch_dtype(p->dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);

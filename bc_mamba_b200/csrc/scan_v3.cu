@@ -645,6 +645,17 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
 #pragma unroll
     for (int c = 0; c < CPW; ++c) sd[c] = 0.f;
 
+    // chunk states past the channel's last chunk are zero (the kernel writes
+    // every slot of x: no pre-zeroing)
+    for (int c = (n + kChunkX - 1) / kChunkX; c < a.n_chunks; ++c) {
+        float* xo = a.x + ((int64_t)ch * a.n_chunks + c) * 2 * N;
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            if (s0 + g < N) {
+                xo[2 * (s0 + g)] = 0.f;
+                xo[2 * (s0 + g) + 1] = 0.f;
+            }
+    }
     // checkpoints for the backward: the state entering events 0, 8, 16, ...
     // of the channel (slot j/8 of the channel's region)
     float* ckb = nullptr;

@@ -16,6 +16,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdlib>
 #include <tuple>
 #include <vector>
 
@@ -172,23 +173,95 @@ std::tuple<std::vector<Tensor>, int64_t> extract_base_events_host_max(Tensor bas
 // expand_base_events(*extract_base_events(x, threshold)[:4], B, d_model,
 // expand) and the maximum per-channel count as a host integer (the one
 // synchronisation of the count pass); bld selects the (B, L, d_model) layout.
+// The first n elements of a larger buffer as a tensor of its own (same
+// storage, no view relation to the buffer).
+static Tensor head_of(const Tensor& buf, int64_t n) {
+    Tensor t = at::empty({0}, buf.options());
+    t.set_(buf.storage(), buf.storage_offset(), {n}, {1});
+    return t;
+}
+
+// Capacity buffers of the asynchronous fill are sized for every position
+// firing, up to this many bytes (BCM_ASYNC_FILL_BYTES overrides it); events
+// past the capacity are filled again after the synchronisation.
+constexpr int64_t kAsyncFillBytes = int64_t(1) << 30;
+
+static int64_t async_fill_bytes() {
+    const char* e = std::getenv("BCM_ASYNC_FILL_BYTES");
+    return (e != nullptr && *e != '\0') ? std::max<int64_t>(0, std::atoll(e)) : kAsyncFillBytes;
+}
+
 std::tuple<std::vector<Tensor>, int64_t> extract_expanded_events(Tensor x, double threshold, int64_t expand,
                                                                   bool bld, const optional<Tensor>& x_conv) {
-    TORCH_CHECK(expand >= 1, "extract_expanded_events: expand must be >= 1");
+    const char* fn = "extract_expanded_events";
+    TORCH_CHECK(expand >= 1, fn, ": expand must be >= 1");
+    TORCH_CHECK(x.is_cuda() && x.is_contiguous() && x.dim() == 3, fn, ": x must be a contiguous 3-D CUDA tensor");
+    const int64_t B = x.size(0), L = bld ? x.size(1) : x.size(2), d_model = bld ? x.size(2) : x.size(1);
     const Tensor* xc = nullptr;
     if (x_conv.has_value() && x_conv->defined()) {
         const Tensor& v = *x_conv;
-        TORCH_CHECK(v.is_cuda() && v.is_contiguous() && v.dim() == 3,
-                    "extract_expanded_events: x_conv must be a contiguous CUDA (B, D, L) tensor");
-        TORCH_CHECK(x.dim() == 3 && v.device() == x.device(), "extract_expanded_events: x_conv on x's device");
-        const int64_t B = x.size(0), L = bld ? x.size(1) : x.size(2), d_model = bld ? x.size(2) : x.size(1);
-        TORCH_CHECK(v.size(0) == B && v.size(1) == d_model * expand && v.size(2) == L,
-                    "extract_expanded_events: x_conv must be (B, d_model*expand, L)");
+        TORCH_CHECK(v.is_cuda() && v.is_contiguous() && v.dim() == 3, fn,
+                    ": x_conv must be a contiguous CUDA (B, D, L) tensor");
+        TORCH_CHECK(v.device() == x.device(), fn, ": x_conv on x's device");
+        TORCH_CHECK(v.size(0) == B && v.size(1) == d_model * expand && v.size(2) == L, fn,
+                    ": x_conv must be (B, d_model*expand, L)");
         xc = &v;
     }
+    const bcm_dtype dt = to_bcm(x.scalar_type(), fn);
+    const int64_t NCb = B * d_model;
+    TORCH_CHECK(NCb * expand < (1ll << 31), fn, ": expanded channels exceed int32");
+    c10::cuda::CUDAGuard guard(x.device());
+    auto opt_i = torch::TensorOptions().dtype(torch::kInt32).device(x.device());
+    auto counts = torch::empty({NCb}, opt_i);
+    auto base_cu = torch::empty({NCb + 1}, opt_i);
+    auto mx = torch::empty({}, opt_i);
+    auto ws = workspace((int64_t)bcm_extract_workspace_bytes(NCb, L), x.device());
+    auto cu_x = torch::empty({NCb * expand + 1}, opt_i);
+    // the fill runs before the host waits for the total, into buffers of the
+    // largest possible total; the outputs are their first E*expand elements
+    const int64_t ub = std::min<int64_t>(NCb * L * expand, (1ll << 31) - 1);
+    const int64_t per_event = 12 + (xc ? (int64_t)xc->element_size() : 0);
+    const int64_t cap = std::min<int64_t>(ub, async_fill_bytes() / per_event);
+    Tensor ch_c = torch::empty({cap}, opt_i), ts_c = torch::empty({cap}, opt_i), kf_c = torch::empty({cap}, opt_i);
+    Tensor x_c;
+    if (xc) x_c = torch::empty({cap}, xc->options());
+    const bool fill_now = cap > 0;
+    int64_t E = 0;
     int32_t mh = 0;
-    auto r = bld ? extract_base_events_bld_impl(x, threshold, &mh, expand, xc)
-                 : extract_base_events_impl(x, threshold, &mh, expand, xc);
+    check_status(bcm_extract_expanded(x.data_ptr(), dt, bld ? 1 : 0, B, d_model, L, (float)threshold, expand,
+                                      counts.data_ptr<int32_t>(), base_cu.data_ptr<int32_t>(), mx.data_ptr<int32_t>(),
+                                      ws.data_ptr(), ws.numel(), cap,
+                                      fill_now ? ch_c.data_ptr<int32_t>() : nullptr,
+                                      fill_now ? ts_c.data_ptr<int32_t>() : nullptr,
+                                      fill_now ? kf_c.data_ptr<int32_t>() : nullptr, cu_x.data_ptr<int32_t>(),
+                                      (fill_now && xc) ? xc->data_ptr() : nullptr,
+                                      xc ? to_bcm(xc->scalar_type(), fn) : BCM_F32,
+                                      (fill_now && xc) ? x_c.data_ptr() : nullptr, &E, &mh, cur_stream()),
+                 fn);
+    const int64_t n = E * expand;
+    TORCH_CHECK(n < (1ll << 31), fn, ": expanded events exceed int32");
+    Tensor ch, ts, kf, x_flat;
+    if (n <= cap) {
+        ch = head_of(ch_c, n);
+        ts = head_of(ts_c, n);
+        kf = head_of(kf_c, n);
+        if (xc) x_flat = head_of(x_c, n);
+    } else {
+        ch = torch::empty({n}, opt_i);
+        ts = torch::empty({n}, opt_i);
+        kf = torch::empty({n}, opt_i);
+        if (xc) x_flat = torch::empty({n}, xc->options());
+        check_status(bcm_extract_expand_fill(NCb, L, base_cu.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), expand,
+                                             ch.data_ptr<int32_t>(), ts.data_ptr<int32_t>(), kf.data_ptr<int32_t>(),
+                                             cu_x.data_ptr<int32_t>(), xc ? xc->data_ptr() : nullptr,
+                                             xc ? to_bcm(xc->scalar_type(), fn) : BCM_F32,
+                                             xc ? x_flat.data_ptr() : nullptr, cur_stream()),
+                     fn);
+    }
+    // expand_base_events' max is 0-d, or [0] of shape (1,) when nothing fires
+    Tensor mo = (E == 0) ? torch::zeros({1}, opt_i) : mx;
+    std::vector<Tensor> r = {ch, ts, kf, cu_x, mo};
+    if (xc) r.push_back(x_flat);
     return {r, (int64_t)mh};
 }
 
@@ -513,8 +586,8 @@ std::vector<Tensor> selective_scan_fwd_flat_ch_impl(
     int64_t n_chunks = (max_seqlen + 2047) / 2048;
     if (n_chunks == 0) n_chunks = 1;
     auto out = torch::empty_like(u_flat);
-    auto x = torch::zeros({P.a.n_channels, n_chunks, P.a.dstate * 2},
-                          u_flat.options().dtype(torch::kFloat32));
+    auto x = torch::empty({P.a.n_channels, n_chunks, P.a.dstate * 2},
+                          u_flat.options().dtype(torch::kFloat32));   // the forward writes every slot
     Tensor out_z;
     if (P.has_z) out_z = torch::empty_like(u_flat);
     bcm_flat_ch_args& a = P.a;

@@ -141,6 +141,33 @@ BCM_API bcm_status bcm_extract_expand_fill(int64_t n_base_channels, int64_t seql
                                   const void* x, bcm_dtype x_dtype, void* x_flat,
                                   cudaStream_t stream);
 
+/* Count + fill + optional gather in one call with its one synchronisation:
+ * the fill is enqueued before the host waits for the event total (the host
+ * waits for that total's copy only), into outputs of `capacity` expanded
+ * events (E_base*expand of them are written when they fit; any beyond
+ * capacity are skipped).  input_layout 0 is the (B, d_model, L) input of
+ * bcm_extract_base_count, 1 the (B, L, d_model) one of
+ * bcm_extract_base_count_bld; counts / base_cu_seqlens / max_seqlen and the
+ * workspace are theirs.  On return *n_events_host = E_base; if
+ * E_base*expand > capacity the caller runs bcm_extract_expand_fill with
+ * outputs of the full size (the workspace and base_cu_seqlens still hold the
+ * mask and offsets).  cu_seqlens[NCb*expand+1] is always written in full.
+ * Interface path of Mamba.extract_events_1d (reference
+ * spike_mamba/e_model.py:371-390, 167-193). */
+BCM_API bcm_status bcm_extract_expanded(const void* input, bcm_dtype dtype,
+                                  int32_t input_layout, int64_t batch,
+                                  int64_t d_model, int64_t seqlen,
+                                  float threshold, int64_t expand,
+                                  int32_t* counts, int32_t* base_cu_seqlens,
+                                  int32_t* max_seqlen,
+                                  void* workspace, size_t workspace_bytes,
+                                  int64_t capacity, int32_t* ch_ids,
+                                  int32_t* t_steps, int32_t* k_flat,
+                                  int32_t* cu_seqlens,
+                                  const void* x, bcm_dtype x_dtype, void* x_flat,
+                                  int64_t* n_events_host, int32_t* max_seqlen_host,
+                                  cudaStream_t stream);
+
 /* ------------------------------------------------------------------------- *
  * Event gather of x[NC, L] at (channel_ids, time_steps) and its transpose.
  * Replaces extract_events_cuda.gather_events_fwd / gather_events_bwd
@@ -305,7 +332,7 @@ typedef struct bcm_flat_ch_args {
     const float* pw_C;
     /* forward outputs */
     void* out;                  /* [E] ungated output                 */
-    float* x;                   /* [NC, n_chunks, 2N], pre-zeroed     */
+    float* x;                   /* [NC, n_chunks, 2N], written in full (zeros past a channel's chunks) */
     void* out_z;                /* [E] gated output when z != NULL    */
     /* backward inputs / outputs (ignored by the forward) */
     const void* dout;           /* [E] gradient of the primary output */

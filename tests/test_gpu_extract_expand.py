@@ -100,3 +100,25 @@ def test_extract_gather_autograd():
         w = torch.randn(x_flat.shape, generator=g).to(dev)
         (x_flat * w).sum().backward()
         assert torch.equal(x_leaf.grad, ops.gather_events_bwd(w, ch, ts, B * dm * expand, L)[0].view(B, -1, L))
+
+
+@pytest.mark.parametrize("cap_bytes", ["0", "16000", "1000000000"])
+def test_capacity_paths(cap_bytes, monkeypatch):
+    """The fill runs before the host waits for the event total, into buffers
+    of a capacity (BCM_ASYNC_FILL_BYTES / 16 bytes per event here); events
+    past it are skipped there and the whole stream is filled again after:
+    every capacity gives the same outputs."""
+    ops = load_ops()
+    g = torch.Generator().manual_seed(12)
+    B, dm, L, expand = 2, 24, 500, 2
+    v = torch.randn(B, dm, L, generator=g).to(dev)
+    xc = torch.randn(B, dm * expand, L, generator=g).to(dev)
+    base = ops.extract_base_events(v, 0.2)
+    ref = ops.expand_base_events(*base[:4], B, dm, expand)
+    assert ref[0].numel() * 16 > 16000            # the middle capacity is partial
+    monkeypatch.setenv("BCM_ASYNC_FILL_BYTES", cap_bytes)
+    got, mx = ops.extract_expanded_events(v, 0.2, expand, x_conv=xc)
+    for a, b in zip(got[:4], ref[:4]):
+        assert torch.equal(a, b)
+    assert mx == int(ref[4].reshape(-1)[0].item())
+    assert torch.equal(got[5], ops.gather_events_fwd(xc, ref[0], ref[1])[0])
