@@ -212,8 +212,11 @@ mask_fill_kernel(const uint32_t* __restrict__ mask, const int32_t* __restrict__ 
 // expanded cu_seqlens entries of its channel.  With x (B, D, L) given it also
 // gathers x at every expanded event (x_flat[o] = x[channel][t], what
 // gather_kernel computes from the finished stream).
+constexpr int kXB = 4;   // events per lane whose x loads are issued together
+constexpr int kXE = 2;   // copies (expand) covered by those loads (more load in the tail)
+
 template <typename T>
-__global__ void __launch_bounds__(kFillWarps * 32)
+__global__ void __launch_bounds__(kFillWarps * 32, 6)
 mask_fill_expand_kernel(const uint32_t* __restrict__ mask, const int32_t* __restrict__ base_cu,
                         int64_t n_rows, int n_words, int expand,
                         int32_t* __restrict__ ch_ids, int32_t* __restrict__ t_steps,
@@ -247,18 +250,40 @@ mask_fill_expand_kernel(const uint32_t* __restrict__ mask, const int32_t* __rest
             st[o++] = w * 32 + b;
         }
         __syncwarp();
-        for (int i = lane; i < total; i += 32) {
-            const int t = st[i];
-            const int prev = st[i - 1];
-            const int kv = (prev < 0) ? (t + 1) : (t - prev);
-            for (int r = 0; r < expand; ++r) {
-                const int64_t o2 = out0 + (int64_t)r * cnt + local + i;
-                const int64_t c2 = row * expand + r;
-                if (o2 >= cap) continue;   // outputs sized below the total: the caller fills again
-                ch_ids[o2] = (int32_t)c2;
-                t_steps[o2] = t;
-                k_flat[o2] = kv;
-                if (x != nullptr) x_flat[o2] = x[c2 * L + t];
+        // kXB events per lane at a time: their x loads (copies r < kXE) are
+        // all issued before any store, so the latencies overlap
+        for (int i0 = 0; i0 < total; i0 += 32 * kXB) {
+            int tv[kXB], kv[kXB];
+            T xv[kXB][kXE];
+#pragma unroll
+            for (int u = 0; u < kXB; ++u) {
+                const int i = i0 + u * 32 + lane;
+                const bool in = i < total;
+                const int t = in ? st[i] : 0;
+                const int prev = in ? st[i - 1] : 0;
+                tv[u] = t;
+                kv[u] = (prev < 0) ? (t + 1) : (t - prev);
+#pragma unroll
+                for (int r = 0; r < kXE; ++r)
+                    xv[u][r] = (x != nullptr && in && r < expand) ? x[(row * expand + r) * L + t] : T{};
+            }
+#pragma unroll
+            for (int u = 0; u < kXB; ++u) {
+                const int i = i0 + u * 32 + lane;
+                if (i >= total) continue;
+                auto put = [&](int r, T xr) {
+                    const int64_t o2 = out0 + (int64_t)r * cnt + local + i;
+                    if (o2 >= cap) return;   // outputs sized below the total: the caller fills again
+                    ch_ids[o2] = (int32_t)(row * expand + r);
+                    t_steps[o2] = tv[u];
+                    k_flat[o2] = kv[u];
+                    if (x != nullptr) x_flat[o2] = xr;
+                };
+#pragma unroll
+                for (int r = 0; r < kXE; ++r)
+                    if (r < expand) put(r, xv[u][r]);
+                for (int r = kXE; r < expand; ++r)   // copies past kXE load here
+                    put(r, x != nullptr ? x[(row * expand + r) * L + tv[u]] : T{});
             }
         }
         __syncwarp();
