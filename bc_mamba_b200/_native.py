@@ -37,6 +37,7 @@ ABI_SYMBOLS = (
     "bcm_flat_ch_bwd_workspace_bytes",
     "bcm_flat_ch_fwd",
     "bcm_flat_ch_bwd",
+    "bcm_event_decode_step",
     "bcm_extract_expand_fill",
     "bcm_extract_expanded",
     "bcm_gather_events_bwd_rows",

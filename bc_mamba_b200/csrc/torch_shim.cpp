@@ -361,6 +361,65 @@ Tensor gather_events_bwd_rows(Tensor grad_x, Tensor time_steps, Tensor cu_seqlen
     return dx;
 }
 
+static Tensor conv_weight2d(const Tensor& w, int64_t D);
+
+// ------------------------------------------------------------------ decode
+// One token of the event path for every channel; the state tensors are
+// updated in place (eta [B*D, N] fp32, counters [B*D, 2] int32, held [B*D]
+// fp32, conv_state [B, D, K] in x's dtype or None), y [B, D] is returned.
+Tensor event_decode_step(Tensor x, Tensor spikes, double threshold, Tensor dt_idle, Tensor dt_active, Tensor A,
+                         Tensor W_B, Tensor W_C, const optional<Tensor>& D_, Tensor eta, Tensor counters,
+                         Tensor held, const optional<Tensor>& conv_state, const optional<Tensor>& conv_weight,
+                         const optional<Tensor>& conv_bias) {
+    const char* fn = "event_decode_step";
+    TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), fn, ": x must be a contiguous CUDA (B, D) tensor");
+    TORCH_CHECK(spikes.is_cuda() && spikes.dim() == 2 && spikes.is_contiguous() &&
+                    spikes.scalar_type() == x.scalar_type() && spikes.size(0) == x.size(0),
+                fn, ": spikes must be a contiguous (B, d_model) tensor of x's dtype");
+    const int64_t B = x.size(0), D = x.size(1), dm = spikes.size(1), N = A.size(1);
+    TORCH_CHECK(A.dim() == 2 && A.size(0) == D && A.scalar_type() == torch::kFloat32, fn, ": A must be fp32 (D, N)");
+    auto f32 = [&](const Tensor& t, const char* name, std::vector<int64_t> shape) {
+        TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32 && t.is_contiguous() && t.sizes() == shape,
+                    fn, ": ", name, " has the wrong dtype, layout or shape");
+    };
+    f32(dt_idle, "dt_idle", {D}); f32(dt_active, "dt_active", {D});
+    f32(W_B, "W_B", {D, N}); f32(W_C, "W_C", {D, N});
+    f32(eta, "eta", {B * D, N}); f32(held, "held", {B * D});
+    TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == torch::kInt32 && counters.is_contiguous() &&
+                    counters.sizes() == torch::IntArrayRef({B * D, 2}),
+                fn, ": counters must be int32 (B*D, 2)");
+    const float* Dp = nullptr;
+    if (D_.has_value() && D_->defined()) { f32(*D_, "D", {D}); Dp = D_->data_ptr<float>(); }
+    void* cs = nullptr;
+    const float* cw = nullptr;
+    const float* cb = nullptr;
+    int64_t K = 0;
+    Tensor cw2;
+    if (conv_state.has_value() && conv_state->defined()) {
+        const Tensor& s = *conv_state;
+        TORCH_CHECK(s.is_cuda() && s.is_contiguous() && s.dim() == 3 && s.size(0) == B && s.size(1) == D &&
+                        s.scalar_type() == x.scalar_type(),
+                    fn, ": conv_state must be a contiguous (B, D, K) tensor of x's dtype");
+        TORCH_CHECK(conv_weight.has_value() && conv_weight->defined(), fn, ": conv_state needs conv_weight");
+        K = s.size(2);
+        cw2 = conv_weight2d(*conv_weight, D);
+        TORCH_CHECK(cw2.size(1) == K, fn, ": conv_weight must have K taps");
+        cs = s.data_ptr();
+        cw = cw2.data_ptr<float>();
+        if (conv_bias.has_value() && conv_bias->defined()) { f32(*conv_bias, "conv_bias", {D}); cb = conv_bias->data_ptr<float>(); }
+    }
+    c10::cuda::CUDAGuard guard(x.device());
+    auto y = torch::empty_like(x);
+    check_status(bcm_event_decode_step(x.data_ptr(), spikes.data_ptr(), to_bcm(x.scalar_type(), fn), B, D, dm, N,
+                                       (float)threshold, dt_idle.data_ptr<float>(), dt_active.data_ptr<float>(),
+                                       A.data_ptr<float>(), A.stride(0), A.stride(1), W_B.data_ptr<float>(),
+                                       W_C.data_ptr<float>(), Dp, cs, cw, cb, K, eta.data_ptr<float>(),
+                                       counters.data_ptr<int32_t>(), held.data_ptr<float>(), y.data_ptr(),
+                                       cur_stream()),
+                 fn);
+    return y;
+}
+
 // ------------------------------------------------------------- conv at events
 // weight [D, K] (or [D, 1, K]) and bias [D] are used as fp32.
 static Tensor conv_weight2d(const Tensor& w, int64_t D) {
@@ -927,6 +986,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("gather_events_bwd_rows", &gather_events_bwd_rows, py::arg("grad_x"), py::arg("time_steps"),
           py::arg("cu_seqlens"), py::arg("n_channels"), py::arg("seqlen"),
           "gather_events_bwd for a stream in extraction order, rows from cu_seqlens -> dx [NC, L]");
+    m.def("event_decode_step", &event_decode_step, py::arg("x"), py::arg("spikes"), py::arg("threshold"),
+          py::arg("dt_idle"), py::arg("dt_active"), py::arg("A"), py::arg("W_B"), py::arg("W_C"),
+          py::arg("D"), py::arg("eta"), py::arg("counters"), py::arg("held"),
+          py::arg("conv_state") = py::none(), py::arg("conv_weight") = py::none(), py::arg("conv_bias") = py::none(),
+          "One token of the event path for every channel (state updated in place) -> y (B, D)");
     m.def("restore_dense_fwd_bitmap", &restore_dense_fwd_bitmap, py::arg("y_flat"), py::arg("time_steps"),
           py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"), py::arg("out_dtype") = py::none(),
           "restore_dense_fwd that also returns the event bitmap (the first B*ceil(L/32)*dim int32 words, "

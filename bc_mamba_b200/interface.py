@@ -323,3 +323,36 @@ def extract_events_1d(hidden_states, x_conv, threshold: float, expand: int):
     x_flat, ch, ts, kf, cu = ExtractGatherFn.apply(x_conv, hidden_states.contiguous(), float(threshold),
                                                    int(expand), True, mx)
     return ch, ts, kf, cu, mx[0], x_flat
+
+
+class EventDecoder:
+    """The event path one token at a time, in place of Mamba.step
+    (reference spike_mamba/e_model.py:508-568, which reads self.pw_B /
+    self.pw_C that Mamba does not define).  Each step runs extraction's
+    compare on the token's spikes, the depthwise scan update of the channels
+    that fire and the restore's hold, so decoding a sequence gives exactly the
+    outputs extract_events_* -> selective_scan_flat_ch_fn (depthwise) ->
+    restore_dense_fn give for it.  With kernel_size > 0 the token's x is the
+    conv input and passes the causal depthwise conv + SiLU first (the
+    conv_state of e_model.py:512-518, kept here).
+
+    State per channel (B*D of them): eta [B*D, N] (normalised scan state),
+    counters [B*D, 2] (tokens since the last event, events so far), held
+    [B*D] (latest output), conv_state [B, D, K]."""
+
+    def __init__(self, batch: int, dim: int, dstate: int, device, dtype=torch.float32, kernel_size: int = 0):
+        nc = batch * dim
+        self.eta = torch.zeros(nc, dstate, dtype=torch.float32, device=device)
+        self.counters = torch.zeros(nc, 2, dtype=torch.int32, device=device)
+        self.held = torch.zeros(nc, dtype=torch.float32, device=device)
+        self.conv_state = (torch.zeros(batch, dim, kernel_size, dtype=dtype, device=device)
+                           if kernel_size > 0 else None)
+
+    def step(self, x, spikes, threshold: float, dt_idle, dt_active, A, W_B, W_C, D=None,
+             conv_weight=None, conv_bias=None):
+        """x [B, D] (u, or the conv input with a conv state), spikes [B, d_model]
+        -> y [B, D].  W_B / W_C are the effective [D, N] weights."""
+        return load_ops().event_decode_step(x.contiguous(), spikes.contiguous(), float(threshold),
+                                            dt_idle.contiguous(), dt_active.contiguous(), A, W_B.contiguous(),
+                                            W_C.contiguous(), D, self.eta, self.counters, self.held,
+                                            self.conv_state, conv_weight, conv_bias)

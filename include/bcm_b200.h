@@ -424,6 +424,38 @@ BCM_API bcm_status bcm_restore_dense_bwd(const void* dout, bcm_dtype dtype,
                                  float* dy, void* workspace, size_t workspace_bytes,
                                  cudaStream_t stream);
 
+/* ------------------------------------------------------------------------- *
+ * Decode: the event path one token at a time.  Replaces Mamba.step
+ *   (reference spike_mamba/e_model.py:508-568), which cannot run as written
+ *   (it reads self.pw_B / self.pw_C, undefined in Mamba) and would update
+ *   every channel at every token; this step is the training path itself
+ *   token by token, so decoding a sequence reproduces, bit for bit, what
+ *   extraction -> flat-channel scan (depthwise) -> restore compute for it.
+ * Channel c = b*dim + d.  x [batch, dim] in dtype: the token's u (x_conv), or
+ * with conv_state [batch, dim, kernel_size] (dtype; rolled in place) the conv
+ * input, passed through silu(conv_bias + sum_j conv_weight[d, j] * state)
+ * first (conv_weight fp32 [dim, kernel_size], kernel_size <= 8, conv_bias
+ * fp32 [dim] or NULL).  spikes [batch, d_model] in dtype; channel (b, d)
+ * fires when spikes[b, d / (dim/d_model)] > threshold (extraction's compare).
+ * A [dim, dstate] fp32 with element strides; W_B / W_C [dim, dstate] fp32
+ * (effective weights: pw_B @ W_B when point-wise mixing is used); D [dim] or
+ * NULL.  State, zeroed before the first token: eta [batch*dim, dstate] fp32,
+ * counters [batch*dim, 2] int32 {tokens since the last event, events so
+ * far}, held [batch*dim] fp32.  y [batch, dim] in dtype: the output of the
+ * channel's latest event among its first 4095 (the restore's hold and search
+ * cap), 0 before its first event.
+ * ------------------------------------------------------------------------- */
+BCM_API bcm_status bcm_event_decode_step(const void* x, const void* spikes, bcm_dtype dtype,
+                                 int64_t batch, int64_t dim, int64_t d_model,
+                                 int64_t dstate, float threshold,
+                                 const float* dt_idle, const float* dt_active,
+                                 const float* A, int64_t A_stride_d, int64_t A_stride_n,
+                                 const float* W_B, const float* W_C, const float* D,
+                                 void* conv_state, const float* conv_weight,
+                                 const float* conv_bias, int64_t kernel_size,
+                                 float* eta, int32_t* counters, float* held,
+                                 void* y, cudaStream_t stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
