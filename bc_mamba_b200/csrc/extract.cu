@@ -370,8 +370,9 @@ __global__ void row_bounds_kernel(const int32_t* __restrict__ ch, int64_t n_even
 // up to kRowPre*32 at a time, all loads independent), the row is zeroed with
 // 16-byte stores while they are in flight, and the events are then written
 // into it (same warp, ordered after the zeros by __syncwarp; L2 merges the
-// writes, so the row reaches DRAM once).  Rows whose times are not strictly
-// increasing inside [0, L) raise *flag_out and are rewritten by the fallback.
+// writes, so the row reaches DRAM once).  A row whose times are not strictly
+// increasing inside [0, L) is rewritten by its own warp: zeros, then its
+// events in stream order (flag_out, when given, is raised as well).
 constexpr int kRowWarps = 8;
 constexpr int kRowPre = 16;
 
@@ -422,29 +423,17 @@ dense_rows_direct_kernel(const T* __restrict__ g, const int32_t* __restrict__ ts
             }
         }
     }
-    if (__any_sync(kFull, bad) && lane == 0) atomicExch(flag_out, 1);
-}
-
-// Fallback of the rows variant (channel of an event given by cu_seqlens, not
-// channel_ids; runs only when *flag is set): every row is zeroed and its
-// events are written in stream order.
-template <typename T>
-__global__ void rows_fallback_kernel(const int32_t* __restrict__ flag, const T* __restrict__ g,
-                                     const int32_t* __restrict__ ts, const int32_t* __restrict__ row_start,
-                                     int64_t n_ch, int L, T* __restrict__ dx) {
-    if (!*flag) return;
-    const int lane = threadIdx.x & 31;
-    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n_ch; r += warps) {
-        T* row = dx + r * (int64_t)L;
+    if (__any_sync(kFull, bad)) {
+        __syncwarp();
         for (int p = lane; p < L; p += 32) row[p] = from_f32<T>(0.f);
         __syncwarp();
-        if (lane == 0)
-            for (int j = row_start[r]; j < row_start[r + 1]; ++j) {
+        if (lane == 0) {
+            for (int j = e_beg; j < e_end; ++j) {
                 const int t = ts[j];
                 if (t >= 0 && t < L) row[t] = g[j];
             }
-        __syncwarp();
+            if (flag_out != nullptr) atomicExch(flag_out, 1);
+        }
     }
 }
 
@@ -925,6 +914,8 @@ extern "C" bcm_status bcm_gather_events_bwd_rows(const void* grad, bcm_dtype dty
                                                  void* dx, void* workspace, size_t workspace_bytes,
                                                  cudaStream_t stream) {
     clear_error();
+    (void)workspace;        // kept for the ABI; a row with unsorted times is fixed by its own warp
+    (void)workspace_bytes;
     BCM_REQUIRE(dtype_ok64(dtype), "gather_events_bwd_rows: unsupported dtype %d", (int)dtype);
     BCM_REQUIRE(n_events >= 0 && n_channels >= 0 && seqlen >= 0, "gather_events_bwd_rows: negative size");
     BCM_REQUIRE(n_events < (1ll << 31) && seqlen < (1ll << 31), "gather_events_bwd_rows: sizes exceed int32");
@@ -936,23 +927,10 @@ extern "C" bcm_status bcm_gather_events_bwd_rows(const void* grad, bcm_dtype dty
         return BCM_OK;
     }
     BCM_REQUIRE(grad && time_steps && cu_seqlens, "gather_events_bwd_rows: null pointer");
-    if (!workspace || workspace_bytes < (size_t)BCM_GATHER_BWD_ROWS_WORKSPACE) {
-        set_error("gather_events_bwd_rows: workspace of %zu bytes < required %zu", workspace_bytes,
-                  (size_t)BCM_GATHER_BWD_ROWS_WORKSPACE);
-        return BCM_ERR_WORKSPACE;
-    }
-    int32_t* flag = static_cast<int32_t*>(workspace);
-    BCM_CUDA_TRY(cudaMemsetAsync(flag, 0, sizeof(int32_t), stream));
     return dispatch_dtype64(dtype, [&](auto tag) -> bcm_status {
         using T = decltype(tag);
-        const bcm_status st = launch_dense_rows<T>(static_cast<const T*>(grad), time_steps, cu_seqlens, nullptr,
-                                                   n_channels, seqlen, static_cast<T*>(dx), flag, stream);
-        if (st != BCM_OK) return st;
-        rows_fallback_kernel<T><<<sm_count() * 2, 256, 0, stream>>>(flag, static_cast<const T*>(grad), time_steps,
-                                                                     cu_seqlens, n_channels, (int)seqlen,
-                                                                     static_cast<T*>(dx));
-        BCM_LAUNCH_CHECK();
-        return BCM_OK;
+        return launch_dense_rows<T>(static_cast<const T*>(grad), time_steps, cu_seqlens, nullptr, n_channels,
+                                    seqlen, static_cast<T*>(dx), nullptr, stream);
     });
 }
 

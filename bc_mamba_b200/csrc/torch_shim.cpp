@@ -353,10 +353,9 @@ Tensor gather_events_bwd_rows(Tensor grad_x, Tensor time_steps, Tensor cu_seqlen
     auto dx = torch::empty({NC, L}, g.options());
     auto ts = time_steps.contiguous();
     auto cu = cu_seqlens.contiguous();
-    Tensor ws = workspace(BCM_GATHER_BWD_ROWS_WORKSPACE, g.device());
     check_status(bcm_gather_events_bwd_rows(g.data_ptr(), to_bcm(g.scalar_type(), "gather_events_bwd_rows"),
                                             ts.data_ptr<int32_t>(), cu.data_ptr<int32_t>(), g.size(0), NC, L,
-                                            dx.data_ptr(), ws.data_ptr(), ws.numel(), cur_stream()),
+                                            dx.data_ptr(), nullptr, 0, cur_stream()),
                  "gather_events_bwd_rows");
     return dx;
 }

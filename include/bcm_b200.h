@@ -196,10 +196,11 @@ BCM_API bcm_status bcm_gather_events_bwd(const void* grad, bcm_dtype dtype,
 /* Gather backward of a stream in extraction order with its cu_seqlens: the
  * events of channel c are [cu_seqlens[c], cu_seqlens[c+1]) (channel_ids is
  * not read), so the row-bounds pass of bcm_gather_events_bwd is skipped.
- * Results equal bcm_gather_events_bwd's for such streams; if a channel's
- * times are not strictly increasing inside [0, seqlen) every row is rewritten
- * by a fallback (zeros, then that row's events in stream order).  Workspace:
- * BCM_GATHER_BWD_ROWS_WORKSPACE bytes.  Used by the interface's gather
+ * Results equal bcm_gather_events_bwd's for such streams; a channel whose
+ * times are not strictly increasing inside [0, seqlen) has its row rewritten
+ * (zeros, then that row's events in stream order).  The workspace arguments
+ * are not used (NULL is fine; BCM_GATHER_BWD_ROWS_WORKSPACE is kept for
+ * callers that size one).  Used by the interface's gather
  * autograd function (reference GatherEventsFn.backward,
  * spike_mamba/e_model.py:179-193), which holds cu_seqlens from extraction. */
 #define BCM_GATHER_BWD_ROWS_WORKSPACE 256
