@@ -127,8 +127,8 @@ KERNELS_PER_STEP = 9
 # profiles/dram_traffic_c1.txt).  Writes that stay in the 126 MB L2 when a
 # kernel ends are not counted.  Re-measured whenever a kernel changes.
 NCU_TRAFFIC_C1 = {
-    "extract": 109.16e6, "scan_fwd": 27.28e6, "restore_fwd": 37.82e6, "restore_bwd": 70.40e6,
-    "scan_bwd": 70.18e6, "gather_bwd": 37.57e6,
+    "extract": 109.04e6, "scan_fwd": 27.45e6, "restore_fwd": 38.20e6, "restore_bwd": 70.59e6,
+    "scan_bwd": 70.54e6, "gather_bwd": 37.33e6,
 }
 
 
