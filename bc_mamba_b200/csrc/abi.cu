@@ -19,17 +19,28 @@ void clear_error() { g_err[0] = 0; }
 
 int sm_count() {
     // Cached per device; the query is cheap but sits on every launch path.
+    // It only sizes grids.  When the device cannot be queried the failure is
+    // recorded in the thread's error message and a B200's 148 SMs size the
+    // grid; the launch that follows then fails and its check returns the
+    // CUDA error as the call's status (a failed query leaves no sticky error).
     static std::mutex mu;
     static int cache[64] = {0};
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess || dev < 0 || dev >= 64) {
+        set_error("SM count query: cudaGetDevice failed (%s, device %d)", cudaGetErrorString(err), dev);
+        return 148;
+    }
     {
         std::lock_guard<std::mutex> lk(mu);
         if (cache[dev]) return cache[dev];
     }
     int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
-        n = 148;
+    err = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (err != cudaSuccess || n <= 0) {
+        set_error("SM count query on device %d failed: %s", dev, cudaGetErrorString(err));
+        return 148;   // not cached: the next call queries again
+    }
     std::lock_guard<std::mutex> lk(mu);
     cache[dev] = n;
     return n;

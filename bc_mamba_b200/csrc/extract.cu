@@ -953,7 +953,11 @@ void* g_scratch_addr[kMaxDevices] = {};
 
 // Device address of the scratch array on the current device.  Host code may
 // not use g_gather_bwd_scratch as a pointer (it names a host-side stand-in),
-// so the address is looked up once per device and cached.
+// so the address is looked up once per device and cached.  With lazy module
+// loading the first lookup on a device loads this library's module there,
+// which is when the array is allocated.  The cache lives as long as the
+// process: after a cudaDeviceReset() the cached address is stale, so the
+// library must not be used across a device reset.
 bcm_status noalloc_scratch(void** out) {
     int dev = -1;
     BCM_CUDA_TRY(cudaGetDevice(&dev));

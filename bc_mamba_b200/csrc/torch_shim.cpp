@@ -16,7 +16,10 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <algorithm>
 #include <cstdlib>
+#include <map>
+#include <mutex>
 #include <tuple>
 #include <vector>
 
@@ -181,10 +184,49 @@ static Tensor head_of(const Tensor& buf, int64_t n) {
     return t;
 }
 
-// Capacity buffers of the asynchronous fill are sized for every position
-// firing, up to this many bytes (BCM_ASYNC_FILL_BYTES overrides it); events
-// past the capacity are filled again after the synchronisation.
+// The fill of the expanded stream is enqueued before the host learns the
+// event total, into capacity buffers whose first E*expand elements become the
+// outputs (views: the whole capacity stays allocated while they live, e.g.
+// saved for the backward).  The capacity is predicted per input shape from
+// the largest totals of the last calls of that shape (kCapHeadroom above
+// them), so a steady training loop pins little more than it uses; the first
+// call of a shape, and any call whose total exceeds the prediction, fills
+// after the synchronisation into exact-size outputs instead.  At most
+// kAsyncFillBytes (BCM_ASYNC_FILL_BYTES overrides it) go to the capacity.
 constexpr int64_t kAsyncFillBytes = int64_t(1) << 30;
+constexpr double kCapHeadroom = 1.25;
+
+struct CapKey {
+    int dev;
+    int64_t ncb, L, expand, xsize;
+    bool operator<(const CapKey& o) const {
+        return std::tie(dev, ncb, L, expand, xsize) < std::tie(o.dev, o.ncb, o.L, o.expand, o.xsize);
+    }
+};
+struct CapHistory {
+    int64_t recent[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int next = 0, seen = 0;
+};
+std::mutex g_cap_mu;
+std::map<CapKey, CapHistory> g_cap;
+
+// Predicted event total (expanded) of a call of this shape; 0 = no history.
+int64_t predicted_events(const CapKey& k) {
+    std::lock_guard<std::mutex> lock(g_cap_mu);
+    auto it = g_cap.find(k);
+    if (it == g_cap.end() || it->second.seen == 0) return 0;
+    int64_t m = 0;
+    for (int64_t v : it->second.recent) m = std::max(m, v);
+    return (int64_t)(m * kCapHeadroom) + 4096;
+}
+
+void record_events(const CapKey& k, int64_t n) {
+    std::lock_guard<std::mutex> lock(g_cap_mu);
+    CapHistory& h = g_cap[k];
+    h.recent[h.next] = n;
+    h.next = (h.next + 1) % 8;
+    h.seen += 1;
+}
 
 static int64_t async_fill_bytes() {
     const char* e = std::getenv("BCM_ASYNC_FILL_BYTES");
@@ -218,10 +260,11 @@ std::tuple<std::vector<Tensor>, int64_t> extract_expanded_events(Tensor x, doubl
     auto ws = workspace((int64_t)bcm_extract_workspace_bytes(NCb, L), x.device());
     auto cu_x = torch::empty({NCb * expand + 1}, opt_i);
     // the fill runs before the host waits for the total, into buffers of the
-    // largest possible total; the outputs are their first E*expand elements
+    // predicted capacity; the outputs are their first E*expand elements
     const int64_t ub = std::min<int64_t>(NCb * L * expand, (1ll << 31) - 1);
     const int64_t per_event = 12 + (xc ? (int64_t)xc->element_size() : 0);
-    const int64_t cap = std::min<int64_t>(ub, async_fill_bytes() / per_event);
+    const CapKey key{(int)x.device().index(), NCb, L, expand, xc ? (int64_t)xc->element_size() : 0};
+    const int64_t cap = std::min<int64_t>({ub, async_fill_bytes() / per_event, predicted_events(key)});
     Tensor ch_c = torch::empty({cap}, opt_i), ts_c = torch::empty({cap}, opt_i), kf_c = torch::empty({cap}, opt_i);
     Tensor x_c;
     if (xc) x_c = torch::empty({cap}, xc->options());
@@ -240,6 +283,7 @@ std::tuple<std::vector<Tensor>, int64_t> extract_expanded_events(Tensor x, doubl
                  fn);
     const int64_t n = E * expand;
     TORCH_CHECK(n < (1ll << 31), fn, ": expanded events exceed int32");
+    record_events(key, n);
     Tensor ch, ts, kf, x_flat;
     if (n <= cap) {
         ch = head_of(ch_c, n);

@@ -1,0 +1,245 @@
+"""Block-stack workload: event blocks stacked in the
+ResidualPreNorm pattern, batch-sharded over ranks.
+
+The reference's LRA model stacks ResidualPreNorm(Mamba) blocks
+(spike_mamba/lra_impl.py:1381-1426): a block maps its spikes s to dv = core(s),
+the membrane leaks and integrates, v <- 0.95*v + dv, and the next block's
+spikes come from that membrane.  One block here runs the event hot path of
+Mamba.forward (spike_mamba/e_model.py:419-506):
+
+    extraction of the block's spikes (B, L, d_model) -> expanded event stream
+    and the gather of x_conv at the events -> depthwise selective scan over the
+    events -> zero-order-hold restore (B, L, D) -> out_proj (D -> d_model)
+
+with Mamba's parameterisation (A = -exp(A_log) (e_model.py:329-334, 463),
+W_B / W_C the halves of W_BC (:321-324, 475-476), dt_idle / dt_active =
+softplus(a0 / a1) + 1e-6 (TwoLevelDelta, :210-230), the D skip (:326) and the
+out_proj weight (:336)).
+
+Spikes: block l thresholds its input membrane v_l (B, L, d_model) directly
+(strict >, as extraction compares) at theta_l, the (1 - rho) quantile of v_l
+calibrated once on the workload's data (``calibrate_thresholds``), so the
+density stays pinned at rho while the spike pattern comes from the layer's own
+membrane.  (The reference's spike head STE(sigmoid(prob_head(LN v)) >= theta)
+does not control density.)  The conv feeding the gather (in_proj, causal
+conv1d, SiLU; e_model.py:428-451) is outside the path: each block's x_conv
+(B, D, L) is an input of the step.
+
+Inputs are generated per GLOBAL batch row from that row's own seed, so a rank
+holding rows [b0, b1) of the global batch sees exactly the rows a single GPU
+holding the whole batch sees (strong scaling: the same data at every world
+size).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Callable, List, Optional, Sequence
+
+import torch
+import torch.nn.functional as F
+
+from .workloads import Config, markov_chain, markov_rates
+
+
+def _inv_softplus(y: torch.Tensor) -> torch.Tensor:
+    return torch.log(torch.expm1(y))
+
+
+def event_path(v, x_conv, threshold: float, expand: int, dt_idle, dt_active, A, W_B, W_C, D):
+    """The event hot path of one block on the GPU: extraction of v (B, L,
+    d_model) at `threshold` with the gather of x_conv (B, D, L) -> depthwise
+    scan -> ZOH restore.  Returns (y_dense (B, L, D), (events, max_seqlen))."""
+    from . import interface as itf
+
+    B, L, _ = v.shape
+    dim = x_conv.shape[1]
+    ch, ts, kf, cu, mx, u_flat = itf.extract_events_1d(v, x_conv, threshold, expand)
+    y, _x = itf.selective_scan_flat_ch_fn(u_flat, kf, cu, mx, dt_idle, dt_active, A, W_B, W_C, D, None,
+                                          is_depthwise_bc=True)
+    return itf.restore_dense_fn(y, ts, cu, dim, L), (int(ch.numel()), int(mx))
+
+
+class _Proj(torch.autograd.Function):
+    """out_proj: y (B, L, D) @ W_out^T -> (B, L, d_model), optionally with
+    TF32 tensor-core GEMMs in forward and backward."""
+
+    @staticmethod
+    def forward(ctx, y, w, tf32: bool):
+        ctx.save_for_backward(y, w)
+        ctx.tf32 = tf32
+        with _tf32(tf32 and y.is_cuda):
+            return F.linear(y, w)
+
+    @staticmethod
+    def backward(ctx, g):
+        y, w = ctx.saved_tensors
+        with _tf32(ctx.tf32 and y.is_cuda):
+            dy = g @ w if ctx.needs_input_grad[0] else None
+            dw = g.reshape(-1, g.shape[-1]).t() @ y.reshape(-1, y.shape[-1]) if ctx.needs_input_grad[1] else None
+        return dy, dw, None
+
+
+class _tf32:
+    def __init__(self, on: bool):
+        self.on = on
+
+    def __enter__(self):
+        self.prev = torch.backends.cuda.matmul.allow_tf32
+        if self.on:
+            torch.backends.cuda.matmul.allow_tf32 = True
+
+    def __exit__(self, *exc):
+        torch.backends.cuda.matmul.allow_tf32 = self.prev
+
+
+@dataclass
+class StackParams:
+    """Parameters of one block (all fp32 leaves)."""
+    A_log: torch.Tensor      # [D, N]
+    W_BC: torch.Tensor       # [D, 2N]
+    D: torch.Tensor          # [D]
+    a0: torch.Tensor         # [D]   dt_idle = softplus(a0) + 1e-6
+    a1: torch.Tensor         # [D]   dt_active = softplus(a1) + 1e-6
+    W_out: torch.Tensor      # [d_model, D]
+
+    def tensors(self) -> List[torch.Tensor]:
+        return [self.A_log, self.W_BC, self.D, self.a0, self.a1, self.W_out]
+
+
+NAMES = ("A_log", "W_BC", "D", "a0", "a1", "W_out")
+
+
+class EventStack:
+    """`blocks` event blocks with the membrane chain v <- leak*v + block(v).
+
+    `path` is the per-block event computation (``event_path`` on the GPU); the
+    CPU tests pass a float64 restatement of the same computation."""
+
+    def __init__(self, cfg: Config, device, seed: int = 0, leak: float = 0.95,
+                 path: Callable = event_path, dtype=torch.float32, proj_tf32: bool = False):
+        self.cfg = cfg
+        self.leak = leak
+        self.path = path
+        # the dense out_proj GEMM (outside the event path) may run on the
+        # tensor cores in TF32; the event path itself is fp32 throughout
+        self.proj_tf32 = proj_tf32
+        g = torch.Generator().manual_seed(seed * 7919 + 17)
+        D, N, dm = cfg.D, cfg.N, cfg.d_model
+        self.params: List[StackParams] = []
+        for _ in range(cfg.blocks):
+            # value distributions of the benchmark configs (A = -(1..N);
+            # W_B, W_C ~ N(0,1); dt = softplus(N(0,1) - 1); D = 1), written in
+            # Mamba's parameterisation; out_proj as nn.Linear's default init
+            dt_i = F.softplus(torch.randn(D, generator=g) - 1.0)
+            dt_a = F.softplus(torch.randn(D, generator=g) - 1.0)
+            p = StackParams(
+                A_log=torch.log(torch.arange(1, N + 1, dtype=torch.float64)).repeat(D, 1),
+                W_BC=torch.randn(D, 2 * N, generator=g, dtype=torch.float64),
+                D=torch.ones(D, dtype=torch.float64),
+                a0=_inv_softplus(dt_i.double() - 1e-6),
+                a1=_inv_softplus(dt_a.double() - 1e-6),
+                W_out=(torch.rand(dm, D, generator=g, dtype=torch.float64) * 2 - 1) / math.sqrt(D),
+            )
+            self.params.append(StackParams(*[t.to(device=device, dtype=dtype).contiguous().requires_grad_(True)
+                                             for t in p.tensors()]))
+
+    def all_params(self) -> List[torch.Tensor]:
+        return [t for p in self.params for t in p.tensors()]
+
+    def block(self, l: int, v: torch.Tensor, x_conv: torch.Tensor, threshold: float):
+        """dv of block l for membrane v (B, L, d_model); returns (dv, the
+        path's (events, max_seqlen))."""
+        p = self.params[l]
+        N = self.cfg.N
+        A = -torch.exp(p.A_log)
+        W_B = p.W_BC[:, :N].contiguous()
+        W_C = p.W_BC[:, N:].contiguous()
+        dt_idle = F.softplus(p.a0) + 1e-6
+        dt_active = F.softplus(p.a1) + 1e-6
+        y_dense, events = self.path(v, x_conv, threshold, self.cfg.expand, dt_idle, dt_active, A, W_B, W_C, p.D)
+        return _Proj.apply(y_dense, p.W_out, self.proj_tf32), events
+
+    def forward(self, v0: torch.Tensor, x_convs: Sequence[torch.Tensor], thresholds: Sequence[float]):
+        """Membrane after the stack and (events, max_seqlen) of every block."""
+        v = v0
+        events = []
+        for l in range(self.cfg.blocks):
+            dv, e = self.block(l, v, x_convs[l], thresholds[l])
+            v = self.leak * v + dv
+            events.append(e)
+        return v, events
+
+
+# ------------------------------------------------------------------ data ----
+def row_generator(cfg: Config, row: int, device) -> torch.Generator:
+    """The generator of global batch row `row` (its own seed)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(cfg.seed * 1_000_003 + 7 * row + 1)
+    return g
+
+
+def stack_inputs(cfg: Config, rows: range, device, dtype=torch.float32) -> dict:
+    """Inputs of global batch rows `rows`: membrane v0 (b, L, d_model),
+    x_conv per block (b, D, L) and the upstream gradient of the final
+    membrane (b, L, d_model).  i.i.d. spikes: v0 ~ N(0, 1).  Markov spikes: a
+    two-state chain per base channel with on-runs of mean 8 and density
+    cfg.rho (started stationary), v0 = state + N(0, 0.25^2), so the calibrated
+    threshold picks the chain's on-runs."""
+    v0, xs, gs = [], [[] for _ in range(cfg.blocks)], []
+    states, unif = [], []
+    for r in rows:
+        g = row_generator(cfg, r, device)
+        v = torch.randn(cfg.L, cfg.d_model, generator=g, device=device)
+        if cfg.spikes == "markov":
+            p_off_on, p_on_off = markov_rates(cfg.rho)
+            states.append(torch.rand(cfg.d_model, generator=g, device=device) < p_off_on / (p_off_on + p_on_off))
+            unif.append(torch.rand(cfg.d_model, cfg.L, generator=g, device=device))
+            v = 0.25 * v
+        v0.append(v)
+        for l in range(cfg.blocks):
+            xs[l].append(torch.randn(cfg.D, cfg.L, generator=g, device=device).to(dtype))
+        gs.append(torch.randn(cfg.L, cfg.d_model, generator=g, device=device))
+    v0 = torch.stack(v0)
+    if cfg.spikes == "markov":
+        on = markov_chain(torch.cat(states), torch.cat(unif), cfg.rho)     # (b*d_model, L)
+        v0 = v0 + on.view(len(rows), cfg.d_model, cfg.L).transpose(1, 2).float()
+    return {"v0": v0.to(dtype).contiguous(), "x_conv": [torch.stack(x).contiguous() for x in xs],
+            "dout": torch.stack(gs).to(dtype).contiguous()}
+
+
+# ----------------------------------------------------------- thresholds ----
+def _row_sample(v: torch.Tensor, t_stride: int = 8, f_stride: int = 4) -> torch.Tensor:
+    """The same positions of every row (so the union over ranks does not
+    depend on how rows are sharded)."""
+    return v[:, ::t_stride, ::f_stride].reshape(-1).float()
+
+
+def global_quantile(v: torch.Tensor, q: float, group=None, gather: bool = True) -> float:
+    """q-quantile (an order statistic) of a fixed per-row sample of v over
+    every rank's rows (gather=False: this process's rows only)."""
+    import torch.distributed as dist
+
+    s = _row_sample(v)
+    if gather and dist.is_available() and dist.is_initialized():
+        parts = [torch.empty_like(s) for _ in range(dist.get_world_size(group))]
+        dist.all_gather(parts, s, group=group)
+        s = torch.cat(parts)
+    n = s.numel()
+    k = max(1, min(n, int(round(q * n))))
+    return float(s.kthvalue(k).values)
+
+
+@torch.no_grad()
+def calibrate_thresholds(stack: EventStack, v0: torch.Tensor, x_convs: Sequence[torch.Tensor],
+                         rho: Optional[float] = None, group=None, gather: bool = True) -> List[float]:
+    """theta_l = the (1 - rho) quantile of block l's input membrane, block by
+    block (each block's membrane depends on the thresholds before it)."""
+    rho = stack.cfg.rho if rho is None else rho
+    v = v0
+    th = []
+    for l in range(stack.cfg.blocks):
+        th.append(global_quantile(v, 1.0 - rho, group, gather))
+        dv, _ = stack.block(l, v, x_convs[l], th[-1])
+        v = stack.leak * v + dv
+    return th

@@ -6,8 +6,9 @@ Per configuration (B batch, D = d_model*expand logical features, N states,
 L positions, rho spike density):
   * membrane v ~ N(0,1) of shape (B, d_model, L); the threshold is the exact
     (1 - rho) order statistic of v, so ~rho of positions fire (i.i.d.);
-    "markov" configs use a per-channel two-state chain with P(on->off) = 1/8,
-    P(off->on) = 1/12 from its stationary start, v in {0, 1}, threshold 0.5;
+    "markov" configs use a per-channel two-state chain with P(on->off) = 1/8
+    (on-runs of mean 8) and P(off->on) set for density rho (1/12 at rho =
+    0.4), from its stationary start, v in {0, 1}, threshold 0.5;
   * x_conv u ~ N(0,1) of shape (B, D, L);
   * dt_idle, dt_active = softplus(N(0,1) - 1), shape (D,);
   * A = -(1..N) for every feature (A_log = log(1..N), the S4D-real init);
@@ -53,27 +54,43 @@ CONFIGS = {
 }
 
 
-def _markov(shape, gen) -> torch.Tensor:
-    """Two-state chain per row: on-run mean 8, off-run mean 12 (density 0.4)."""
-    rows, L = shape
-    p_off_on, p_on_off = 1.0 / 12.0, 1.0 / 8.0
-    p_on = p_off_on / (p_off_on + p_on_off)  # stationary P(on) = 0.4
-    state = torch.rand(rows, generator=gen) < p_on
-    out = torch.empty(rows, L, dtype=torch.bool)
-    r = torch.rand(rows, L, generator=gen)
-    for t in range(L):
+def markov_rates(rho: float = 0.4):
+    """(P(off->on), P(on->off)) of the two-state spike chain: on-runs of mean
+    length 8 and stationary density rho (rho = 0.4: off-runs of mean 12)."""
+    if rho == 0.4:
+        return 1.0 / 12.0, 1.0 / 8.0
+    return rho / (8.0 * (1.0 - rho)), 1.0 / 8.0
+
+
+def markov_chain(state: torch.Tensor, r: torch.Tensor, rho: float = 0.4) -> torch.Tensor:
+    """Run the chain from `state` (rows,) bool over the uniforms r (rows, L);
+    returns the (rows, L) bool on/off path (works on any device)."""
+    p_off_on, p_on_off = markov_rates(rho)
+    out = torch.empty(r.shape, dtype=torch.bool, device=r.device)
+    for t in range(r.shape[1]):
         out[:, t] = state
-        flip_off = state & (r[:, t] < 1.0 / 8.0)
-        flip_on = (~state) & (r[:, t] < 1.0 / 12.0)
+        flip_off = state & (r[:, t] < p_on_off)
+        flip_on = (~state) & (r[:, t] < p_off_on)
         state = (state & ~flip_off) | flip_on
     return out
+
+
+def _markov(shape, gen, rho: float = 0.4) -> torch.Tensor:
+    """Two-state chain per row: on-run mean 8, stationary density rho (0.4:
+    off-run mean 12), started from its stationary distribution."""
+    rows, L = shape
+    p_off_on, p_on_off = markov_rates(rho)
+    p_on = p_off_on / (p_off_on + p_on_off)
+    state = torch.rand(rows, generator=gen) < p_on
+    r = torch.rand(rows, L, generator=gen)
+    return markov_chain(state, r, rho)
 
 
 def spikes_membrane(cfg: Config, gen: torch.Generator):
     """(v, threshold): membrane (B, d_model, L) float32 and the firing threshold."""
     shape = (cfg.B, cfg.d_model, cfg.L)
     if cfg.spikes == "markov":
-        v = _markov((cfg.B * cfg.d_model, cfg.L), gen).reshape(shape).float()
+        v = _markov((cfg.B * cfg.d_model, cfg.L), gen, cfg.rho).reshape(shape).float()
         return v, 0.5
     v = torch.randn(shape, generator=gen)
     n = v.numel()

@@ -6,7 +6,10 @@
  * Each entry point replaces one binding of the reference's pybind11
  * extensions; the reference location it replaces is cited beside it.  The
  * caller owns and allocates every buffer (outputs and workspaces); the library
- * allocates nothing, keeps no state between calls, and is re-entrant.
+ * allocates nothing, keeps no state between calls, and is re-entrant — with
+ * one exception, bcm_gather_events_bwd_noalloc, which keeps its scratch in a
+ * fixed per-device array inside the library (so its calls must not overlap
+ * on the GPU; see its block below).
  *
  * Conventions
  *   - Every function returns a bcm_status.  BCM_OK (0) means success; any
@@ -230,7 +233,11 @@ BCM_API bcm_status bcm_gather_events_bwd_rows(const void* grad, bcm_dtype dtype,
  * calls that can overlap on the GPU (on different streams without ordering
  * between them) race on it and must not be issued.  The first call on each
  * device looks up the array's device address (the device must be current)
- * and should come before any stream capture.
+ * and should come before any stream capture; with CUDA's lazy module loading
+ * that first lookup is also when the library's module is loaded on the device
+ * and the array is allocated, so the first call can allocate while later
+ * calls do not.  The address is cached per device for the life of the
+ * process: do not keep using the library across a cudaDeviceReset().
  * ------------------------------------------------------------------------- */
 #define BCM_GATHER_BWD_NOALLOC_MAX_CHANNELS 262144
 

@@ -22,6 +22,12 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
 
+
+def default_root() -> Path:
+    """The reference checkout: $BCM_REFERENCE_ROOT, else the mount point of
+    the build container."""
+    return Path(os.environ.get("BCM_REFERENCE_ROOT", "/root/reference"))
+
 SOURCES = {
     "extract_events_cuda": ["csrc/extract/extract_events_cuda.cu"],
     "restore_dense_cuda_nodecay": [
@@ -90,5 +96,5 @@ def load(name: str):
 
 
 if __name__ == "__main__":
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    root = Path(sys.argv[1]) if len(sys.argv) > 1 else default_root()
     build(root, sys.argv[2:] or None)

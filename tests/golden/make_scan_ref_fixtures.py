@@ -116,7 +116,9 @@ def make_case(ssi, name, cfg, legacy_bc=False, with_z=False, dense_seed=123):
 
 
 def main():
-    ref = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    from oracle.build_ref import default_root
+
+    ref = Path(sys.argv[1]) if len(sys.argv) > 1 else default_root()
     ssi = import_reference(ref)
     torch.manual_seed(0)
     c0 = CONFIGS["c0"]

@@ -30,6 +30,9 @@ def test_library_loads_and_exports_every_symbol():
     lib = bc_mamba_b200.load_library()
     for s in declared_symbols():
         assert isinstance(getattr(lib, s), ctypes._CFuncPtr), s
+    # the allocation-free gather backward is declared and exported like the rest
+    assert "bcm_gather_events_bwd_noalloc" in declared_symbols()
+    assert isinstance(lib.bcm_gather_events_bwd_noalloc, ctypes._CFuncPtr)
     assert lib.bcm_abi_version() == 1
     assert lib.bcm_last_error() == b""
 

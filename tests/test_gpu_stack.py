@@ -1,0 +1,83 @@
+"""GPU parity of the block-stack workload against the
+float64 oracle path: the 4-block stack on the B200 (CUDA event path, fp32,
+fp32 out_proj) and the same stack on the CPU with the oracle path, same
+parameters and thresholds.  Each CPU block extracts its events from the
+membrane the GPU block saw (extraction is not differentiable in it), so both
+sides run on identical event streams and differ only by rounding; the final
+membrane, every parameter gradient and every x_conv gradient agree within the
+fp32 tolerance.  Event counts and densities are checked exactly against the
+oracle's extraction."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import TOL_F32, assert_close
+from stack_oracle import oracle_path
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def _cfg(spikes, rho):
+    from bc_mamba_b200.workloads import CONFIGS
+
+    return CONFIGS["c4"].with_(B=4, D=64, N=16, L=1500, rho=rho, spikes=spikes, blocks=4, seed=9)
+
+
+@pytest.mark.parametrize("spikes,rho", [("iid", 0.1), ("iid", 0.5), ("markov", 0.25)])
+def test_stack_matches_oracle(spikes, rho):
+    from bc_mamba_b200 import stack as stk
+
+    cfg = _cfg(spikes, rho)
+    inp = stk.stack_inputs(cfg, range(cfg.B), dev)
+    seen = []
+
+    def gpu_path(v, *a):
+        seen.append(v.detach().double().cpu())
+        return stk.event_path(v, *a)
+
+    gpu = stk.EventStack(cfg, dev, seed=cfg.seed, path=gpu_path)
+    thr = stk.calibrate_thresholds(gpu, inp["v0"], inp["x_conv"])
+    seen.clear()
+    xs = [x.clone().requires_grad_(True) for x in inp["x_conv"]]
+    v, ev = gpu.forward(inp["v0"], xs, thr)
+    v.backward(inp["dout"])
+    torch.cuda.synchronize()
+
+    it = iter(range(cfg.blocks))
+
+    def cpu_path(v_cpu, *a):
+        return oracle_path(seen[next(it)], *a)
+
+    cpu = stk.EventStack(cfg, "cpu", seed=cfg.seed, path=cpu_path, dtype=torch.float64)
+    xs_c = [x.detach().double().cpu().requires_grad_(True) for x in inp["x_conv"]]
+    v_c, ev_c = cpu.forward(inp["v0"].double().cpu(), xs_c, thr)
+    v_c.backward(inp["dout"].double().cpu())
+
+    assert [e for e, _ in ev] == [e for e, _ in ev_c]
+    assert [m for _, m in ev] == [m for _, m in ev_c]
+    dens = [e / (cfg.B * cfg.L * cfg.D) for e, _ in ev]
+    assert all(0.5 * rho < d < 2 * rho for d in dens), dens
+    assert_close(v, v_c.detach().numpy(), TOL_F32, "membrane after the stack")
+    for name, a, b in zip([f"{n}[{l}]" for l in range(cfg.blocks) for n in stk.NAMES],
+                          gpu.all_params(), cpu.all_params()):
+        assert_close(a.grad, b.grad.numpy(), TOL_F32, "d" + name)
+    for l, (a, b) in enumerate(zip(xs, xs_c)):
+        assert_close(a.grad, b.grad.numpy(), TOL_F32, f"dx_conv[{l}]")
+
+
+def test_stack_thresholds_pin_density_at_full_rows():
+    """At the benchmark's row length and width the calibrated thresholds give
+    the target density in every block (one shard of 8 rows)."""
+    from bc_mamba_b200 import stack as stk
+    from bc_mamba_b200.workloads import CONFIGS
+
+    for spikes in ("iid", "markov"):
+        cfg = CONFIGS["c4"].with_(B=8, spikes=spikes, rho=0.1)
+        inp = stk.stack_inputs(cfg, range(cfg.B), dev)
+        model = stk.EventStack(cfg, dev, seed=cfg.seed, proj_tf32=True)
+        thr = stk.calibrate_thresholds(model, inp["v0"], inp["x_conv"])
+        with torch.no_grad():
+            _v, ev = model.forward(inp["v0"], inp["x_conv"], thr)
+        dens = np.array([e / (cfg.B * cfg.L * cfg.D) for e, _ in ev])
+        assert np.all(np.abs(dens - 0.1) < 0.01), (spikes, dens)

@@ -24,8 +24,18 @@ def ref():
     return mods
 
 
+# one block of configs[4] at the top of its density sweep with bursty spikes:
+# B = 128, L = 4000, rho = 0.5 Markov: about a quarter of the channels hold
+# more than 2048 events (two chunk states)
+VARIANTS = {"c4_markov50": ("c4", dict(rho=0.5, spikes="markov"))}
+
+
 def _run_both(ref, cfg_name, rho=None):
-    cfg = CONFIGS[cfg_name] if rho is None else CONFIGS[cfg_name].with_(rho=rho)
+    if cfg_name in VARIANTS:
+        base, kw = VARIANTS[cfg_name]
+        cfg = CONFIGS[base].with_(**kw)
+    else:
+        cfg = CONFIGS[cfg_name] if rho is None else CONFIGS[cfg_name].with_(rho=rho)
     ops = load_ops()
     inp = make_inputs(cfg, device=dev)
     ee = ref["extract_events_cuda"]
@@ -47,9 +57,11 @@ def _run_both(ref, cfg_name, rho=None):
     return cfg, inp, ch, ts, kf, cu, int(mx), uf
 
 
-@pytest.mark.parametrize("cfg_name", ["c0", "c1", "c2", "c3"])
+@pytest.mark.parametrize("cfg_name", ["c0", "c1", "c2", "c3", "c4_markov50"])
 def test_against_reference_cuda(ref, cfg_name):
     cfg, inp, ch, ts, kf, cu, mx, uf = _run_both(ref, cfg_name)
+    if cfg_name == "c4_markov50":
+        assert mx > 2048   # multi-chunk channels are exercised
     ops = load_ops()
     ss = ref["selective_scan_cuda"]
     rd = ref["restore_dense_cuda_nodecay"]

@@ -92,6 +92,35 @@ def test_noalloc_matches_existing_entry_two_calls_in_a_row():
         assert torch.equal(got, want)
 
 
+def test_noalloc_call_allocates_no_device_memory():
+    """After a first call on the device (which may load the library's module
+    and with it the fixed array), a call changes neither the caching
+    allocator's counters nor the device's free memory: it allocates nothing."""
+    lib = _lib()
+    g, ch, t, n_ch, L = _case(CONFIGS["c0"].with_(B=4, D=128, L=777), torch.float32, shuffle=False, seed=13)
+    dx = _garbage(n_ch, L, g.dtype)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call():
+        st = lib.bcm_gather_events_bwd_noalloc(g.data_ptr(), DTYPES[g.dtype], ch.data_ptr(), t.data_ptr(),
+                                               ch.numel(), n_ch, L, dx.data_ptr(), stream)
+        assert st == 0, lib.bcm_last_error()
+
+    call()                      # warm: module loaded, symbol address cached
+    torch.cuda.synchronize()
+    alloc0, reserved0 = torch.cuda.memory_allocated(), torch.cuda.memory_reserved()
+    free0, _total = torch.cuda.mem_get_info()
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    free1, _total = torch.cuda.mem_get_info()
+    assert torch.cuda.memory_allocated() == alloc0
+    assert torch.cuda.memory_reserved() == reserved0
+    # a device allocation shows as at least one 2 MiB page of free memory gone
+    assert free1 >= free0 - (1 << 20), (free0, free1)
+    assert not torch.isnan(dx).any()
+
+
 def test_noalloc_rejects_more_channels_than_its_scratch_holds():
     lib = _lib()
     torch.zeros(1, device=dev)
