@@ -16,14 +16,20 @@ W_B / W_C the halves of W_BC (:321-324, 475-476), dt_idle / dt_active =
 softplus(a0 / a1) + 1e-6 (TwoLevelDelta, :210-230), the D skip (:326) and the
 out_proj weight (:336)).
 
-Spikes: block l thresholds its input membrane v_l (B, L, d_model) directly
-(strict >, as extraction compares) at theta_l, the (1 - rho) quantile of v_l
-calibrated once on the workload's data (``calibrate_thresholds``), so the
-density stays pinned at rho while the spike pattern comes from the layer's own
-membrane.  (The reference's spike head STE(sigmoid(prob_head(LN v)) >= theta)
-does not control density.)  The conv feeding the gather (in_proj, causal
-conv1d, SiLU; e_model.py:428-451) is outside the path: each block's x_conv
-(B, D, L) is an input of the step.
+Spikes: feature j of block l fires where its input membrane v_l[..., j]
+exceeds theta_l[j], the (1 - rho) quantile of that feature's membrane
+calibrated once on the workload's data (``calibrate_thresholds``): every
+feature fires at rate rho (the reference regularises each layer's rate
+towards a target, lra_impl.py SequenceClassifierBase target_rate) and the
+spike pattern comes from the layer's own membrane.  (The reference's spike
+head STE(sigmoid(prob_head(LN v)) >= theta) does not control density.)  The
+stack carries the membrane relative to the next block's thresholds,
+s_l = v_l - theta_l, so extraction compares s_l > 0 with the reference's
+scalar-threshold API and the offsets ride in out_proj's epilogue:
+s_{l+1} = leak*s_l + (y_l W_out^T + c_l), c_l = leak*theta_l - theta_{l+1}
+(theta after the last block = 0, so the stack's output is v itself).  The
+conv feeding the gather (in_proj, causal conv1d, SiLU; e_model.py:428-451) is
+outside the path: each block's x_conv (B, D, L) is an input of the step.
 
 Inputs are generated per GLOBAL batch row from that row's own seed, so a rank
 holding rows [b0, b1) of the global batch sees exactly the rows a single GPU
@@ -61,15 +67,16 @@ def event_path(v, x_conv, threshold: float, expand: int, dt_idle, dt_active, A, 
 
 
 class _Proj(torch.autograd.Function):
-    """out_proj: y (B, L, D) @ W_out^T -> (B, L, d_model), optionally with
-    TF32 tensor-core GEMMs in forward and backward."""
+    """out_proj: y (B, L, D) @ W_out^T + c -> (B, L, d_model) with a constant
+    per-feature offset c (no gradient), optionally with TF32 tensor-core GEMMs
+    in forward and backward."""
 
     @staticmethod
-    def forward(ctx, y, w, tf32: bool):
+    def forward(ctx, y, w, c, tf32: bool):
         ctx.save_for_backward(y, w)
         ctx.tf32 = tf32
         with _tf32(tf32 and y.is_cuda):
-            return F.linear(y, w)
+            return F.linear(y, w, c)
 
     @staticmethod
     def backward(ctx, g):
@@ -77,7 +84,7 @@ class _Proj(torch.autograd.Function):
         with _tf32(ctx.tf32 and y.is_cuda):
             dy = g @ w if ctx.needs_input_grad[0] else None
             dw = g.reshape(-1, g.shape[-1]).t() @ y.reshape(-1, y.shape[-1]) if ctx.needs_input_grad[1] else None
-        return dy, dw, None
+        return dy, dw, None, None
 
 
 class _tf32:
@@ -147,9 +154,10 @@ class EventStack:
     def all_params(self) -> List[torch.Tensor]:
         return [t for p in self.params for t in p.tensors()]
 
-    def block(self, l: int, v: torch.Tensor, x_conv: torch.Tensor, threshold: float):
-        """dv of block l for membrane v (B, L, d_model); returns (dv, the
-        path's (events, max_seqlen))."""
+    def block(self, l: int, s: torch.Tensor, x_conv: torch.Tensor, offset=None):
+        """Block l on its membrane relative to its thresholds, s (B, L,
+        d_model) (a feature fires where s > 0): returns (y W_out^T + offset,
+        the path's (events, max_seqlen))."""
         p = self.params[l]
         N = self.cfg.N
         A = -torch.exp(p.A_log)
@@ -157,18 +165,25 @@ class EventStack:
         W_C = p.W_BC[:, N:].contiguous()
         dt_idle = F.softplus(p.a0) + 1e-6
         dt_active = F.softplus(p.a1) + 1e-6
-        y_dense, events = self.path(v, x_conv, threshold, self.cfg.expand, dt_idle, dt_active, A, W_B, W_C, p.D)
-        return _Proj.apply(y_dense, p.W_out, self.proj_tf32), events
+        y_dense, events = self.path(s, x_conv, 0.0, self.cfg.expand, dt_idle, dt_active, A, W_B, W_C, p.D)
+        return _Proj.apply(y_dense, p.W_out, offset, self.proj_tf32), events
 
-    def forward(self, v0: torch.Tensor, x_convs: Sequence[torch.Tensor], thresholds: Sequence[float]):
-        """Membrane after the stack and (events, max_seqlen) of every block."""
-        v = v0
+    def offsets(self, thetas: Sequence[torch.Tensor]) -> List[torch.Tensor]:
+        """c_l = leak*theta_l - theta_{l+1} (theta after the last block = 0)."""
+        n = self.cfg.blocks
+        return [(self.leak * thetas[l] - (thetas[l + 1] if l + 1 < n else 0.0)).contiguous() for l in range(n)]
+
+    def forward(self, v0: torch.Tensor, x_convs: Sequence[torch.Tensor], thetas: Sequence[torch.Tensor]):
+        """Membrane after the stack and (events, max_seqlen) of every block;
+        thetas[l] (d_model,) are block l's firing thresholds."""
+        c = self.offsets(thetas)
+        s = v0 - thetas[0]
         events = []
         for l in range(self.cfg.blocks):
-            dv, e = self.block(l, v, x_convs[l], thresholds[l])
-            v = self.leak * v + dv
+            dv, e = self.block(l, s, x_convs[l], c[l])
+            s = torch.add(dv, s, alpha=self.leak)
             events.append(e)
-        return v, events
+        return s, events
 
 
 # ------------------------------------------------------------------ data ----
@@ -209,37 +224,38 @@ def stack_inputs(cfg: Config, rows: range, device, dtype=torch.float32) -> dict:
 
 
 # ----------------------------------------------------------- thresholds ----
-def _row_sample(v: torch.Tensor, t_stride: int = 8, f_stride: int = 4) -> torch.Tensor:
-    """The same positions of every row (so the union over ranks does not
-    depend on how rows are sharded)."""
-    return v[:, ::t_stride, ::f_stride].reshape(-1).float()
+def _row_sample(v: torch.Tensor, t_stride: int = 4) -> torch.Tensor:
+    """(d_model, n) sample of v (b, L, d_model): the same positions of every
+    row, so the union over ranks does not depend on how rows are sharded."""
+    return v[:, ::t_stride, :].reshape(-1, v.shape[-1]).t().float().contiguous()
 
 
-def global_quantile(v: torch.Tensor, q: float, group=None, gather: bool = True) -> float:
-    """q-quantile (an order statistic) of a fixed per-row sample of v over
-    every rank's rows (gather=False: this process's rows only)."""
+def feature_quantiles(v: torch.Tensor, q: float, group=None, gather: bool = True) -> torch.Tensor:
+    """Per-feature q-quantile (an order statistic) of a fixed per-row sample
+    of v over every rank's rows (gather=False: this process's rows only)."""
     import torch.distributed as dist
 
     s = _row_sample(v)
     if gather and dist.is_available() and dist.is_initialized():
         parts = [torch.empty_like(s) for _ in range(dist.get_world_size(group))]
         dist.all_gather(parts, s, group=group)
-        s = torch.cat(parts)
-    n = s.numel()
+        s = torch.cat(parts, dim=1)
+    n = s.shape[1]
     k = max(1, min(n, int(round(q * n))))
-    return float(s.kthvalue(k).values)
+    return s.kthvalue(k, dim=1).values.to(v.dtype)
 
 
 @torch.no_grad()
 def calibrate_thresholds(stack: EventStack, v0: torch.Tensor, x_convs: Sequence[torch.Tensor],
-                         rho: Optional[float] = None, group=None, gather: bool = True) -> List[float]:
-    """theta_l = the (1 - rho) quantile of block l's input membrane, block by
-    block (each block's membrane depends on the thresholds before it)."""
+                         rho: Optional[float] = None, group=None, gather: bool = True) -> List[torch.Tensor]:
+    """theta_l[j] = the (1 - rho) quantile of feature j of block l's input
+    membrane, block by block (each block's membrane depends on the
+    thresholds before it)."""
     rho = stack.cfg.rho if rho is None else rho
     v = v0
     th = []
     for l in range(stack.cfg.blocks):
-        th.append(global_quantile(v, 1.0 - rho, group, gather))
-        dv, _ = stack.block(l, v, x_convs[l], th[-1])
+        th.append(feature_quantiles(v, 1.0 - rho, group, gather))
+        dv, _ = stack.block(l, (v - th[-1]).contiguous(), x_convs[l])
         v = stack.leak * v + dv
     return th

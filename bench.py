@@ -381,7 +381,10 @@ def run_stack(args, cfg, rank, world, local, dev):
                    "global_batch": cfg.B, "seq_len": cfg.L, "blocks": cfg.blocks,
                    "events_per_step_all_ranks": E_all, "events_per_block_rank0": [e for e, _ in ev],
                    "max_seqlen_per_block_rank0": [mx for _, mx in ev],
-                   "density_per_block_rank0": dens, "thresholds": thr,
+                   "density_per_block_rank0": dens,
+                   "thresholds": "per feature, calibrated per block to the (1 - rho) quantile of the "
+                                 "block's input membrane (range per block: "
+                                 + ", ".join(f"[{float(t.min()):.3g}, {float(t.max()):.3g}]" for t in thr) + ")",
                    "parallelism": f"dp{world} (batch rows sharded, one gradient all-reduce per block)",
                    "l2": "256 MiB memset flush before every timed step, outside its window; inputs > L2"},
         "e2e": e2e,

@@ -51,7 +51,7 @@ def test_stack_matches_oracle(spikes, rho):
 
     cpu = stk.EventStack(cfg, "cpu", seed=cfg.seed, path=cpu_path, dtype=torch.float64)
     xs_c = [x.detach().double().cpu().requires_grad_(True) for x in inp["x_conv"]]
-    v_c, ev_c = cpu.forward(inp["v0"].double().cpu(), xs_c, thr)
+    v_c, ev_c = cpu.forward(inp["v0"].double().cpu(), xs_c, [t.double().cpu() for t in thr])
     v_c.backward(inp["dout"].double().cpu())
 
     assert [e for e, _ in ev] == [e for e, _ in ev_c]
@@ -67,8 +67,9 @@ def test_stack_matches_oracle(spikes, rho):
 
 
 def test_stack_thresholds_pin_density_at_full_rows():
-    """At the benchmark's row length and width the calibrated thresholds give
-    the target density in every block (one shard of 8 rows)."""
+    """At the benchmark's row length and width the calibrated per-feature
+    thresholds give the target density in every block (one shard of 8 rows),
+    and no channel fires far more often than the rest."""
     from bc_mamba_b200 import stack as stk
     from bc_mamba_b200.workloads import CONFIGS
 
@@ -79,5 +80,8 @@ def test_stack_thresholds_pin_density_at_full_rows():
         thr = stk.calibrate_thresholds(model, inp["v0"], inp["x_conv"])
         with torch.no_grad():
             _v, ev = model.forward(inp["v0"], inp["x_conv"], thr)
+        # a channel's count is about rho * L: the busiest stays within 2x
+        assert all(mx < 2 * 0.1 * cfg.L for _, mx in ev), [mx for _, mx in ev]
         dens = np.array([e / (cfg.B * cfg.L * cfg.D) for e, _ in ev])
-        assert np.all(np.abs(dens - 0.1) < 0.01), (spikes, dens)
+        # each feature's threshold is an order statistic of 8 x 1000 samples
+        assert np.all(np.abs(dens - 0.1) < 0.02), (spikes, dens)
