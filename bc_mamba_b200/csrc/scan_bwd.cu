@@ -561,24 +561,41 @@ bcm_status launch_bwd(const ScanArgs& a, bool dw, bool has_z, cudaStream_t st) {
     }
 }
 
+// Workspace of the backward: [checkpoints (staged kernels) | decay tables +
+// tile carries (event-parallel kernels)] [per-row parameter partials]
+// [W_B/W_C mixed by pw] [their gradients].
 struct BwdLayout {
     size_t ckpt_off, ckpt_bytes, part_off, part_bytes, weff_off, weff_bytes, dweff_off, total;
-    int NP, part_stride;
+    size_t tab_off, carry_off;
+    int NP, part_stride, part_rows;
+    bool seg;
 };
 
 BwdLayout bwd_layout(const bcm_flat_ch_args* p) {
     BwdLayout L{};
+    ScanArgs a;
+    scan_fill_args(p, a);
+    L.seg = p->n_events > 0 && seg_supported(a);
     int G, LPC;
     pick_layout((int)p->dstate, G, LPC);
     L.NP = G * LPC;
     if (p->bc_mode == BCM_BC_DEPTHWISE && dw_fast_supported((int)p->dstate))
         L.NP = dw_fast_np((int)p->dstate);
-    L.part_stride = (3 * L.NP + 3 + 3) / 4 * 4;
-    const size_t slots = (size_t)(p->n_events >> 3) + (size_t)p->n_channels + 1;
+    L.part_rows = (int)p->n_channels;
     L.ckpt_off = 0;
-    L.ckpt_bytes = align_up(slots * L.NP * sizeof(float), 256);
+    if (L.seg) {
+        L.NP = (int)p->dstate;
+        L.part_rows = seg_part_rows(a);
+        L.tab_off = 0;
+        L.carry_off = seg_table_bytes(a);
+        L.ckpt_bytes = L.carry_off + seg_carry_bytes(a);
+    } else {
+        const size_t slots = (size_t)(p->n_events >> 3) + (size_t)p->n_channels + 1;
+        L.ckpt_bytes = align_up(slots * L.NP * sizeof(float), 256);
+    }
+    L.part_stride = (3 * L.NP + 3 + 3) / 4 * 4;
     L.part_off = L.ckpt_off + L.ckpt_bytes;
-    L.part_bytes = align_up((size_t)p->n_channels * L.part_stride * sizeof(float), 256);
+    L.part_bytes = align_up((size_t)L.part_rows * L.part_stride * sizeof(float), 256);
     L.weff_off = L.part_off + L.part_bytes;
     L.weff_bytes = p->pw_B ? align_up((size_t)2 * p->dim * p->dstate * sizeof(float), 256) : 0;
     L.dweff_off = L.weff_off + L.weff_bytes;
@@ -629,8 +646,12 @@ extern "C" bcm_status bcm_flat_ch_bwd(const bcm_flat_ch_args* p, cudaStream_t st
         a.B = WB_eff;
         a.C = WC_eff;
     }
-    // every channel writes its partial row, so no clearing is needed
-    if (p->n_events > 0 && dw && dw_fast_supported(a.dstate)) {
+    // every channel (warp group) writes its partial row, so no clearing is needed
+    if (L.seg) {
+        st = seg_bwd_launch(a, p->dtype, reinterpret_cast<float*>(ws + L.tab_off), a.ckpt,
+                            reinterpret_cast<float*>(ws + L.carry_off), stream);
+        if (st != BCM_OK) return st;
+    } else if (p->n_events > 0 && dw && dw_fast_supported(a.dstate)) {
         st = dw_fast_launch(a, p->dtype, true, stream);
         if (st != BCM_OK) return st;
     } else if (p->n_events > 0) {
@@ -659,7 +680,7 @@ extern "C" bcm_status bcm_flat_ch_bwd(const bcm_flat_ch_args* p, cudaStream_t st
         const int total = dim * (3 * N + 3);
         const int threads = 256;
         reduce_parts_kernel<<<ceil_div(total, threads), threads, 0, stream>>>(
-            a.ws_part, L.part_stride, L.NP, (int)p->n_channels, dim, N, p->dA, dWB_target,
+            a.ws_part, L.part_stride, L.NP, L.part_rows, dim, N, p->dA, dWB_target,
             dWC_target, dw ? 1 : 0, want_B, want_C, p->ddt_idle, p->ddt_active, p->dD);
         BCM_LAUNCH_CHECK();
     }

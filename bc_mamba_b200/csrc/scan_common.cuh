@@ -140,4 +140,17 @@ bcm_status v3_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t 
 int v3_ckpt_np(int dstate);
 size_t v3_ckpt_bytes(const ScanArgs& a);
 
+// Event-parallel kernels (scan_seg.cu): depthwise, no gate, dstate <= 64.
+// The forward needs a decay-table workspace of seg_table_bytes and writes the
+// state entering every tile into the checkpoint buffer (seg_carry_bytes);
+// the backward needs the same table, the carries (from the forward, or it
+// writes them into carry_ws itself) and seg_part_rows partial rows.
+bool seg_supported(const ScanArgs& a);
+size_t seg_table_bytes(const ScanArgs& a);
+size_t seg_carry_bytes(const ScanArgs& a);
+int seg_part_rows(const ScanArgs& a);
+bcm_status seg_fwd_launch(const ScanArgs& a, bcm_dtype dtype, float* table_ws, float* carries, cudaStream_t st);
+bcm_status seg_bwd_launch(const ScanArgs& a, bcm_dtype dtype, float* table_ws, const float* fwd_carries,
+                          float* carry_ws, cudaStream_t st);
+
 }  // namespace bcm

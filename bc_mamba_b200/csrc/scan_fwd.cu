@@ -286,7 +286,7 @@ void scan_fill_args(const bcm_flat_ch_args* p, ScanArgs& a) {
     a.du = p->du; a.dB_ev = nullptr; a.dC_ev = nullptr; a.dz = p->dz;
     a.ws_ckpt = nullptr; a.ws_part = nullptr; a.part_stride = 0;
     a.ckpt = nullptr;
-    if (p->ckpt != nullptr && v3_ckpt_bytes(a) > 0) a.ckpt = p->ckpt;   // else ignored
+    if (p->ckpt != nullptr && (seg_supported(a) || v3_ckpt_bytes(a) > 0)) a.ckpt = p->ckpt;   // else ignored
 }
 
 bcm_status scan_launch_pw_mix(const bcm_flat_ch_args* p, float* WB_eff, float* WC_eff,
@@ -306,15 +306,27 @@ bcm_status scan_launch_pw_mix(const bcm_flat_ch_args* p, float* WB_eff, float* W
 
 using namespace bcm;
 
+// Forward workspace: [W_B/W_C mixed by pw (pw only)] [decay tables (event-parallel kernels)]
+static size_t fwd_pw_bytes(const bcm_flat_ch_args* p) {
+    return p->pw_B == nullptr ? 0 : align_up((size_t)(2 * p->dim * p->dstate * sizeof(float)), 256);
+}
+
+static bool fwd_seg(const bcm_flat_ch_args* p, ScanArgs& a) {
+    if (p->n_events <= 0 || p->n_channels <= 0 || p->dim <= 0 || p->dstate <= 0) return false;
+    scan_fill_args(p, a);
+    return seg_supported(a);
+}
+
 extern "C" size_t bcm_flat_ch_fwd_workspace_bytes(const bcm_flat_ch_args* p) {
-    if (!p || p->pw_B == nullptr) return 0;
-    return align_up((size_t)(2 * p->dim * p->dstate * sizeof(float)), 256);
+    if (!p) return 0;
+    ScanArgs a;
+    return fwd_pw_bytes(p) + (fwd_seg(p, a) ? seg_table_bytes(a) : 0);
 }
 
 extern "C" size_t bcm_flat_ch_ckpt_bytes(const bcm_flat_ch_args* p) {
     if (!p || p->n_events <= 0 || p->n_channels <= 0 || p->dim <= 0 || p->dstate <= 0) return 0;
     ScanArgs a;
-    scan_fill_args(p, a);
+    if (fwd_seg(p, a)) return seg_carry_bytes(a);
     return v3_ckpt_bytes(a);
 }
 
@@ -324,12 +336,12 @@ extern "C" bcm_status bcm_flat_ch_fwd(const bcm_flat_ch_args* p, cudaStream_t st
     if (st != BCM_OK) return st;
     ScanArgs a;
     scan_fill_args(p, a);
+    const size_t need = bcm_flat_ch_fwd_workspace_bytes(p);
+    if (need > 0 && (!p->workspace || p->workspace_bytes < need)) {
+        set_error("flat_ch fwd: workspace of %zu bytes < required %zu", p->workspace_bytes, need);
+        return BCM_ERR_WORKSPACE;
+    }
     if (p->pw_B) {
-        const size_t need = bcm_flat_ch_fwd_workspace_bytes(p);
-        if (!p->workspace || p->workspace_bytes < need) {
-            set_error("flat_ch fwd: workspace of %zu bytes < required %zu", p->workspace_bytes, need);
-            return BCM_ERR_WORKSPACE;
-        }
         float* WB_eff = static_cast<float*>(p->workspace);
         float* WC_eff = WB_eff + p->dim * p->dstate;
         st = scan_launch_pw_mix(p, WB_eff, WC_eff, stream);
@@ -339,6 +351,11 @@ extern "C" bcm_status bcm_flat_ch_fwd(const bcm_flat_ch_args* p, cudaStream_t st
     }
     const bool dw = p->bc_mode == BCM_BC_DEPTHWISE;
     const bool has_z = p->z != nullptr;
+    if (p->n_events > 0 && seg_supported(a)) {
+        // event-parallel kernels: write every slot of x themselves
+        float* tab = reinterpret_cast<float*>(static_cast<char*>(p->workspace) + fwd_pw_bytes(p));
+        return seg_fwd_launch(a, p->dtype, tab, a.ckpt, stream);
+    }
     // x is written in full: the staged forward writes every slot itself,
     // every other path writes the chunks that exist onto zeros
     const bool staged = p->n_events > 0 && dw && dw_fast_supported(a.dstate) && v3_supported(a, false);

@@ -1,0 +1,116 @@
+"""GPU parity of the event-parallel depthwise scan kernels (scan_seg.cu)
+against the float64 oracle: warp groups of 1..16 batch rows (BCM_SEG_CPW pins
+the group size, which at these sizes would otherwise be 1), ragged, empty and
+one-event channels, channels spanning many 256-event tiles and several
+2048-event chunks, gaps past the 256-row decay table, every dstate up to 64,
+16-bit inputs, and the backward with and without the forward's tile carries
+(bit-identical to each other).  Tolerance as test_gpu_scan.py."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import TOL_16, TOL_F32
+from test_gpu_scan import _events, _params, _run_and_check
+from bc_mamba_b200.workloads import CONFIGS
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def cpw(request):
+    old = os.environ.get("BCM_SEG_CPW")
+    os.environ["BCM_SEG_CPW"] = str(request.param)
+    yield request.param
+    if old is None:
+        os.environ.pop("BCM_SEG_CPW", None)
+    else:
+        os.environ["BCM_SEG_CPW"] = old
+
+
+def _ragged(B, D, N, seed, lo=0, hi=90, kmax=9, big_gap_every=0):
+    rng = np.random.default_rng(seed)
+    NC = B * D
+    n = rng.integers(lo, hi, NC)
+    n[::5] = 0
+    n[1::7] = 1
+    cu = np.zeros(NC + 1, np.int32)
+    cu[1:] = np.cumsum(n)
+    E = int(cu[-1])
+    k = rng.integers(1, kmax, E).astype(np.int32)
+    if big_gap_every:
+        k[::big_gap_every] = rng.integers(257, 900, k[::big_gap_every].size)
+    u = rng.standard_normal(E).astype(np.float32)
+    return u, k, cu, int(n.max())
+
+
+@pytest.mark.parametrize("cpw", [1, 3, 16], indirect=True)
+def test_seg_ragged_groups(cpw):
+    B, D, N = 16, 4, 16
+    u, k, cu, mx = _ragged(B, D, N, seed=3)
+    dti, dta, A, WB, WC, Dv = _params(D, N, 3)
+    _run_and_check(u, k, cu, mx, dti, dta, A, WB, WC, D=Dv)
+
+
+@pytest.mark.parametrize("cpw", [2, 8], indirect=True)
+def test_seg_tiny_channels_many_per_lane(cpw):
+    """Channels of 0..5 events: a lane's 8 events cross several channels."""
+    B, D, N = 32, 2, 16
+    u, k, cu, mx = _ragged(B, D, N, seed=4, lo=0, hi=6)
+    dti, dta, A, WB, WC, Dv = _params(D, N, 4)
+    _run_and_check(u, k, cu, mx, dti, dta, A, WB, WC, D=Dv)
+
+
+@pytest.mark.parametrize("cpw", [1, 4], indirect=True)
+def test_seg_gaps_past_table(cpw):
+    B, D, N = 8, 4, 16
+    u, k, cu, mx = _ragged(B, D, N, seed=5, lo=20, hi=400, big_gap_every=7)
+    dti, dta, A, WB, WC, Dv = _params(D, N, 5)
+    _run_and_check(u, k, cu, mx, 0.01 * dti, 0.01 * dta, A, WB, WC, D=Dv)
+
+
+@pytest.mark.parametrize("cpw", [1, 2], indirect=True)
+def test_seg_multi_chunk_channels(cpw):
+    """Channels of up to ~4800 events: many tiles and three x chunks."""
+    c = CONFIGS["c0"].with_(B=4, D=4, N=16, L=6000, rho=0.8, seed=23)
+    inp, ch, t, k, cu, mx, u = _events(c)
+    assert mx > 4096
+    dti, dta, A, WB, WC, Dv = _params(c.D, c.N, 23)
+    res, _ = _run_and_check(u, k, cu, mx, dti, dta, A, WB, WC, D=Dv)
+    assert res[1].shape[1] == (mx + 2047) // 2048
+
+
+@pytest.mark.parametrize("N", [1, 3, 8, 16, 33, 64])
+def test_seg_dstates(N):
+    c = CONFIGS["c0"].with_(B=4, D=8, N=N, L=700, rho=0.3, seed=60 + N)
+    inp, ch, t, k, cu, mx, u = _events(c)
+    dti, dta, A, WB, WC, Dv = _params(c.D, N, N)
+    _run_and_check(u, k, cu, mx, dti, dta, A, WB, WC, D=Dv)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_seg_16bit(dtype):
+    c = CONFIGS["c0"].with_(B=4, D=8, N=16, L=900, rho=0.3, seed=61)
+    inp, ch, t, k, cu, mx, u = _events(c)
+    dti, dta, A, WB, WC, Dv = _params(c.D, c.N, 61)
+    _run_and_check(u, k, cu, mx, dti, dta, A, WB, WC, D=Dv, dtype=dtype, tol=TOL_16)
+
+
+def test_seg_no_skip_and_pw_mixing():
+    c = CONFIGS["c0"].with_(B=4, D=8, N=16, L=600, rho=0.3, seed=62)
+    inp, ch, t, k, cu, mx, u = _events(c)
+    dti, dta, A, WB, WC, _ = _params(c.D, c.N, 62)
+    rng = np.random.default_rng(62)
+    pw = (rng.standard_normal((c.D, c.D)).astype(np.float32) * 0.3,
+          rng.standard_normal((c.D, c.D)).astype(np.float32) * 0.3)
+    _run_and_check(u, k, cu, mx, dti, dta, A, WB, WC, D=None, pw=pw)
+
+
+def test_seg_bench_shape_rows():
+    """The c4 row layout (128 rows per feature, density 10 %) on a short
+    sequence, with the group size the kernels pick themselves."""
+    c = CONFIGS["c4"].with_(D=4, L=600)
+    inp, ch, t, k, cu, mx, u = _events(c)
+    p = lambda n: inp[n].numpy()
+    _run_and_check(u, k, cu, mx, p("dt_idle"), p("dt_active"), p("A"), p("W_B"), p("W_C"), D=p("D"))
