@@ -342,22 +342,19 @@ __device__ __forceinline__ int lower_bound8(const int32_t* __restrict__ a, int n
     return lo + c;
 }
 
-// ---- tile forward --------------------------------------------------------------
+// ---- sweep forward -------------------------------------------------------------
 // A warp owns one batch row b, 32 features (lane = channel) and a range of
-// positions (whole 64-row windows).  Per window the events of its 32 channels
-// are loaded coalesced, channel by channel (32 events per load, lane = event),
-// and scattered into a shared-memory tile of (value, flag) pairs
-// [row][channel] (pitch 33: the scatter of one channel's rows and the row
-// reads are conflict-free); the sweep then reads its row of the tile (lane =
-// channel), holds or replaces the value, stores the 32 features of the row
-// with one coalesced store, clears the slot and collects the event bits into
-// the bitmap words.  The first load of the next window's events is issued
-// before the sweep.  Per unit it also records the local index of its first
-// event for the backward.
-constexpr int kFW = 2;        // warps (units) per CTA
-constexpr int kTW = 64;       // rows per window
-constexpr int kTP = 33;       // tile pitch (float2 slots)
-constexpr int kSweepWarpsPerSM = 12;
+// positions [t_beg, t_end) (whole 32-position words).  Each lane finds its
+// channel's first event at or after t_beg, then keeps the times and values of
+// its next kQ events in registers, loaded kQ events ahead so every load has
+// kQ gaps' worth of positions to arrive.  Per position the lane holds or
+// replaces its value and the warp stores one coalesced row of 32 features;
+// per 32 positions each lane stores its word of event bits (the bitmap the
+// backward sweeps), and the unit records its lanes' first event indices.
+// No shared memory and few registers, so many units run per SM.
+constexpr int kQ = 4;               // events held ahead per lane
+constexpr int kFU = 4;              // units (warps) per CTA
+constexpr int kSweepUnitsPerSM = 48;
 
 struct SweepLayout {
     int n_dblk, part_len, n_parts;
@@ -365,20 +362,13 @@ struct SweepLayout {
 };
 
 template <typename Tin, typename Tout>
-__global__ void __launch_bounds__(kFW * 32)
-restore_fwd_tile(const Tin* __restrict__ y, const int32_t* __restrict__ ts, const int32_t* __restrict__ cu,
-                 int D, int L, int nw, int part_len, int n_dblk, int n_parts, int64_t n_units,
-                 Tout* __restrict__ out, uint32_t* __restrict__ bm, int32_t* __restrict__ e_start) {
-    __shared__ float2 s_tile[kFW][kTW * kTP];
-    __shared__ int s_e[kFW][32];    // next unconsumed event of each channel (global index)
-    __shared__ int s_end[kFW][32];  // end of each channel's addressable events (global index)
-    const int w_in = threadIdx.x >> 5;
-    const int64_t unit = (int64_t)blockIdx.x * kFW + w_in;
+__global__ void __launch_bounds__(kFU * 32)
+restore_fwd_sweep(const Tin* __restrict__ y, const int32_t* __restrict__ ts, const int32_t* __restrict__ cu,
+                  int D, int L, int nw, int part_len, int n_dblk, int n_parts, int64_t n_units,
+                  Tout* __restrict__ out, uint32_t* __restrict__ bm, int32_t* __restrict__ e_start) {
+    const int64_t unit = (int64_t)blockIdx.x * kFU + (threadIdx.x >> 5);
     if (unit >= n_units) return;   // warp-uniform; the kernel has no block barrier
     const int lane = threadIdx.x & 31;
-    float2* tile = s_tile[w_in];
-    int* se = s_e[w_in];
-    int* send = s_end[w_in];
     const BUnit u = bunit(unit, n_dblk, n_parts, part_len, L);
     const int d = u.d0 + lane;
     const bool valid = d < D;
@@ -388,75 +378,43 @@ restore_fwd_tile(const Tin* __restrict__ y, const int32_t* __restrict__ ts, cons
         beg = cu[c];
         n = min(cu[c + 1] - beg, kCap);
     }
-    const int p = (u.t_beg == 0) ? 0 : lower_bound8(ts + beg, n, u.t_beg);
-    float cur = (p > 0) ? to_f32<Tin>(y[beg + p - 1]) : 0.f;
+    const int p = (u.t_beg == 0 || n <= 0) ? 0 : lower_bound8(ts + beg, n, u.t_beg);
     if (e_start != nullptr) e_start[unit * 32 + lane] = p;
-    se[lane] = beg + p;
-    send[lane] = beg + n;
-    for (int i = lane; i < kTW * kTP; i += 32) tile[i] = make_float2(0.f, 0.f);
-    __syncwarp();
-
-    // first 32 events of every channel from its next unconsumed event
-    int pt[32];
-    float pv[32];
-    auto prefetch = [&]() {
+    float cur = (p > 0) ? to_f32<Tin>(y[beg + p - 1]) : 0.f;
+    int tq[kQ];
+    float yq[kQ];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-            const int j = se[c] + lane;
-            const bool in = j < send[c];
-            pt[c] = in ? ts[j] : INT_MAX;
-            pv[c] = in ? to_f32<Tin>(y[j]) : 0.f;
-        }
-    };
-    prefetch();
+    for (int q = 0; q < kQ; ++q) {
+        const int j = p + q;
+        tq[q] = (j < n) ? ts[beg + j] : INT_MAX;
+        yq[q] = (j < n) ? to_f32<Tin>(y[beg + j]) : 0.f;
+    }
+    int nxt = p + kQ;
     Tout* col = out + (u.b * L + u.t_beg) * (int64_t)D + (valid ? d : 0);
     uint32_t* mcol = (bm != nullptr) ? bm + (u.b * nw + (u.t_beg >> 5)) * (int64_t)D + d : nullptr;
-    for (int t0 = u.t_beg; t0 < u.t_end; t0 += kTW) {
-        const int wend = min(t0 + kTW, u.t_end);
-        // 1. scatter this window's events into the tile (channel by channel)
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-            const bool in = pt[c] < wend;
-            if (in) tile[(pt[c] - t0) * kTP + c] = make_float2(pv[c], 1.f);
-            int taken = __popc(__ballot_sync(kFull, in));
-            if (taken == 32) {   // a dense window: more events of this channel
-                int e = se[c] + 32;
-                const int end = send[c];
-                while (true) {
-                    const int j = e + lane;
-                    const int tt = j < end ? ts[j] : INT_MAX;
-                    const bool in2 = tt < wend;
-                    if (in2) tile[(tt - t0) * kTP + c] = make_float2(to_f32<Tin>(y[j]), 1.f);
-                    const int k2 = __popc(__ballot_sync(kFull, in2));
-                    taken += k2;
-                    e += 32;
-                    if (k2 < 32) break;
-                }
-            }
-            if (lane == 0) se[c] += taken;
-        }
-        __syncwarp();
-        if (t0 + kTW < u.t_end) prefetch();   // next window's first loads, in flight during the sweep
-        // 2. sweep: lane = channel, one coalesced row store per position
+    for (int t0 = u.t_beg; t0 < u.t_end; t0 += 32) {
         uint32_t m = 0u;
+        const int rows = min(32, u.t_end - t0);
+#pragma unroll 8
+        for (int r = 0; r < 32; ++r) {
+            if (r >= rows) break;   // warp-uniform
+            if (t0 + r == tq[0]) {
+                cur = yq[0];
 #pragma unroll
-        for (int r = 0; r < kTW; ++r) {
-            const int t = t0 + r;
-            float2* slot = tile + r * kTP + lane;
-            const float2 sv = *slot;
-            *slot = make_float2(0.f, 0.f);
-            const bool hit = sv.y != 0.f;
-            cur = hit ? sv.x : cur;
-            m |= (hit ? 1u : 0u) << (r & 31);
-            if (valid && t < wend) col[(int64_t)r * D] = from_f32<Tout>(cur);
-            if ((r & 31) == 31) {
-                if (mcol != nullptr && valid && t - 31 < wend) mcol[(int64_t)(r >> 5) * D] = m;
-                m = 0u;
+                for (int q = 0; q + 1 < kQ; ++q) {
+                    tq[q] = tq[q + 1];
+                    yq[q] = yq[q + 1];
+                }
+                tq[kQ - 1] = (nxt < n) ? ts[beg + nxt] : INT_MAX;
+                yq[kQ - 1] = (nxt < n) ? to_f32<Tin>(y[beg + nxt]) : 0.f;
+                ++nxt;
+                m |= 1u << r;
             }
+            if (valid) col[(int64_t)r * D] = from_f32<Tout>(cur);
         }
-        __syncwarp();
-        col += (int64_t)kTW * D;
-        if (mcol != nullptr) mcol += (int64_t)(kTW / 32) * D;
+        if (mcol != nullptr && valid) *mcol = m;
+        col += (int64_t)32 * D;
+        if (mcol != nullptr) mcol += D;
     }
 }
 
@@ -495,22 +453,21 @@ restore_bwd_bitmap(const T* __restrict__ dout, const int32_t* __restrict__ cu, c
     int open = -1;          // owned event whose interval is running
     float acc = 0.f;
     const T* col = dout + (u.b * L + u.t_beg) * (int64_t)D + dc;
-    for (int t0 = u.t_beg; t0 < L; t0 += 64) {
+    for (int t0 = u.t_beg; t0 < L; t0 += 32) {
         if (t0 >= u.t_end && !__any_sync(kFull, open >= 0)) break;
         const uint32_t m0 = valid ? mcol[(int64_t)(t0 >> 5) * D] : 0u;
-        const uint32_t m1 = (valid && t0 + 32 < L) ? mcol[(int64_t)((t0 >> 5) + 1) * D] : 0u;
-        float v[64];
-        if (t0 + 64 <= L) {
+        float v[32];
+        if (t0 + 32 <= L) {
 #pragma unroll
-            for (int r = 0; r < 64; ++r) v[r] = to_f32<T>(col[(int64_t)r * D]);
+            for (int r = 0; r < 32; ++r) v[r] = to_f32<T>(col[(int64_t)r * D]);
         } else {
 #pragma unroll
-            for (int r = 0; r < 64; ++r) v[r] = (t0 + r < L) ? to_f32<T>(col[(int64_t)r * D]) : 0.f;
+            for (int r = 0; r < 32; ++r) v[r] = (t0 + r < L) ? to_f32<T>(col[(int64_t)r * D]) : 0.f;
         }
-        col += (int64_t)64 * D;
+        col += (int64_t)32 * D;
 #pragma unroll
-        for (int r = 0; r < 64; ++r) {
-            const bool hit = (((r < 32 ? m0 : m1) >> (r & 31)) & 1u) != 0u;
+        for (int r = 0; r < 32; ++r) {
+            const bool hit = ((m0 >> r) & 1u) != 0u;
             if (hit && open >= 0) dy[open] = acc;   // an event starts here: the running interval ends
             open = hit ? ((t0 + r < u.t_end) ? e : -1) : open;
             e += hit ? 1 : 0;
@@ -534,19 +491,18 @@ static int restore_part_len(int64_t n_blocks_2d, int64_t L) {
     return (int)std::min<int64_t>(len, std::max<int64_t>((L + kTT - 1) / kTT * kTT, kTT));
 }
 
-// Unit layout of the tile forward and the bitmap backward (shared, so that
+// Unit layout of the sweep forward and the bitmap backward (shared, so that
 // the backward can read the forward's per-unit start indices): warp units of
-// 32 features x part_len positions (whole 64-row windows), as many as the SMs
-// hold at once (kSweepWarpsPerSM warps each), more only when the batch rows
-// alone exceed that.
+// 32 features x part_len positions (whole 32-position words), about
+// kSweepUnitsPerSM per SM, more only when the batch rows alone exceed that.
 static SweepLayout sweep_layout(int64_t B, int64_t D, int64_t L) {
     SweepLayout s;
     s.n_dblk = (int)((D + 31) / 32);
     const int64_t cols = B * s.n_dblk;
-    const int64_t cap = (int64_t)sm_count() * kSweepWarpsPerSM;
-    const int64_t parts = std::max<int64_t>(1, cap / std::max<int64_t>(1, cols));
+    const int64_t target = (int64_t)sm_count() * kSweepUnitsPerSM;
+    const int64_t parts = std::max<int64_t>(1, (target + cols - 1) / std::max<int64_t>(1, cols));
     int64_t len = (L + parts - 1) / parts;
-    len = std::max<int64_t>(kTW, (len + kTW - 1) / kTW * kTW);
+    len = std::max<int64_t>(32, (len + 31) / 32 * 32);
     s.part_len = (int)len;
     s.n_parts = (int)((L + len - 1) / len);
     s.n_units = cols * s.n_parts;
@@ -572,7 +528,7 @@ static bcm_status restore_fwd_impl(const void* y_flat, bcm_dtype y_dtype, const 
                 "restore_dense_fwd: null pointer");
     const int64_t B = n_channels / dim;
     const SweepLayout lay = sweep_layout(B, dim, seqlen);
-    BCM_REQUIRE((lay.n_units + kFW - 1) / kFW < (1ll << 31), "restore_dense_fwd: too many units");
+    BCM_REQUIRE((lay.n_units + kFU - 1) / kFU < (1ll << 31), "restore_dense_fwd: too many units");
     const int nw = (int)((seqlen + 31) / 32);
     // the per-unit start indices follow the bitmap words
     int32_t* e_start = bitmap ? reinterpret_cast<int32_t*>(reinterpret_cast<char*>(bitmap) +
@@ -581,7 +537,7 @@ static bcm_status restore_fwd_impl(const void* y_flat, bcm_dtype y_dtype, const 
     auto launch = [&](auto tin, auto tout) -> bcm_status {
         using Tin = decltype(tin);
         using Tout = decltype(tout);
-        restore_fwd_tile<Tin, Tout><<<(unsigned)((lay.n_units + kFW - 1) / kFW), kFW * 32, 0, stream>>>(
+        restore_fwd_sweep<Tin, Tout><<<(unsigned)((lay.n_units + kFU - 1) / kFU), kFU * 32, 0, stream>>>(
             static_cast<const Tin*>(y_flat), time_steps, cu_seqlens, (int)dim, (int)seqlen, nw, lay.part_len,
             lay.n_dblk, lay.n_parts, lay.n_units, static_cast<Tout*>(out), bitmap, e_start);
         BCM_LAUNCH_CHECK();

@@ -34,7 +34,9 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "scan_common.cuh"
 
@@ -699,23 +701,24 @@ size_t seg_bwd_smem(int N) {
     return (size_t)(head + kSegBwdWarps * seg_bwd_warp_floats<kSegR>(N)) * sizeof(float);
 }
 
-// Opt a kernel into the device's shared-memory maximum (once per device).
-template <typename K>
-bcm_status seg_optin(K kernel, size_t smem, const char* what) {
+// Opt a kernel into the device's shared-memory maximum (once per kernel and
+// device).  Keyed by the kernel's address: the instantiations share one
+// function type, so a per-type cache would skip all but the first.
+bcm_status seg_optin(const void* kernel, size_t smem, const char* what) {
     static std::mutex mu;
-    static int done[64] = {};
+    static std::map<std::pair<const void*, int>, int> done;
     int dev = 0;
     BCM_CUDA_TRY(cudaGetDevice(&dev));
-    BCM_REQUIRE(dev >= 0 && dev < 64, "%s: device %d out of range", what, dev);
     std::lock_guard<std::mutex> lock(mu);
-    if (done[dev] == 0) {
-        int mx = 0;
-        BCM_CUDA_TRY(cudaDeviceGetAttribute(&mx, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-        BCM_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, mx));
-        done[dev] = mx;
+    int& mx = done[{kernel, dev}];
+    if (mx == 0) {
+        int lim = 0;
+        BCM_CUDA_TRY(cudaDeviceGetAttribute(&lim, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        BCM_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+        mx = lim;
     }
-    if (smem > (size_t)done[dev]) {
-        set_error("%s: %zu bytes of shared memory exceed the device limit %d", what, smem, done[dev]);
+    if (smem > (size_t)mx) {
+        set_error("%s: %zu bytes of shared memory exceed the device limit %d", what, smem, mx);
         return BCM_ERR_UNSUPPORTED;
     }
     return BCM_OK;
@@ -736,7 +739,7 @@ bcm_status seg_fwd_t(const ScanArgs& a, const float* tab, float* carries, cudaSt
     const size_t smem = seg_fwd_smem(a.dstate);
     auto kern = seg_fwd_kernel<T, kSegR, CARRY_ONLY>;
     if (smem > 48 * 1024) {
-        const bcm_status s = seg_optin(kern, smem, "flat_ch fwd");
+        const bcm_status s = seg_optin(reinterpret_cast<const void*>(kern), smem, "flat_ch fwd");
         if (s != BCM_OK) return s;
     }
     kern<<<a.dim * g.ctas_per_d, 32 * kSegFwdWarps, smem, st>>>(a, tab, g, carries);
@@ -750,7 +753,7 @@ bcm_status seg_bwd_t(const ScanArgs& a, const float* tab, const float* carries, 
     const size_t smem = seg_bwd_smem(a.dstate);
     auto kern = seg_bwd_kernel<T, kSegR>;
     if (smem > 48 * 1024) {
-        const bcm_status s = seg_optin(kern, smem, "flat_ch bwd");
+        const bcm_status s = seg_optin(reinterpret_cast<const void*>(kern), smem, "flat_ch bwd");
         if (s != BCM_OK) return s;
     }
     kern<<<a.dim * g.ctas_per_d, 32 * kSegBwdWarps, smem, st>>>(a, tab, g, carries);

@@ -1,9 +1,10 @@
 """GPU parity of the event decode step (``event_decode_step`` through
-``interface.EventDecoder``): decoding a sequence token by token equals, bit
-for bit in fp32, the forward path on the same inputs (fused extraction ->
-staged depthwise scan -> restore), and the decode oracle within the fp32
-tolerance; with the conv state it equals conv-at-events -> scan -> restore;
-16-bit inputs within the 16-bit tolerance."""
+``interface.EventDecoder``): decoding a sequence token by token equals the
+forward path on the same inputs (fused extraction -> depthwise scan ->
+restore) and the decode oracle within the fp32 tolerance (the forward
+composes lane aggregates with the scan operator, so its rounding differs from
+one event at a time); with the conv state it equals conv-at-events -> scan ->
+restore; 16-bit inputs within the 16-bit tolerance."""
 import numpy as np
 import pytest
 import torch
@@ -68,7 +69,7 @@ def test_decode_equals_forward(B, d_model, expand, N, L, rho):
     got = _decode(xs, spikes, p)
     ref = _forward(xs, spikes, p)
     assert got.shape == ref.shape
-    assert torch.equal(got, ref)
+    assert_close(got, ref.cpu().numpy(), TOL_F32, "decode vs forward")
     oracle = dc.decode_sequence(xs.numpy(), spikes.numpy(), 0.5, **{k: v.numpy() for k, v in p.items()})
     assert_close(got, oracle, TOL_F32, "decode vs oracle")
 
