@@ -566,16 +566,18 @@ bcm_status launch_bwd(const ScanArgs& a, bool dw, bool has_z, cudaStream_t st) {
 // [W_B/W_C mixed by pw] [their gradients].
 struct BwdLayout {
     size_t ckpt_off, ckpt_bytes, part_off, part_bytes, weff_off, weff_bytes, dweff_off, total;
-    size_t tab_off, carry_off;
+    size_t tab_off, carry_off, order_off;
     int NP, part_stride, part_rows;
-    bool seg;
+    bool seg, staged;
 };
 
 BwdLayout bwd_layout(const bcm_flat_ch_args* p) {
     BwdLayout L{};
     ScanArgs a;
     scan_fill_args(p, a);
-    L.seg = p->n_events > 0 && seg_supported(a);
+    L.seg = p->n_events > 0 && seg_selected(a);
+    L.staged = !L.seg && p->n_events > 0 && p->bc_mode == BCM_BC_DEPTHWISE &&
+               dw_fast_supported((int)p->dstate) && v3_supported(a, true);
     int G, LPC;
     pick_layout((int)p->dstate, G, LPC);
     L.NP = G * LPC;
@@ -599,7 +601,8 @@ BwdLayout bwd_layout(const bcm_flat_ch_args* p) {
     L.weff_off = L.part_off + L.part_bytes;
     L.weff_bytes = p->pw_B ? align_up((size_t)2 * p->dim * p->dstate * sizeof(float), 256) : 0;
     L.dweff_off = L.weff_off + L.weff_bytes;
-    L.total = L.dweff_off + L.weff_bytes;
+    L.order_off = L.dweff_off + L.weff_bytes;
+    L.total = L.order_off + (L.staged ? row_order_bytes(a) : 0);
     return L;
 }
 
@@ -652,6 +655,12 @@ extern "C" bcm_status bcm_flat_ch_bwd(const bcm_flat_ch_args* p, cudaStream_t st
                             reinterpret_cast<float*>(ws + L.carry_off), stream);
         if (st != BCM_OK) return st;
     } else if (p->n_events > 0 && dw && dw_fast_supported(a.dstate)) {
+        if (L.staged) {
+            int* order = reinterpret_cast<int*>(ws + L.order_off);
+            st = row_order_launch(a, order, stream);
+            if (st != BCM_OK) return st;
+            a.row_order = order;
+        }
         st = dw_fast_launch(a, p->dtype, true, stream);
         if (st != BCM_OK) return st;
     } else if (p->n_events > 0) {

@@ -36,7 +36,15 @@ struct ScanArgs {
                       // backward reads them instead of recomputing (nullable)
     float* ws_part;   // backward: per-channel parameter-gradient partials
     int part_stride;  // floats per channel in ws_part
+    const int* row_order;  // staged kernels (nullable): batch rows of each feature d in
+                           // descending event count, [dim][n_channels/dim], so the rows a
+                           // warp walks in lockstep have similar lengths
 };
+
+// Batch row of slot b of feature d in the staged kernels' walk.
+__device__ __forceinline__ int scan_row(const ScanArgs& a, int d, int b) {
+    return a.row_order ? a.row_order[d * (a.n_channels / a.dim) + b] : b;
+}
 
 // Decay factor exp2(clamp(delta*A2, -126, 126)) with the accurate exp2f
 // (as the reference): with long-memory states (a close to 1) a biased
@@ -146,6 +154,14 @@ size_t v3_ckpt_bytes(const ScanArgs& a);
 // the backward needs the same table, the carries (from the forward, or it
 // writes them into carry_ws itself) and seg_part_rows partial rows.
 bool seg_supported(const ScanArgs& a);
+// Whether the dispatch runs the event-parallel kernels for these arguments
+// (BCM_SCAN_SEG: 0 never, 1 where the staged kernels do not apply (default),
+// 2 wherever supported).
+bool seg_selected(const ScanArgs& a);
+// Staged kernels: the row order (scan_row) of every feature, written into
+// `order` ([dim][B] ints, row_order_bytes) by one small kernel.
+size_t row_order_bytes(const ScanArgs& a);
+bcm_status row_order_launch(const ScanArgs& a, int* order, cudaStream_t st);
 size_t seg_table_bytes(const ScanArgs& a);
 size_t seg_carry_bytes(const ScanArgs& a);
 int seg_part_rows(const ScanArgs& a);

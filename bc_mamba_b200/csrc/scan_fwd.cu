@@ -286,7 +286,8 @@ void scan_fill_args(const bcm_flat_ch_args* p, ScanArgs& a) {
     a.du = p->du; a.dB_ev = nullptr; a.dC_ev = nullptr; a.dz = p->dz;
     a.ws_ckpt = nullptr; a.ws_part = nullptr; a.part_stride = 0;
     a.ckpt = nullptr;
-    if (p->ckpt != nullptr && (seg_supported(a) || v3_ckpt_bytes(a) > 0)) a.ckpt = p->ckpt;   // else ignored
+    a.row_order = nullptr;
+    if (p->ckpt != nullptr && (seg_selected(a) || v3_ckpt_bytes(a) > 0)) a.ckpt = p->ckpt;   // else ignored
 }
 
 bcm_status scan_launch_pw_mix(const bcm_flat_ch_args* p, float* WB_eff, float* WC_eff,
@@ -306,7 +307,8 @@ bcm_status scan_launch_pw_mix(const bcm_flat_ch_args* p, float* WB_eff, float* W
 
 using namespace bcm;
 
-// Forward workspace: [W_B/W_C mixed by pw (pw only)] [decay tables (event-parallel kernels)]
+// Forward workspace: [W_B/W_C mixed by pw (pw only)] then [decay tables
+// (event-parallel kernels)] or [row order (staged kernels)]
 static size_t fwd_pw_bytes(const bcm_flat_ch_args* p) {
     return p->pw_B == nullptr ? 0 : align_up((size_t)(2 * p->dim * p->dstate * sizeof(float)), 256);
 }
@@ -314,13 +316,23 @@ static size_t fwd_pw_bytes(const bcm_flat_ch_args* p) {
 static bool fwd_seg(const bcm_flat_ch_args* p, ScanArgs& a) {
     if (p->n_events <= 0 || p->n_channels <= 0 || p->dim <= 0 || p->dstate <= 0) return false;
     scan_fill_args(p, a);
-    return seg_supported(a);
+    return seg_selected(a);
+}
+
+static bool fwd_staged(const bcm_flat_ch_args* p, const ScanArgs& a) {
+    return p->n_events > 0 && p->bc_mode == BCM_BC_DEPTHWISE && dw_fast_supported(a.dstate) &&
+           v3_supported(a, false);
 }
 
 extern "C" size_t bcm_flat_ch_fwd_workspace_bytes(const bcm_flat_ch_args* p) {
     if (!p) return 0;
     ScanArgs a;
-    return fwd_pw_bytes(p) + (fwd_seg(p, a) ? seg_table_bytes(a) : 0);
+    if (fwd_seg(p, a)) return fwd_pw_bytes(p) + seg_table_bytes(a);
+    if (p->n_events > 0 && p->n_channels > 0 && p->dim > 0 && p->dstate > 0) {
+        scan_fill_args(p, a);
+        if (fwd_staged(p, a)) return fwd_pw_bytes(p) + row_order_bytes(a);
+    }
+    return fwd_pw_bytes(p);
 }
 
 extern "C" size_t bcm_flat_ch_ckpt_bytes(const bcm_flat_ch_args* p) {
@@ -351,14 +363,21 @@ extern "C" bcm_status bcm_flat_ch_fwd(const bcm_flat_ch_args* p, cudaStream_t st
     }
     const bool dw = p->bc_mode == BCM_BC_DEPTHWISE;
     const bool has_z = p->z != nullptr;
-    if (p->n_events > 0 && seg_supported(a)) {
+    if (p->n_events > 0 && seg_selected(a)) {
         // event-parallel kernels: write every slot of x themselves
         float* tab = reinterpret_cast<float*>(static_cast<char*>(p->workspace) + fwd_pw_bytes(p));
         return seg_fwd_launch(a, p->dtype, tab, a.ckpt, stream);
     }
     // x is written in full: the staged forward writes every slot itself,
     // every other path writes the chunks that exist onto zeros
-    const bool staged = p->n_events > 0 && dw && dw_fast_supported(a.dstate) && v3_supported(a, false);
+    const bool staged = fwd_staged(p, a);
+    if (staged) {
+        // rows of similar event counts share a warp
+        int* order = reinterpret_cast<int*>(static_cast<char*>(p->workspace) + fwd_pw_bytes(p));
+        st = row_order_launch(a, order, stream);
+        if (st != BCM_OK) return st;
+        a.row_order = order;
+    }
     if (!staged)
         BCM_CUDA_TRY(cudaMemsetAsync(p->x, 0, (size_t)a.n_channels * a.n_chunks * 2 * a.dstate * sizeof(float),
                                      stream));

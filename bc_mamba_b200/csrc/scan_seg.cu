@@ -26,11 +26,13 @@
 //    recurrence before it; the backward walks tiles last to first with a
 //    reverse scan for the adjoint gamma_i = a_{i+1}*gamma_{i+1} + g_i*u_i.
 //
-// Chunk states x[ch, c] = (prod a, h) after each 2048-event chunk are written
-// with prod a = exp2(A*log2(e)*sum delta), sum delta = dt_idle*(sum k - n) +
-// dt_active*n from an integer segmented scan of the gaps; this equals the
-// reference's running product of clamped decays except where an event's
-// exponent exceeds +126 (a state growing by 2^126 in one step).
+// Chunk states x[ch, c] = (prod a, h) after each 2048-event chunk, prod a
+// over all events of the channel so far (the reference carries it across
+// chunks), are written with prod a = exp2(A*log2(e)*sum delta), sum delta =
+// dt_idle*(sum k - n) + dt_active*n from an integer segmented scan of the
+// gaps; this equals the reference's running product of clamped decays except
+// where an event's exponent exceeds +126 (a state growing by 2^126 in one
+// step).
 #include <stdlib.h>
 
 #include <algorithm>
@@ -285,7 +287,7 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
                     const bool hit = (unsigned)(kv - 1) < (unsigned)kSegKMax;
                     ix[r] = (j == 0) ? 0 : (hit ? kv : kSegPadRow);
                     if (j != 0 && !hit) exm |= 1u << r;
-                    if ((j & (kChunkX - 1)) == 0) hdm |= 1u << r;
+                    if (j == 0) hdm |= 1u << r;
                     if (((j + 1) & (kChunkX - 1)) == 0 || j == n - 1) cem |= 1u << r;
                 } else {
                     w[r] = 0.f;
@@ -294,7 +296,9 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
                 }
             }
         }
-        // ---- chunk bookkeeping for x: segmented gap sums (heads at chunk starts)
+        // ---- chunk bookkeeping for x: gap sums since the channel's first
+        // event (prod a of x runs from the channel start, as the reference's
+        // chunk prefix does), segmented at channel starts
         if (!CARRY_ONLY) {
             int v = 0, f = 0;
 #pragma unroll
@@ -328,7 +332,7 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
                         const int p = pl + r;
                         while (p >= vs[c + 1]) ++c;
                         const int j = p - vs[c];
-                        const int cnt = (j & (kChunkX - 1)) + 1;
+                        const int cnt = j + 1;
                         const int chunk = j / kChunkX;
                         sxr[segpad(q0 + r)] = chunk < nchk ? W->ch[c] * nchk + chunk : -1;
                         ssd[segpad(q0 + r)] = fmaf(dti, (float)(K - cnt), dta * (float)cnt);
@@ -766,12 +770,16 @@ bcm_status seg_bwd_t(const ScanArgs& a, const float* tab, const float* carries, 
 // The event-parallel kernels serve the depthwise mode without the silu gate
 // for dstate <= 64 when every feature has the same number of batch rows.
 bool seg_supported(const ScanArgs& a) {
-    static const int mode = [] {
-        const char* e = getenv("BCM_SCAN_SEG");
-        return e ? atoi(e) : 1;
-    }();
-    return mode != 0 && a.bc_mode == BCM_BC_DEPTHWISE && a.z == nullptr && a.dstate <= 64 && a.dim > 0 &&
+    return a.bc_mode == BCM_BC_DEPTHWISE && a.z == nullptr && a.dstate <= 64 && a.dim > 0 &&
            a.n_channels % a.dim == 0 && a.n_events > 0;
+}
+
+bool seg_selected(const ScanArgs& a) {
+    const char* e = getenv("BCM_SCAN_SEG");
+    const int mode = e ? atoi(e) : 1;
+    if (mode == 0 || !seg_supported(a)) return false;
+    if (mode >= 2) return true;
+    return !(v3_supported(a, false) && v3_supported(a, true));
 }
 
 size_t seg_table_bytes(const ScanArgs& a) {

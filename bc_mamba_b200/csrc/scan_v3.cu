@@ -26,6 +26,8 @@
 //    reductions once per tile.
 #include <stdlib.h>
 
+#include <algorithm>
+
 #include <mutex>
 #include <type_traits>
 
@@ -219,12 +221,12 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
     const int b0 = (blockIdx.x % bgroups) * CPW;
     const int N = a.dstate;
     if (lane < CPW) {
-        const int c = (b0 + lane) * a.dim + d;
+        const int c = scan_row(a, d, b0 + lane) * a.dim + d;
         s_beg[lane] = a.cu[c];
         s_n[lane] = a.cu[c + 1] - a.cu[c];
     }
     build_table3<NP>(tab, a, d, lane);
-    const int ch = (b0 + grp) * a.dim + d;
+    const int ch = scan_row(a, d, b0 + grp) * a.dim + d;
     const int beg = s_beg[grp], n = s_n[grp];
     const int nch = (n + kChunkX - 1) / kChunkX;
     const int nch_max = warp_max(nch);
@@ -608,14 +610,14 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
     const int N = a.dstate;
 
     if (lane < CPW) {
-        const int c = (b0 + lane) * a.dim + d;
+        const int c = scan_row(a, d, b0 + lane) * a.dim + d;
         s_beg[lane] = a.cu[c];
         s_n[lane] = a.cu[c + 1] - a.cu[c];
     }
     build_table_block<NP, G>(tab, a, d);
     __syncthreads();
 
-    const int ch = (b0 + grp) * a.dim + d;
+    const int ch = scan_row(a, d, b0 + grp) * a.dim + d;
     const int n = s_n[grp];
     const int n_max = warp_max(n);
     const int s0 = q * G;
@@ -891,6 +893,44 @@ size_t v3_ckpt_bytes(const ScanArgs& a) {
         return 0;
     const size_t slots = (size_t)(a.n_events >> 3) + (size_t)a.n_channels + 1;
     return slots * (size_t)padded_states(a.dstate) * sizeof(float);
+}
+
+// Batch rows of each feature by descending event count (ties by row): one
+// CTA per feature ranks its rows by counting.  Rows past 4096 per feature
+// keep their order (order[b] = b).
+__global__ void row_order_kernel(const int32_t* __restrict__ cu, int dim, int Bn, int* __restrict__ order) {
+    extern __shared__ int s_n[];
+    const int d = blockIdx.x;
+    for (int b = threadIdx.x; b < Bn; b += blockDim.x) {
+        const int c = b * dim + d;
+        s_n[b] = cu[c + 1] - cu[c];
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < Bn; b += blockDim.x) {
+        const int nb = s_n[b];
+        int rank = 0;
+        for (int b2 = 0; b2 < Bn; ++b2) {
+            const int n2 = s_n[b2];
+            rank += (n2 > nb || (n2 == nb && b2 < b)) ? 1 : 0;
+        }
+        order[d * Bn + rank] = b;
+    }
+}
+
+size_t row_order_bytes(const ScanArgs& a) {
+    return align_up((size_t)a.n_channels * sizeof(int), 256);
+}
+
+bcm_status row_order_launch(const ScanArgs& a, int* order, cudaStream_t st) {
+    const int Bn = a.n_channels / a.dim;
+    if (Bn > 4096) {
+        set_error("flat_ch: row order needs at most 4096 rows per feature, got %d", Bn);
+        return BCM_ERR_UNSUPPORTED;
+    }
+    const int threads = std::min(256, std::max(32, (Bn + 31) / 32 * 32));
+    row_order_kernel<<<a.dim, threads, Bn * sizeof(int), st>>>(a.cu, a.dim, Bn, order);
+    BCM_LAUNCH_CHECK();
+    return BCM_OK;
 }
 
 bcm_status v3_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t st) {

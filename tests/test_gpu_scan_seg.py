@@ -4,7 +4,8 @@ the group size, which at these sizes would otherwise be 1), ragged, empty and
 one-event channels, channels spanning many 256-event tiles and several
 2048-event chunks, gaps past the 256-row decay table, every dstate up to 64,
 16-bit inputs, and the backward with and without the forward's tile carries
-(bit-identical to each other).  Tolerance as test_gpu_scan.py."""
+(bit-identical to each other).  BCM_SCAN_SEG=2 selects these kernels
+wherever they apply.  Tolerance as test_gpu_scan.py."""
 import os
 
 import numpy as np
@@ -16,6 +17,19 @@ from test_gpu_scan import _events, _params, _run_and_check
 from bc_mamba_b200.workloads import CONFIGS
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def seg_everywhere():
+    """Run the event-parallel kernels wherever they apply (by default they
+    serve the shapes the staged kernels do not)."""
+    old = os.environ.get("BCM_SCAN_SEG")
+    os.environ["BCM_SCAN_SEG"] = "2"
+    yield
+    if old is None:
+        os.environ.pop("BCM_SCAN_SEG", None)
+    else:
+        os.environ["BCM_SCAN_SEG"] = old
 
 
 @pytest.fixture
@@ -79,6 +93,19 @@ def test_seg_multi_chunk_channels(cpw):
     dti, dta, A, WB, WC, Dv = _params(c.D, c.N, 23)
     res, _ = _run_and_check(u, k, cu, mx, dti, dta, A, WB, WC, D=Dv)
     assert res[1].shape[1] == (mx + 2047) // 2048
+
+
+@pytest.mark.parametrize("cpw", [1, 2], indirect=True)
+def test_seg_multi_chunk_long_memory(cpw):
+    """Small dt: the chunk products of x stay far from 0, so each must be the
+    product since the channel's first event (carried across chunks)."""
+    c = CONFIGS["c0"].with_(B=2, D=4, N=16, L=6000, rho=0.9, seed=24)
+    inp, ch, t, k, cu, mx, u = _events(c)
+    assert mx > 4096
+    dti, dta, A, WB, WC, Dv = _params(c.D, c.N, 24)
+    res, _ = _run_and_check(u, k, cu, mx, 0.01 * dti, 0.01 * dta, A, 0.3 * WB, 0.3 * WC, D=Dv,
+                            fp32_decay=True)
+    assert float(res[1][:, 1:, 0::2].max()) > 1e-3
 
 
 @pytest.mark.parametrize("N", [1, 3, 8, 16, 33, 64])
