@@ -57,6 +57,9 @@ __device__ __forceinline__ float decay_fast(float delta, float A2) {
 // depthwise path tabulates decays per integer gap, so each rounded value is
 // reused by every event with that gap; rounding it correctly keeps the
 // coherent error of long-memory states (a close to 1) at the fp32 limit.
+// Gaps past a table take decay_fast, the reference's exp2f: they are rare and
+// their values hardly repeat, and a double-precision exp2 per event and state
+// would make a sparse channel cost hundreds of times a dense one.
 __device__ __forceinline__ float decay_exact(float delta, float A2) {
     const float x = fmaxf(fminf(delta * A2, 126.0f), -126.0f);
     return (float)exp2((double)x);

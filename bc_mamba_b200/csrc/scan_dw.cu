@@ -89,7 +89,7 @@ __device__ __forceinline__ void lookup(const float* tab, bool tab_ok, int k, flo
         table_row<G>(tab + (k - 1) * NP + q * G, dec);
     } else {
 #pragma unroll
-        for (int g = 0; g < G; ++g) dec[g] = decay_exact(delta, A2[g]);
+        for (int g = 0; g < G; ++g) dec[g] = decay_fast(delta, A2[g]);
     }
 }
 

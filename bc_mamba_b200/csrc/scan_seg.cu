@@ -355,7 +355,7 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
                 const float A2 = s_A2[s];
 #pragma unroll
                 for (int r = 0; r < R; ++r)
-                    if (exm >> r & 1) av[r] = decay_exact(event_delta(dti, dta, kk[r]), A2);
+                    if (exm >> r & 1) av[r] = decay_fast(event_delta(dti, dta, kk[r]), A2);
             }
             float A = av[0], Bv = w[0];
 #pragma unroll
@@ -560,7 +560,7 @@ seg_bwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, const floa
                 const float A2 = s_A2[s];
 #pragma unroll
                 for (int r = 0; r < R; ++r)
-                    if (exm >> r & 1) av[r] = decay_exact(event_delta(dti, dta, sk[segpad(q0 + r)]), A2);
+                    if (exm >> r & 1) av[r] = decay_fast(event_delta(dti, dta, sk[segpad(q0 + r)]), A2);
             }
             // forward: incoming state of each lane
             float A = av[0], Bv = w[0];

@@ -263,7 +263,7 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
                 for (int g = 0; g < G; ++g) {
                     const int s = q * G + g;
                     const float Ar = s < N ? a.A[d * a.A_sd + s * a.A_sn] : 0.f;
-                    dec[g] = decay_exact(dl, (float)((double)Ar * 1.4426950408889634));
+                    dec[g] = decay_fast(dl, (float)((double)Ar * 1.4426950408889634));
                 }
             }
         }
@@ -728,7 +728,7 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
                 if (real && (!hit || dl > dlim)) {
 #pragma unroll
                     for (int g = 0; g < G; ++g) {
-                        dec[g] = decay_exact(dl, A2[g]);
+                        dec[g] = decay_fast(dl, A2[g]);
                         if (dl > dclamp) {
                             const float x = dl * A2[g];
                             corr[g] += fmaxf(fminf(x, 126.0f), -126.0f) - x;
