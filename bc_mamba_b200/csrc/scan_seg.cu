@@ -38,6 +38,7 @@
 #include <algorithm>
 #include <map>
 #include <mutex>
+#include <type_traits>
 #include <utility>
 
 #include "scan_common.cuh"
@@ -53,7 +54,13 @@ constexpr int kSegMaxCPW = 16;       // batch rows per warp group
 constexpr int kSegFwdWarps = 8;
 constexpr int kSegBwdWarps = 4;
 
+// States are processed in pairs (s, s+1) with the packed fp32x2 FMA of
+// sm_100 (per component the same rounding as fmaf); an odd dstate gets one
+// padding state with A = 0 and W = 0, which contributes nothing.
+__host__ __device__ __forceinline__ int seg_pairs(int N) { return (N + 1) >> 1; }
+
 __device__ __forceinline__ int segpad(int q) { return q + (q >> 5); }
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
 
 // Largest c in [0, nc) with vs[c] <= p (vs[0] = 0 <= p).  Skips empty channels.
 __device__ __forceinline__ int seg_find(const int* vs, int nc, int p) {
@@ -65,22 +72,27 @@ __device__ __forceinline__ int seg_find(const int* vs, int nc, int p) {
     return lo;
 }
 
-// Per-feature decay tables tab[d][s][row] (rows as kSegTR).
-__global__ void seg_table_kernel(ScanArgs a, float* __restrict__ tab) {
-    const int64_t total = (int64_t)a.dim * a.dstate * kSegTR;
+__device__ __forceinline__ float seg_A2(const ScanArgs& a, int d, int s) {
+    return s < a.dstate ? (float)((double)a.A[d * a.A_sd + s * a.A_sn] * 1.4426950408889634) : 0.f;
+}
+
+// Per-feature decay tables of state pairs, tab[d][pair][row] (rows as kSegTR).
+__global__ void seg_table_kernel(ScanArgs a, float2* __restrict__ tab) {
+    const int NP2 = seg_pairs(a.dstate);
+    const int64_t total = (int64_t)a.dim * NP2 * kSegTR;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int row = (int)(i % kSegTR);
-        const int64_t ds = i / kSegTR;
-        const int s = (int)(ds % a.dstate), d = (int)(ds / a.dstate);
-        float v;
+        const int64_t dp = i / kSegTR;
+        const int sp = (int)(dp % NP2), d = (int)(dp / NP2);
+        float2 v;
         if (row == 0) {
-            v = 0.f;
+            v = make_float2(0.f, 0.f);
         } else if (row == kSegPadRow) {
-            v = 1.f;
+            v = make_float2(1.f, 1.f);
         } else {
-            const float A2 = (float)((double)a.A[d * a.A_sd + s * a.A_sn] * 1.4426950408889634);
-            v = decay_exact(event_delta(a.dt_idle[d], a.dt_active[d], row), A2);
+            const float dl = event_delta(a.dt_idle[d], a.dt_active[d], row);
+            v = make_float2(decay_exact(dl, seg_A2(a, d, 2 * sp)), decay_exact(dl, seg_A2(a, d, 2 * sp + 1)));
         }
         tab[i] = v;
     }
@@ -117,30 +129,37 @@ __device__ __forceinline__ void seg_setup(const ScanArgs& a, int d, int b0, int 
     __syncwarp();
 }
 
+__device__ __forceinline__ float2 shfl_up2(float2 v, int off) {
+    return make_float2(__shfl_up_sync(kFull, v.x, off), __shfl_up_sync(kFull, v.y, off));
+}
+__device__ __forceinline__ float2 shfl_down2(float2 v, int off) {
+    return make_float2(__shfl_down_sync(kFull, v.x, off), __shfl_down_sync(kFull, v.y, off));
+}
+
 // Kogge-Stone inclusive scan of the (a, b) operator over the warp's lanes
-// (lane order = event order).
-__device__ __forceinline__ void seg_scan_up(float& A, float& B, int lane) {
+// (lane order = event order), two states at once.
+__device__ __forceinline__ void seg_scan_up(float2& A, float2& B, int lane) {
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
-        const float Ao = __shfl_up_sync(kFull, A, off);
-        const float Bo = __shfl_up_sync(kFull, B, off);
+        const float2 Ao = shfl_up2(A, off);
+        const float2 Bo = shfl_up2(B, off);
         if (lane >= off) {
-            B = fmaf(A, Bo, B);
-            A *= Ao;
+            B = __ffma2_rn(A, Bo, B);
+            A = __fmul2_rn(A, Ao);
         }
     }
 }
 
 // Suffix (right-to-left) scan: lane L composes its map gamma_first(L) =
 // M_L*gamma_first(L+1) + G_L with the lanes to its right.
-__device__ __forceinline__ void seg_scan_down(float& M, float& G, int lane) {
+__device__ __forceinline__ void seg_scan_down(float2& M, float2& G, int lane) {
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
-        const float Mo = __shfl_down_sync(kFull, M, off);
-        const float Go = __shfl_down_sync(kFull, G, off);
+        const float2 Mo = shfl_down2(M, off);
+        const float2 Go = shfl_down2(G, off);
         if (lane + off < 32) {
-            G = fmaf(M, Go, G);
-            M *= Mo;
+            G = __ffma2_rn(M, Go, G);
+            M = __fmul2_rn(M, Mo);
         }
     }
 }
@@ -151,57 +170,76 @@ struct SegTile {
     static constexpr int PADT = TILE + TILE / 32;
 };
 
-// Floats of one warp's shared-memory region (rounded to 16 bytes).
-template <int R>
-constexpr int seg_fwd_warp_floats(int N) {
-    return (5 * SegTile<R>::PADT + 2 * N + (int)(sizeof(SegWarp) / 4) + 3) / 4 * 4;
+// Shared memory (floats): a CTA head with the table and per-pair constants,
+// then one region per warp (all rounded to 16 bytes).
+__host__ __device__ constexpr int seg_head_floats(int N) {
+    return (2 * seg_pairs(N) * kSegTR + 6 * seg_pairs(N) + 3) / 4 * 4;
 }
 template <int R>
-constexpr int seg_bwd_warp_floats(int N) {
-    return (4 * SegTile<R>::PADT + 3 * N + (int)(sizeof(SegWarp) / 4) + 64 * N + 3) / 4 * 4;
+__host__ __device__ constexpr int seg_fwd_warp_floats(int N) {
+    return (5 * SegTile<R>::PADT + 4 * seg_pairs(N) + (int)(sizeof(SegWarp) / 4) + 3) / 4 * 4;
+}
+template <int R>
+__host__ __device__ constexpr int seg_bwd_warp_floats(int N) {
+    return (4 * SegTile<R>::PADT + 6 * seg_pairs(N) + (int)(sizeof(SegWarp) / 4) + 128 * seg_pairs(N) + 3) / 4 * 4;
+}
+
+// Copy the feature's table and per-pair constants into the CTA head:
+// c0 = (W_B*W_C) pairs, c1 = W_B pairs (forward) or W_B*W_C*A pairs
+// (backward), c2 = A*log2(e) pairs.
+__device__ __forceinline__ void seg_load_head(const ScanArgs& a, int d, const float2* gtab, float2* tab,
+                                              float2* c0, float2* c1, float2* c2, bool bwd) {
+    const int N = a.dstate, NP2 = seg_pairs(N);
+    const float2* src = gtab + (int64_t)d * NP2 * kSegTR;
+    for (int i = threadIdx.x; i < NP2 * kSegTR; i += blockDim.x) tab[i] = src[i];
+    for (int sp = threadIdx.x; sp < NP2; sp += blockDim.x) {
+        float cw[2], x1[2], A2[2];
+        for (int h = 0; h < 2; ++h) {
+            const int s = 2 * sp + h;
+            const bool ok = s < N;
+            const float wb = ok ? a.B[d * N + s] : 0.f;
+            cw[h] = ok ? wb * a.C[d * N + s] : 0.f;
+            x1[h] = bwd ? (ok ? cw[h] * a.A[d * a.A_sd + s * a.A_sn] : 0.f) : wb;
+            A2[h] = seg_A2(a, d, s);
+        }
+        c0[sp] = make_float2(cw[0], cw[1]);
+        c1[sp] = make_float2(x1[0], x1[1]);
+        c2[sp] = make_float2(A2[0], A2[1]);
+    }
 }
 
 // =============================================================== forward ====
 // CARRY_ONLY: only the state entering every tile (for a backward that was not
 // given the forward's carries); no outputs.
 template <typename T, int R, bool CARRY_ONLY>
-__global__ void __launch_bounds__(32 * kSegFwdWarps)
-seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __restrict__ carries) {
+__global__ void __launch_bounds__(32 * kSegFwdWarps, 2)
+seg_fwd_kernel(ScanArgs a, const float2* __restrict__ gtab, SegGeom g, float* __restrict__ carries) {
     constexpr int TILE = SegTile<R>::TILE;
     constexpr int PADT = SegTile<R>::PADT;
     extern __shared__ __align__(16) float sm[];
-    const int N = a.dstate;
+    const int N = a.dstate, NP2 = seg_pairs(N);
     const int d = blockIdx.x / g.ctas_per_d;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* tab = sm;
-    float* s_cw = tab + N * kSegTR;
-    float* s_wb = s_cw + N;
-    float* s_A2 = s_wb + N;
-    const int head = (N * kSegTR + 3 * N + 3) / 4 * 4;
+    const int head = seg_head_floats(N);
     {
         unsigned dyn;
         asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
         if ((size_t)dyn < (size_t)(head + g.warps * seg_fwd_warp_floats<R>(N)) * sizeof(float)) return;
     }
+    float2* tab = reinterpret_cast<float2*>(sm);
+    float2* s_cw = tab + NP2 * kSegTR;
+    float2* s_wb = s_cw + NP2;
+    float2* s_A2 = s_wb + NP2;
     float* wr = sm + head + warp * seg_fwd_warp_floats<R>(N);
     float* su = wr;
     int* sk = reinterpret_cast<int*>(su + PADT);
     int* se = sk + PADT;
     int* sxr = se + PADT;
     float* ssd = reinterpret_cast<float*>(sxr + PADT);
-    float* carry = ssd + PADT;                        // [2][N]
-    SegWarp* W = reinterpret_cast<SegWarp*>(carry + 2 * N);
+    float2* carry = reinterpret_cast<float2*>(ssd + PADT);      // [2][NP2]
+    SegWarp* W = reinterpret_cast<SegWarp*>(carry + 2 * NP2);
 
-    {
-        const float* src = gtab + (int64_t)d * N * kSegTR;
-        for (int i = threadIdx.x; i < N * kSegTR; i += blockDim.x) tab[i] = src[i];
-        for (int s = threadIdx.x; s < N; s += blockDim.x) {
-            const float wb = a.B[d * N + s];
-            s_cw[s] = wb * a.C[d * N + s];
-            s_wb[s] = wb;
-            s_A2[s] = (float)((double)a.A[d * a.A_sd + s * a.A_sn] * 1.4426950408889634);
-        }
-    }
+    seg_load_head(a, d, gtab, tab, s_cw, s_wb, s_A2, false);
     __syncthreads();
     const int grp = (blockIdx.x % g.ctas_per_d) * g.warps + warp;
     if (grp >= g.groups_per_d) return;        // no barrier below
@@ -226,15 +264,15 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
             for (int i = lane; i < cnt; i += 32) xo[i] = 0.f;
         }
     }
-    for (int s = lane; s < N; s += 32) carry[s] = 0.f;
-    int kc = 0;    // gap sum of the chunk running into the next tile (warp-uniform)
+    for (int sp = lane; sp < NP2; sp += 32) carry[sp] = make_float2(0.f, 0.f);
+    int kc = 0;    // gap sum since the start of the channel running into the next tile
     const int n_tiles = (Ew + TILE - 1) / TILE;
     __syncwarp();
 
     for (int t = 0; t < n_tiles; ++t) {
         const int p0 = t * TILE;
-        float* cin = carry + (t & 1) * N;
-        float* cout = carry + ((t + 1) & 1) * N;
+        const float2* cin = carry + (t & 1) * NP2;
+        float2* cout = carry + ((t + 1) & 1) * NP2;
         // ---- stage the tile: coalesced along each channel's events
 #pragma unroll
         for (int m = 0; m < R; ++m) {
@@ -260,8 +298,8 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
             const int c0 = seg_find(vs, nc, p0);
             const int e0 = W->base[c0] + (p0 - vs[c0]);
             if (e0 >= 0 && e0 < a.n_events) {
-                const int64_t slot = (int64_t)e0 / TILE + W->ch[c0];
-                for (int s = lane; s < N; s += 32) carries[slot * N + s] = cin[s];
+                float2* dst = reinterpret_cast<float2*>(carries) + ((int64_t)e0 / TILE + W->ch[c0]) * NP2;
+                for (int sp = lane; sp < NP2; sp += 32) dst[sp] = cin[sp];
             }
         }
         __syncwarp();
@@ -269,7 +307,7 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
         // ---- this lane's events
         const int q0 = lane * R, pl = p0 + q0;
         float w[R];
-        int ix[R], kk[R];
+        int ix[R];
         unsigned exm = 0, cem = 0, hdm = 0;
         {
             int c = seg_find(vs, nc, min(pl, Ew - 1));
@@ -278,12 +316,10 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
                 const int p = pl + r;
                 const float uv = su[segpad(q0 + r)];
                 const int kv = sk[segpad(q0 + r)];
-                kk[r] = kv;
                 if (p < Ew) {
                     while (p >= vs[c + 1]) ++c;
                     const int j = p - vs[c], n = vs[c + 1] - vs[c];
-                    const float dl = event_delta(dti, dta, kv);
-                    w[r] = dl * uv * uv;
+                    w[r] = event_delta(dti, dta, kv) * uv * uv;
                     const bool hit = (unsigned)(kv - 1) < (unsigned)kSegKMax;
                     ix[r] = (j == 0) ? 0 : (hit ? kv : kSegPadRow);
                     if (j != 0 && !hit) exm |= 1u << r;
@@ -292,19 +328,21 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
                 } else {
                     w[r] = 0.f;
                     ix[r] = kSegPadRow;
-                    kk[r] = 0;
                 }
             }
         }
-        // ---- chunk bookkeeping for x: gap sums since the channel's first
-        // event (prod a of x runs from the channel start, as the reference's
-        // chunk prefix does), segmented at channel starts
+        const bool wexact = __any_sync(kFull, exm != 0);
+        const bool wchunk = !CARRY_ONLY && __any_sync(kFull, cem != 0);
+        // ---- chunk bookkeeping for x (tiles holding a chunk end): gap sums
+        // since each channel's first event (prod a of x runs from the channel
+        // start, as the reference's chunk prefix does), segmented at channel
+        // starts; kc carries the running sum into the next tile
         if (!CARRY_ONLY) {
             int v = 0, f = 0;
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 if (hdm >> r & 1) { v = 0; f = 1; }
-                v += kk[r];
+                v += sk[segpad(q0 + r)];
             }
             int vi = v, fi = f;
 #pragma unroll
@@ -316,83 +354,101 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
                     fi |= fo;
                 }
             }
-            int ve = __shfl_up_sync(kFull, vi, 1), fe = __shfl_up_sync(kFull, fi, 1);
-            if (lane == 0) { ve = 0; fe = 0; }
-            const int kbase = fe ? ve : kc + ve;
-            const int v31 = __shfl_sync(kFull, vi, 31), f31 = __shfl_sync(kFull, fi, 31);
-            kc = f31 ? v31 : kc + v31;
-            if (cem) {
-                int K = kbase;
+            if (wchunk && cem) {
+                int ve = __shfl_up_sync(kFull, vi, 1), fe = __shfl_up_sync(kFull, fi, 1);
+                if (lane == 0) { ve = 0; fe = 0; }
+                int K = fe ? ve : kc + ve;
                 int c = seg_find(vs, nc, min(pl, Ew - 1));
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
                     if (hdm >> r & 1) K = 0;
-                    K += kk[r];
+                    K += sk[segpad(q0 + r)];
                     if (cem >> r & 1) {
                         const int p = pl + r;
                         while (p >= vs[c + 1]) ++c;
                         const int j = p - vs[c];
-                        const int cnt = j + 1;
                         const int chunk = j / kChunkX;
                         sxr[segpad(q0 + r)] = chunk < nchk ? W->ch[c] * nchk + chunk : -1;
-                        ssd[segpad(q0 + r)] = fmaf(dti, (float)(K - cnt), dta * (float)cnt);
+                        ssd[segpad(q0 + r)] = fmaf(dti, (float)(K - (j + 1)), dta * (float)(j + 1));
                     }
                 }
+            } else if (wchunk) {
+                (void)__shfl_up_sync(kFull, vi, 1);
+                (void)__shfl_up_sync(kFull, fi, 1);
             }
+            const int v31 = __shfl_sync(kFull, vi, 31), f31 = __shfl_sync(kFull, fi, 31);
+            kc = f31 ? v31 : kc + v31;
         }
 
-        // ---- states
-        const bool wexact = __any_sync(kFull, exm != 0);
-        float acc[R];
+        // ---- state pairs
+        float2 acc[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r) acc[r] = 0.f;
-        for (int s = 0; s < N; ++s) {
-            const float* ts = tab + s * kSegTR;
-            float av[R];
+        for (int r = 0; r < R; ++r) acc[r] = make_float2(0.f, 0.f);
+        auto pair_pass = [&](auto chunk_c, int sp) {
+            constexpr bool CHUNK = decltype(chunk_c)::value;
+            const float2* ts = tab + sp * kSegTR;
+            float2 av[R];
 #pragma unroll
             for (int r = 0; r < R; ++r) av[r] = ts[ix[r]];
             if (wexact && exm) {
-                const float A2 = s_A2[s];
+                const float2 A2 = s_A2[sp];
 #pragma unroll
                 for (int r = 0; r < R; ++r)
-                    if (exm >> r & 1) av[r] = decay_fast(event_delta(dti, dta, kk[r]), A2);
+                    if (exm >> r & 1) {
+                        const float dl = event_delta(dti, dta, sk[segpad(q0 + r)]);
+                        av[r] = make_float2(decay_fast(dl, A2.x), decay_fast(dl, A2.y));
+                    }
             }
-            float A = av[0], Bv = w[0];
+            float2 A = av[0], Bv = f2(w[0]);
 #pragma unroll
             for (int r = 1; r < R; ++r) {
-                Bv = fmaf(av[r], Bv, w[r]);
-                A *= av[r];
+                Bv = __ffma2_rn(av[r], Bv, f2(w[r]));
+                A = __fmul2_rn(A, av[r]);
             }
             seg_scan_up(A, Bv, lane);
-            const float c_in = cin[s];
             // the carries-only pass computes the states exactly as here, so a
             // backward from either pass sees bit-identical carries
-            float Ae = __shfl_up_sync(kFull, A, 1), Be = __shfl_up_sync(kFull, Bv, 1);
-            if (lane == 0) { Ae = 1.f; Be = 0.f; }
-            float eta = fmaf(Ae, c_in, Be);
-            const float cw = s_cw[s];
+            float2 Ae = shfl_up2(A, 1), Be = shfl_up2(Bv, 1);
+            if (lane == 0) {
+                Ae = make_float2(1.f, 1.f);
+                Be = make_float2(0.f, 0.f);
+            }
+            float2 eta = __ffma2_rn(Ae, cin[sp], Be);
+            const float2 cw = s_cw[sp];
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                eta = fmaf(av[r], eta, w[r]);
-                acc[r] = fmaf(cw, eta, acc[r]);
-                if (!CARRY_ONLY && (cem >> r & 1)) {
+                eta = __ffma2_rn(av[r], eta, f2(w[r]));
+                acc[r] = __ffma2_rn(cw, eta, acc[r]);
+                if (CHUNK && (cem >> r & 1)) {
                     const int xr = sxr[segpad(q0 + r)];
                     if (xr >= 0) {
                         float* xo = a.x + (int64_t)xr * 2 * N;
-                        xo[2 * s] = exp2f(s_A2[s] * ssd[segpad(q0 + r)]);
-                        xo[2 * s + 1] = s_wb[s] * eta;
+                        const float sd = ssd[segpad(q0 + r)];
+                        const float2 A2 = s_A2[sp], wb = s_wb[sp];
+                        xo[4 * sp] = exp2f(A2.x * sd);
+                        xo[4 * sp + 1] = wb.x * eta.x;
+                        if (2 * sp + 1 < N) {
+                            xo[4 * sp + 2] = exp2f(A2.y * sd);
+                            xo[4 * sp + 3] = wb.y * eta.y;
+                        }
                     }
                 }
             }
-            const float cnew = __shfl_sync(kFull, eta, 31);
-            if (lane == 0) cout[s] = cnew;
+            const float2 cnew = make_float2(__shfl_sync(kFull, eta.x, 31), __shfl_sync(kFull, eta.y, 31));
+            if (lane == 0) cout[sp] = cnew;
+        };
+        if (wchunk) {
+            for (int sp = 0; sp < NP2; ++sp) pair_pass(std::true_type{}, sp);
+        } else {
+#pragma unroll 2
+            for (int sp = 0; sp < NP2; ++sp) pair_pass(std::false_type{}, sp);
         }
         if (!CARRY_ONLY) {
             // ---- outputs y = D*u + u*acc, stored coalesced
 #pragma unroll
             for (int r = 0; r < R; ++r) {
                 const float uv = su[segpad(q0 + r)];
-                su[segpad(q0 + r)] = fmaf(Dv, uv, uv * acc[r]);
+                su[segpad(q0 + r)] = fmaf(Dv, uv, uv * (acc[r].x + acc[r].y));
             }
             __syncwarp();
             T* out = static_cast<T*>(a.out);
@@ -408,9 +464,9 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
 }
 
 // ============================================================== backward ====
-// Per tile (last to first) and state: forward scan for eta from the tile's
-// incoming state, reverse scan for gamma (the adjoint of eta divided by cw)
-// from the next tile's outgoing term, then
+// Per tile (last to first) and state pair: forward scan for eta from the
+// tile's incoming state, reverse scan for gamma (the adjoint of eta divided by
+// cw) from the next tile's outgoing term, then
 //   du_i  = D*g_i + g_i*sum_s cw_s*eta_i,s + 2*delta_i*u_i*sum_s cw_s*gamma_i,s
 //   dd_i  = u_i^2*sum_s cw_s*gamma_i,s + sum_s cw_s*A_s*gamma_i,s*a_i,s*eta_{i-1},s
 //   dA_s  = cw_s*sum_i gamma_i,s*a_i,s*eta_{i-1},s*delta_i
@@ -420,45 +476,35 @@ seg_fwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, float* __r
 // Parameter sums are per-warp partials, rows grp*dim + d of ws_part, reduced
 // over the groups of a feature in a fixed order afterwards.
 template <typename T, int R>
-__global__ void __launch_bounds__(32 * kSegBwdWarps)
-seg_bwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, const float* __restrict__ carries) {
+__global__ void __launch_bounds__(32 * kSegBwdWarps, 3)
+seg_bwd_kernel(ScanArgs a, const float2* __restrict__ gtab, SegGeom g, const float* __restrict__ carries) {
     constexpr int TILE = SegTile<R>::TILE;
     constexpr int PADT = SegTile<R>::PADT;
     extern __shared__ __align__(16) float sm[];
-    const int N = a.dstate;
+    const int N = a.dstate, NP2 = seg_pairs(N);
     const int d = blockIdx.x / g.ctas_per_d;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* tab = sm;
-    float* s_cw = tab + N * kSegTR;
-    float* s_cwA = s_cw + N;
-    float* s_A2 = s_cwA + N;
-    const int head = (N * kSegTR + 3 * N + 3) / 4 * 4;
+    const int head = seg_head_floats(N);
     {
         unsigned dyn;
         asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
         if ((size_t)dyn < (size_t)(head + g.warps * seg_bwd_warp_floats<R>(N)) * sizeof(float)) return;
     }
+    float2* tab = reinterpret_cast<float2*>(sm);
+    float2* s_cw = tab + NP2 * kSegTR;
+    float2* s_cwA = s_cw + NP2;
+    float2* s_A2 = s_cwA + NP2;
     float* wr = sm + head + warp * seg_bwd_warp_floats<R>(N);
     float* su = wr;
     int* sk = reinterpret_cast<int*>(su + PADT);
     float* sd = reinterpret_cast<float*>(sk + PADT);
     int* se = reinterpret_cast<int*>(sd + PADT);
-    float* gcar = reinterpret_cast<float*>(se + PADT);   // [2][N] gamma terms entering from the next tile
-    float* ecar = gcar + 2 * N;                          // [N] state entering the tile
-    SegWarp* W = reinterpret_cast<SegWarp*>(ecar + N);
-    float2* sacc = reinterpret_cast<float2*>(wr + (seg_bwd_warp_floats<R>(N) - 64 * N));   // [N][32]
+    float2* gcar = reinterpret_cast<float2*>(se + PADT);   // [2][NP2] terms entering from the next tile
+    float2* ecar = gcar + 2 * NP2;                          // [NP2] state entering the tile
+    SegWarp* W = reinterpret_cast<SegWarp*>(ecar + NP2);
+    float4* sacc = reinterpret_cast<float4*>(wr + (seg_bwd_warp_floats<R>(N) - 128 * NP2));   // [NP2][32]
 
-    {
-        const float* src = gtab + (int64_t)d * N * kSegTR;
-        for (int i = threadIdx.x; i < N * kSegTR; i += blockDim.x) tab[i] = src[i];
-        for (int s = threadIdx.x; s < N; s += blockDim.x) {
-            const float Ar = a.A[d * a.A_sd + s * a.A_sn];
-            const float cw = a.B[d * N + s] * a.C[d * N + s];
-            s_cw[s] = cw;
-            s_cwA[s] = cw * Ar;
-            s_A2[s] = (float)((double)Ar * 1.4426950408889634);
-        }
-    }
+    seg_load_head(a, d, gtab, tab, s_cw, s_cwA, s_A2, true);
     __syncthreads();
     const int grp = (blockIdx.x % g.ctas_per_d) * g.warps + warp;
     if (grp >= g.groups_per_d) return;
@@ -474,16 +520,16 @@ seg_bwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, const floa
     const T* dout = static_cast<const T*>(a.dout);
     T* du = static_cast<T*>(a.du);
 
-    for (int s = 0; s < N; ++s) sacc[s * 32 + lane] = make_float2(0.f, 0.f);
+    for (int sp = 0; sp < NP2; ++sp) sacc[sp * 32 + lane] = make_float4(0.f, 0.f, 0.f, 0.f);
     const int n_tiles = (Ew + TILE - 1) / TILE;
-    for (int s = lane; s < N; s += 32) gcar[(n_tiles & 1) * N + s] = 0.f;
+    for (int sp = lane; sp < NP2; sp += 32) gcar[(n_tiles & 1) * NP2 + sp] = make_float2(0.f, 0.f);
     float l_ddi = 0.f, l_dda = 0.f, l_dD = 0.f;
     __syncwarp();
 
     for (int t = n_tiles - 1; t >= 0; --t) {
         const int p0 = t * TILE;
-        const float* gin = gcar + ((t + 1) & 1) * N;
-        float* gout = gcar + (t & 1) * N;
+        const float2* gin = gcar + ((t + 1) & 1) * NP2;
+        float2* gout = gcar + (t & 1) * NP2;
 #pragma unroll
         for (int m = 0; m < R; ++m) {
             const int q = m * 32 + lane, p = p0 + q;
@@ -505,13 +551,12 @@ seg_bwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, const floa
             sk[segpad(q)] = kv;
             se[segpad(q)] = e;
         }
-        const int c0 = seg_find(vs, nc, p0);
-        const int e0 = W->base[c0] + (p0 - vs[c0]);
-        if (t > 0 && e0 >= 0 && e0 < a.n_events) {
-            const int64_t slot = (int64_t)e0 / TILE + W->ch[c0];
-            for (int s = lane; s < N; s += 32) ecar[s] = carries[slot * N + s];
-        } else {
-            for (int s = lane; s < N; s += 32) ecar[s] = 0.f;
+        {
+            const int c0 = seg_find(vs, nc, p0);
+            const int e0 = W->base[c0] + (p0 - vs[c0]);
+            const float2* src = reinterpret_cast<const float2*>(carries) + ((int64_t)e0 / TILE + W->ch[c0]) * NP2;
+            const bool from = t > 0 && e0 >= 0 && e0 < a.n_events;
+            for (int sp = lane; sp < NP2; sp += 32) ecar[sp] = from ? src[sp] : make_float2(0.f, 0.f);
         }
         __syncwarp();
 
@@ -551,75 +596,84 @@ seg_bwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, const floa
 #pragma unroll
         for (int r = 0; r < R; ++r) te[r] = tg[r] = ta[r] = 0.f;
 
-        for (int s = 0; s < N; ++s) {
-            const float* ts = tab + s * kSegTR;
-            float av[R];
+        for (int sp = 0; sp < NP2; ++sp) {
+            const float2* ts = tab + sp * kSegTR;
+            float2 av[R];
 #pragma unroll
             for (int r = 0; r < R; ++r) av[r] = ts[ix[r]];
             if (wexact && exm) {
-                const float A2 = s_A2[s];
+                const float2 A2 = s_A2[sp];
 #pragma unroll
                 for (int r = 0; r < R; ++r)
-                    if (exm >> r & 1) av[r] = decay_fast(event_delta(dti, dta, sk[segpad(q0 + r)]), A2);
+                    if (exm >> r & 1) {
+                        const float dlr = event_delta(dti, dta, sk[segpad(q0 + r)]);
+                        av[r] = make_float2(decay_fast(dlr, A2.x), decay_fast(dlr, A2.y));
+                    }
             }
             // forward: incoming state of each lane
-            float A = av[0], Bv = w[0];
+            float2 A = av[0], Bv = f2(w[0]);
 #pragma unroll
             for (int r = 1; r < R; ++r) {
-                Bv = fmaf(av[r], Bv, w[r]);
-                A *= av[r];
+                Bv = __ffma2_rn(av[r], Bv, f2(w[r]));
+                A = __fmul2_rn(A, av[r]);
             }
             seg_scan_up(A, Bv, lane);
-            float Ae = __shfl_up_sync(kFull, A, 1), Be = __shfl_up_sync(kFull, Bv, 1);
-            if (lane == 0) { Ae = 1.f; Be = 0.f; }
-            const float eta_in = fmaf(Ae, ecar[s], Be);
+            float2 Ae = shfl_up2(A, 1), Be = shfl_up2(Bv, 1);
+            if (lane == 0) {
+                Ae = make_float2(1.f, 1.f);
+                Be = make_float2(0.f, 0.f);
+            }
+            const float2 eta_in = __ffma2_rn(Ae, ecar[sp], Be);
             // reverse: multiplier of event r is the next event's decay (0 after
             // a channel's last event); lane 31's last event takes the term
             // entering from the next tile instead
-            const float a_next = __shfl_down_sync(kFull, av[0], 1);
-            const float g_in = gin[s];
-            float mlast = (lane == 31) ? 1.f : a_next;
-            if (lsm >> (R - 1) & 1) mlast = (lane == 31) ? 1.f : 0.f;
-            float G = (lane == 31) ? g_in : 0.f;
-            float M = (lane == 31) ? 0.f : 1.f;
-            G = fmaf(mlast, G, qv[R - 1]);
-            M *= mlast;
+            const float2 a_next = shfl_down2(av[0], 1);
+            const float2 g_in = gin[sp];
+            const bool top = lane == 31;
+            float2 mlast = top ? f2(1.f) : a_next;
+            if (!top && (lsm >> (R - 1) & 1)) mlast = f2(0.f);
+            float2 G = top ? g_in : f2(0.f);
+            float2 M = top ? f2(0.f) : f2(1.f);
+            G = __ffma2_rn(mlast, G, f2(qv[R - 1]));
+            M = __fmul2_rn(M, mlast);
 #pragma unroll
             for (int r = R - 2; r >= 0; --r) {
-                const float m = (lsm >> r & 1) ? 0.f : av[r + 1];
-                G = fmaf(m, G, qv[r]);
-                M *= m;
+                const float2 m = (lsm >> r & 1) ? f2(0.f) : av[r + 1];
+                G = __ffma2_rn(m, G, f2(qv[r]));
+                M = __fmul2_rn(M, m);
             }
             seg_scan_down(M, G, lane);
-            const float X = __shfl_down_sync(kFull, G, 1);
+            const float2 X = shfl_down2(G, 1);
             // pass 2: states and adjoints of the lane's events
-            const float cw = s_cw[s], cwA = s_cwA[s];
-            float ap[R];
-            float eta = eta_in;
+            const float2 cw = s_cw[sp], cwA = s_cwA[sp];
+            float2 ap[R];
+            float2 eta = eta_in;
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-                ap[r] = av[r] * eta;
-                eta = ap[r] + w[r];
-                te[r] = fmaf(cw, eta, te[r]);
+                ap[r] = __fmul2_rn(av[r], eta);
+                eta = __fadd2_rn(ap[r], f2(w[r]));
+                te[r] = fmaf(cw.x, eta.x, fmaf(cw.y, eta.y, te[r]));
             }
-            float gam = (lane == 31) ? g_in : X;
-            float SA = 0.f, SB = 0.f;
+            float2 gam = top ? g_in : X;
+            float2 SA = f2(0.f), SB = f2(0.f);
 #pragma unroll
             for (int r = R - 1; r >= 0; --r) {
-                const float m = (r == R - 1) ? mlast : ((lsm >> r & 1) ? 0.f : av[r + 1]);
-                gam = fmaf(m, gam, qv[r]);
-                tg[r] = fmaf(cw, gam, tg[r]);
-                const float pr = gam * ap[r];
-                ta[r] = fmaf(cwA, pr, ta[r]);
-                SA = fmaf(pr, dl[r], SA);
-                SB = fmaf(gam, w[r], SB);
+                const float2 m = (r == R - 1) ? mlast : ((lsm >> r & 1) ? f2(0.f) : av[r + 1]);
+                gam = __ffma2_rn(m, gam, f2(qv[r]));
+                tg[r] = fmaf(cw.x, gam.x, fmaf(cw.y, gam.y, tg[r]));
+                const float2 pr = __fmul2_rn(gam, ap[r]);
+                ta[r] = fmaf(cwA.x, pr.x, fmaf(cwA.y, pr.y, ta[r]));
+                SA = __ffma2_rn(pr, f2(dl[r]), SA);
+                SB = __ffma2_rn(gam, f2(w[r]), SB);
             }
             // term entering the previous tile: this tile's first decay x gamma
-            if (lane == 0) gout[s] = av[0] * gam;
-            float2 acc2 = sacc[s * 32 + lane];
-            acc2.x += SA;
-            acc2.y += SB;
-            sacc[s * 32 + lane] = acc2;
+            if (lane == 0) gout[sp] = __fmul2_rn(av[0], gam);
+            float4 acc4 = sacc[sp * 32 + lane];
+            acc4.x += SA.x;
+            acc4.y += SA.y;
+            acc4.z += SB.x;
+            acc4.w += SB.y;
+            sacc[sp * 32 + lane] = acc4;
         }
         // ---- per-event outputs
 #pragma unroll
@@ -652,16 +706,25 @@ seg_bwd_kernel(ScanArgs a, const float* __restrict__ gtab, SegGeom g, const floa
         l_dD += __shfl_xor_sync(kFull, l_dD, off);
     }
     float* part = a.ws_part + ((int64_t)grp * a.dim + d) * a.part_stride;
-    for (int s = lane; s < N; s += 32) {
-        float SA = 0.f, SB = 0.f;
+    for (int sp = lane; sp < NP2; sp += 32) {
+        float4 t4 = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int l = 0; l < 32; ++l) {
-            const float2 v = sacc[s * 32 + l];
-            SA += v.x;
-            SB += v.y;
+            const float4 v = sacc[sp * 32 + l];
+            t4.x += v.x;
+            t4.y += v.y;
+            t4.z += v.z;
+            t4.w += v.w;
         }
-        part[s] = s_cw[s] * SA;
-        part[N + s] = a.C[d * N + s] * SB;
-        part[2 * N + s] = a.B[d * N + s] * SB;
+        const float2 cw = s_cw[sp];
+        const float sa[2] = {t4.x, t4.y}, sb[2] = {t4.z, t4.w}, c[2] = {cw.x, cw.y};
+        for (int h = 0; h < 2; ++h) {
+            const int s = 2 * sp + h;
+            if (s < N) {
+                part[s] = c[h] * sa[h];
+                part[N + s] = a.C[d * N + s] * sb[h];
+                part[2 * N + s] = a.B[d * N + s] * sb[h];
+            }
+        }
     }
     if (lane == 0) {
         part[3 * N] = l_ddi;
@@ -697,12 +760,10 @@ SegGeom seg_geom(const ScanArgs& a, int warps) {
 }
 
 size_t seg_fwd_smem(int N) {
-    const int head = (N * kSegTR + 3 * N + 3) / 4 * 4;
-    return (size_t)(head + kSegFwdWarps * seg_fwd_warp_floats<kSegR>(N)) * sizeof(float);
+    return (size_t)(seg_head_floats(N) + kSegFwdWarps * seg_fwd_warp_floats<kSegR>(N)) * sizeof(float);
 }
 size_t seg_bwd_smem(int N) {
-    const int head = (N * kSegTR + 3 * N + 3) / 4 * 4;
-    return (size_t)(head + kSegBwdWarps * seg_bwd_warp_floats<kSegR>(N)) * sizeof(float);
+    return (size_t)(seg_head_floats(N) + kSegBwdWarps * seg_bwd_warp_floats<kSegR>(N)) * sizeof(float);
 }
 
 // Opt a kernel into the device's shared-memory maximum (once per kernel and
@@ -729,10 +790,10 @@ bcm_status seg_optin(const void* kernel, size_t smem, const char* what) {
 }
 
 bcm_status seg_build_table(const ScanArgs& a, float* tab, cudaStream_t st) {
-    const int64_t total = (int64_t)a.dim * a.dstate * kSegTR;
+    const int64_t total = (int64_t)a.dim * seg_pairs(a.dstate) * kSegTR;
     const int threads = 256;
     const int grid = (int)std::min<int64_t>((total + threads - 1) / threads, (int64_t)sm_count() * 8);
-    seg_table_kernel<<<grid, threads, 0, st>>>(a, tab);
+    seg_table_kernel<<<grid, threads, 0, st>>>(a, reinterpret_cast<float2*>(tab));
     BCM_LAUNCH_CHECK();
     return BCM_OK;
 }
@@ -746,7 +807,8 @@ bcm_status seg_fwd_t(const ScanArgs& a, const float* tab, float* carries, cudaSt
         const bcm_status s = seg_optin(reinterpret_cast<const void*>(kern), smem, "flat_ch fwd");
         if (s != BCM_OK) return s;
     }
-    kern<<<a.dim * g.ctas_per_d, 32 * kSegFwdWarps, smem, st>>>(a, tab, g, carries);
+    kern<<<a.dim * g.ctas_per_d, 32 * kSegFwdWarps, smem, st>>>(a, reinterpret_cast<const float2*>(tab), g,
+                                                                 carries);
     BCM_LAUNCH_CHECK();
     return BCM_OK;
 }
@@ -760,7 +822,8 @@ bcm_status seg_bwd_t(const ScanArgs& a, const float* tab, const float* carries, 
         const bcm_status s = seg_optin(reinterpret_cast<const void*>(kern), smem, "flat_ch bwd");
         if (s != BCM_OK) return s;
     }
-    kern<<<a.dim * g.ctas_per_d, 32 * kSegBwdWarps, smem, st>>>(a, tab, g, carries);
+    kern<<<a.dim * g.ctas_per_d, 32 * kSegBwdWarps, smem, st>>>(a, reinterpret_cast<const float2*>(tab), g,
+                                                                 carries);
     BCM_LAUNCH_CHECK();
     return BCM_OK;
 }
@@ -783,12 +846,12 @@ bool seg_selected(const ScanArgs& a) {
 }
 
 size_t seg_table_bytes(const ScanArgs& a) {
-    return align_up((size_t)a.dim * a.dstate * kSegTR * sizeof(float), 256);
+    return align_up((size_t)a.dim * seg_pairs(a.dstate) * kSegTR * sizeof(float2), 256);
 }
 
 size_t seg_carry_bytes(const ScanArgs& a) {
     const size_t slots = (size_t)a.n_events / SegTile<kSegR>::TILE + (size_t)a.n_channels + 1;
-    return align_up(slots * a.dstate * sizeof(float), 256);
+    return align_up(slots * seg_pairs(a.dstate) * sizeof(float2), 256);
 }
 
 // Rows of partials the backward writes (groups per feature x dim).

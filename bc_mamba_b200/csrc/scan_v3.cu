@@ -728,7 +728,9 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
                 if (real && (!hit || dl > dlim)) {
 #pragma unroll
                     for (int g = 0; g < G; ++g) {
-                        dec[g] = decay_fast(dl, A2[g]);
+                        // tabulated gaps keep the table's value (the backward
+                        // reads the same table), others take exp2f
+                        if (!hit) dec[g] = decay_fast(dl, A2[g]);
                         if (dl > dclamp) {
                             const float x = dl * A2[g];
                             corr[g] += fmaxf(fminf(x, 126.0f), -126.0f) - x;
