@@ -73,15 +73,19 @@ class _Proj(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, y, w, c, tf32: bool):
+        from .interface import cuda_stage
+
         ctx.save_for_backward(y, w)
         ctx.tf32 = tf32
-        with _tf32(tf32 and y.is_cuda):
+        with cuda_stage("out_projection"), _tf32(tf32 and y.is_cuda):
             return F.linear(y, w, c)
 
     @staticmethod
     def backward(ctx, g):
+        from .interface import cuda_stage
+
         y, w = ctx.saved_tensors
-        with _tf32(ctx.tf32 and y.is_cuda):
+        with cuda_stage("out_projection_backward"), _tf32(ctx.tf32 and y.is_cuda):
             dy = g @ w if ctx.needs_input_grad[0] else None
             dw = g.reshape(-1, g.shape[-1]).t() @ y.reshape(-1, y.shape[-1]) if ctx.needs_input_grad[1] else None
         return dy, dw, None, None

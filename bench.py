@@ -217,8 +217,14 @@ def stage_times(step, zero, flush, steps):
             step()
     torch.cuda.synchronize()
     per_op = {k: 0.0 for k in STAGE_OPS.values()}
+    other = {}
     for name, s_ev, e_ev in log:
-        per_op[STAGE_OPS[name]] += s_ev.elapsed_time(e_ev) / steps
+        ms = s_ev.elapsed_time(e_ev) / steps
+        if name in STAGE_OPS:
+            per_op[STAGE_OPS[name]] += ms
+        else:
+            other[name] = other.get(name, 0.0) + ms
+    stage_times.other = other
     return per_op
 
 
@@ -392,6 +398,7 @@ def run_stack(args, cfg, rank, world, local, dev):
         "pipeline_roofline": pipe,
         "hot_path": {"ms_per_step": hot_ms, "events_per_s": E_all / (hot_ms * 1e-3),
                      "other_ms_per_step": ms_per_step - hot_ms,
+                     "other_timed_ms": getattr(stage_times, "other", {}),
                      "other": "out_proj GEMMs (TF32 tensor cores, outside the event path), membrane "
                               "updates, gradient all-reduces, launch gaps"},
         "per_op_ms": per_op,
