@@ -602,7 +602,7 @@ BwdLayout bwd_layout(const bcm_flat_ch_args* p) {
     L.weff_bytes = p->pw_B ? align_up((size_t)2 * p->dim * p->dstate * sizeof(float), 256) : 0;
     L.dweff_off = L.weff_off + L.weff_bytes;
     L.order_off = L.dweff_off + L.weff_bytes;
-    L.total = L.order_off + (L.staged ? row_order_bytes(a) : 0);
+    L.total = L.order_off + (L.staged ? staged_prep_bytes(a) : 0);
     return L;
 }
 
@@ -656,10 +656,8 @@ extern "C" bcm_status bcm_flat_ch_bwd(const bcm_flat_ch_args* p, cudaStream_t st
         if (st != BCM_OK) return st;
     } else if (p->n_events > 0 && dw && dw_fast_supported(a.dstate)) {
         if (L.staged) {
-            int* order = reinterpret_cast<int*>(ws + L.order_off);
-            st = row_order_launch(a, order, stream);
+            st = staged_prep_launch(a, ws + L.order_off, stream);
             if (st != BCM_OK) return st;
-            a.row_order = order;
         }
         st = dw_fast_launch(a, p->dtype, true, stream);
         if (st != BCM_OK) return st;

@@ -39,6 +39,9 @@ struct ScanArgs {
     const int* row_order;  // staged kernels (nullable): batch rows of each feature d in
                            // descending event count, [dim][n_channels/dim], so the rows a
                            // warp walks in lockstep have similar lengths
+    const float* dtab;     // staged kernels (nullable): decay tables computed once per call,
+                           // [dim][padded dstate][kKT3 + 1], copied by each CTA instead of
+                           // evaluating exp2 in double per CTA
 };
 
 // Batch row of slot b of feature d in the staged kernels' walk.
@@ -161,10 +164,11 @@ bool seg_supported(const ScanArgs& a);
 // (BCM_SCAN_SEG: 0 never, 1 where the staged kernels do not apply (default),
 // 2 wherever supported).
 bool seg_selected(const ScanArgs& a);
-// Staged kernels: the row order (scan_row) of every feature, written into
-// `order` ([dim][B] ints, row_order_bytes) by one small kernel.
-size_t row_order_bytes(const ScanArgs& a);
-bcm_status row_order_launch(const ScanArgs& a, int* order, cudaStream_t st);
+// Staged kernels: per-call preparation in a workspace of staged_prep_bytes:
+// the row order (scan_row) of every feature and the decay tables (dtab);
+// staged_prep_launch fills it and points a.row_order / a.dtab at it.
+size_t staged_prep_bytes(const ScanArgs& a);
+bcm_status staged_prep_launch(ScanArgs& a, void* ws, cudaStream_t st);
 size_t seg_table_bytes(const ScanArgs& a);
 size_t seg_carry_bytes(const ScanArgs& a);
 int seg_part_rows(const ScanArgs& a);

@@ -287,6 +287,7 @@ void scan_fill_args(const bcm_flat_ch_args* p, ScanArgs& a) {
     a.ws_ckpt = nullptr; a.ws_part = nullptr; a.part_stride = 0;
     a.ckpt = nullptr;
     a.row_order = nullptr;
+    a.dtab = nullptr;
     if (p->ckpt != nullptr && (seg_selected(a) || v3_ckpt_bytes(a) > 0)) a.ckpt = p->ckpt;   // else ignored
 }
 
@@ -330,7 +331,7 @@ extern "C" size_t bcm_flat_ch_fwd_workspace_bytes(const bcm_flat_ch_args* p) {
     if (fwd_seg(p, a)) return fwd_pw_bytes(p) + seg_table_bytes(a);
     if (p->n_events > 0 && p->n_channels > 0 && p->dim > 0 && p->dstate > 0) {
         scan_fill_args(p, a);
-        if (fwd_staged(p, a)) return fwd_pw_bytes(p) + row_order_bytes(a);
+        if (fwd_staged(p, a)) return fwd_pw_bytes(p) + staged_prep_bytes(a);
     }
     return fwd_pw_bytes(p);
 }
@@ -372,11 +373,9 @@ extern "C" bcm_status bcm_flat_ch_fwd(const bcm_flat_ch_args* p, cudaStream_t st
     // every other path writes the chunks that exist onto zeros
     const bool staged = fwd_staged(p, a);
     if (staged) {
-        // rows of similar event counts share a warp
-        int* order = reinterpret_cast<int*>(static_cast<char*>(p->workspace) + fwd_pw_bytes(p));
-        st = row_order_launch(a, order, stream);
+        // rows of similar event counts share a warp; decay tables once per call
+        st = staged_prep_launch(a, static_cast<char*>(p->workspace) + fwd_pw_bytes(p), stream);
         if (st != BCM_OK) return st;
-        a.row_order = order;
     }
     if (!staged)
         BCM_CUDA_TRY(cudaMemsetAsync(p->x, 0, (size_t)a.n_channels * a.n_chunks * 2 * a.dstate * sizeof(float),

@@ -53,17 +53,24 @@ struct V3 {
 
 // Table layout: float4 groups of states, [s/4][row] -> a lane's G decays of
 // one row are G/4 vector loads; rows of different lanes spread over banks.
+// Decay of gap `row` for state s of feature d: from the per-call table when
+// one was computed, else evaluated here (row 0 and padded states = 1).
+template <int NP>
+__device__ __forceinline__ float table_entry(const ScanArgs& a, int d, int s, int row) {
+    if (a.dtab != nullptr) return a.dtab[((int64_t)d * NP + s) * kRows3 + row];
+    float v = 1.f;
+    if (row > 0 && s < a.dstate) {
+        const float A2 = (float)((double)a.A[d * a.A_sd + s * a.A_sn] * 1.4426950408889634);
+        v = decay_exact(event_delta(a.dt_idle[d], a.dt_active[d], row), A2);
+    }
+    return v;
+}
+
 template <int NP>
 __device__ void build_table3(float* tab, const ScanArgs& a, int d, int lane) {
-    const float dti = a.dt_idle[d], dta = a.dt_active[d];
     for (int e = lane; e < kRows3 * NP; e += 32) {
-        const int row = e / NP, s = e % NP;
-        float v = 1.f;
-        if (row > 0 && s < a.dstate) {
-            const float A2 = (float)((double)a.A[d * a.A_sd + s * a.A_sn] * 1.4426950408889634);
-            v = decay_exact(event_delta(dti, dta, row), A2);
-        }
-        tab[((s >> 2) * kRows3 + row) * 4 + (s & 3)] = v;
+        const int row = e % kRows3, s = e / kRows3;
+        tab[((s >> 2) * kRows3 + row) * 4 + (s & 3)] = table_entry<NP>(a, d, s, row);
     }
     __syncwarp();
 }
@@ -535,14 +542,9 @@ static_assert(V4<2, 64>::WARP_FLOATS % 4 == 0 && V4<1, 16>::WARP_FLOATS % 4 == 0
 // groups [state/4][row] (as build_table3) for G >= 4.
 template <int NP, int G>
 __device__ void build_table_block(float* tab, const ScanArgs& a, int d) {
-    const float dti = a.dt_idle[d], dta = a.dt_active[d];
     for (int e = threadIdx.x; e < kRows3 * NP; e += blockDim.x) {
-        const int row = e / NP, s = e % NP;
-        float v = 1.f;
-        if (row > 0 && s < a.dstate) {
-            const float A2 = (float)((double)a.A[d * a.A_sd + s * a.A_sn] * 1.4426950408889634);
-            v = decay_exact(event_delta(dti, dta, row), A2);
-        }
+        const int row = e % kRows3, s = e / kRows3;
+        const float v = table_entry<NP>(a, d, s, row);
         if (G >= 4) tab[((s >> 2) * kRows3 + row) * 4 + (s & 3)] = v;
         else if (G == 2) tab[((s >> 1) * kRows3 + row) * 2 + (s & 1)] = v;
         else tab[s * kRows3 + row] = v;
@@ -919,19 +921,49 @@ __global__ void row_order_kernel(const int32_t* __restrict__ cu, int dim, int Bn
     }
 }
 
-size_t row_order_bytes(const ScanArgs& a) {
+// Decay tables of the staged kernels, [dim][NP][kKT3 + 1], once per call.
+__global__ void staged_table_kernel(ScanArgs a, int NP, float* __restrict__ tab) {
+    const int64_t total = (int64_t)a.dim * NP * kRows3;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int row = (int)(i % kRows3);
+        const int64_t ds = i / kRows3;
+        const int s = (int)(ds % NP), d = (int)(ds / NP);
+        float v = 1.f;
+        if (row > 0 && s < a.dstate) {
+            const float A2 = (float)((double)a.A[d * a.A_sd + s * a.A_sn] * 1.4426950408889634);
+            v = decay_exact(event_delta(a.dt_idle[d], a.dt_active[d], row), A2);
+        }
+        tab[i] = v;
+    }
+}
+
+static size_t row_order_bytes(const ScanArgs& a) {
     return align_up((size_t)a.n_channels * sizeof(int), 256);
 }
 
-bcm_status row_order_launch(const ScanArgs& a, int* order, cudaStream_t st) {
+size_t staged_prep_bytes(const ScanArgs& a) {
+    return row_order_bytes(a) + align_up((size_t)a.dim * padded_states(a.dstate) * kRows3 * sizeof(float), 256);
+}
+
+bcm_status staged_prep_launch(ScanArgs& a, void* ws, cudaStream_t st) {
     const int Bn = a.n_channels / a.dim;
     if (Bn > 4096) {
         set_error("flat_ch: row order needs at most 4096 rows per feature, got %d", Bn);
         return BCM_ERR_UNSUPPORTED;
     }
+    int* order = static_cast<int*>(ws);
+    float* tab = reinterpret_cast<float*>(static_cast<char*>(ws) + row_order_bytes(a));
     const int threads = std::min(256, std::max(32, (Bn + 31) / 32 * 32));
     row_order_kernel<<<a.dim, threads, Bn * sizeof(int), st>>>(a.cu, a.dim, Bn, order);
     BCM_LAUNCH_CHECK();
+    const int NP = padded_states(a.dstate);
+    const int64_t total = (int64_t)a.dim * NP * kRows3;
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)sm_count() * 8);
+    staged_table_kernel<<<grid, 256, 0, st>>>(a, NP, tab);
+    BCM_LAUNCH_CHECK();
+    a.row_order = order;
+    a.dtab = tab;
     return BCM_OK;
 }
 
