@@ -345,15 +345,14 @@ __device__ __forceinline__ int lower_bound8(const int32_t* __restrict__ a, int n
 // ---- sweep forward -------------------------------------------------------------
 // A warp owns one batch row b, 32 features (lane = channel) and a range of
 // positions [t_beg, t_end) (whole 32-position words).  Each lane finds its
-// channel's first event at or after t_beg, then walks its events in batches of
-// kQ held in registers: the next batch is loaded when the current one starts,
-// so its loads have kQ events' worth of positions to arrive, and the event a
-// position needs is picked from the batch by select.  Per position the lane
-// holds or replaces its value and the warp stores one coalesced row of 32
-// features; per 32 positions each lane stores its word of event bits (the
-// bitmap the backward sweeps), and the unit records its lanes' first event
-// indices.  No shared memory and few registers, so many units run per SM.
-constexpr int kQ = 4;               // events per register batch
+// channel's first event at or after t_beg, then keeps the times and values of
+// its next kQ events in registers, loaded kQ events ahead so every load has
+// kQ gaps' worth of positions to arrive.  Per position the lane holds or
+// replaces its value and the warp stores one coalesced row of 32 features;
+// per 32 positions each lane stores its word of event bits (the bitmap the
+// backward sweeps), and the unit records its lanes' first event indices.
+// No shared memory and few registers, so many units run per SM.
+constexpr int kQ = 4;               // events held ahead per lane
 constexpr int kFU = 4;              // units (warps) per CTA
 constexpr int kSweepUnitsPerSM = 48;
 
@@ -361,17 +360,6 @@ struct SweepLayout {
     int n_dblk, part_len, n_parts;
     int64_t n_units;
 };
-
-template <typename Tin>
-__device__ __forceinline__ void load_batch(const int32_t* __restrict__ ts, const Tin* __restrict__ y, int beg, int n,
-                                           int j0, int (&tq)[kQ], float (&yq)[kQ]) {
-#pragma unroll
-    for (int q = 0; q < kQ; ++q) {
-        const int j = j0 + q;
-        tq[q] = (j < n) ? ts[beg + j] : INT_MAX;
-        yq[q] = (j < n) ? to_f32<Tin>(y[beg + j]) : 0.f;
-    }
-}
 
 template <typename Tin, typename Tout>
 __global__ void __launch_bounds__(kFU * 32)
@@ -393,38 +381,34 @@ restore_fwd_sweep(const Tin* __restrict__ y, const int32_t* __restrict__ ts, con
     const int p = (u.t_beg == 0 || n <= 0) ? 0 : lower_bound8(ts + beg, n, u.t_beg);
     if (e_start != nullptr) e_start[unit * 32 + lane] = p;
     float cur = (p > 0) ? to_f32<Tin>(y[beg + p - 1]) : 0.f;
-    int tq[kQ], tn[kQ];
-    float yq[kQ], yn[kQ];
-    load_batch(ts, y, beg, n, p, tq, yq);
-    load_batch(ts, y, beg, n, p + kQ, tn, yn);
-    int jb = p + 2 * kQ;   // first event of the batch after `tn`
-    int c = 0;             // next event of the current batch
+    int tq[kQ];
+    float yq[kQ];
+#pragma unroll
+    for (int q = 0; q < kQ; ++q) {
+        const int j = p + q;
+        tq[q] = (j < n) ? ts[beg + j] : INT_MAX;
+        yq[q] = (j < n) ? to_f32<Tin>(y[beg + j]) : 0.f;
+    }
+    int nxt = p + kQ;
     Tout* col = out + (u.b * L + u.t_beg) * (int64_t)D + (valid ? d : 0);
     uint32_t* mcol = (bm != nullptr) ? bm + (u.b * nw + (u.t_beg >> 5)) * (int64_t)D + d : nullptr;
     for (int t0 = u.t_beg; t0 < u.t_end; t0 += 32) {
         uint32_t m = 0u;
         const int rows = min(32, u.t_end - t0);
-#pragma unroll 4
-        for (int r = 0; r < rows; ++r) {
-            int tnext = tq[kQ - 1];
+#pragma unroll 8
+        for (int r = 0; r < 32; ++r) {
+            if (r >= rows) break;   // warp-uniform
+            if (t0 + r == tq[0]) {
+                cur = yq[0];
 #pragma unroll
-            for (int q = kQ - 2; q >= 0; --q) tnext = (c == q) ? tq[q] : tnext;
-            if (t0 + r == tnext) {
-                float v = yq[kQ - 1];
-#pragma unroll
-                for (int q = kQ - 2; q >= 0; --q) v = (c == q) ? yq[q] : v;
-                cur = v;
-                m |= 1u << r;
-                if (++c == kQ) {   // batch done: the prefetched one takes over
-#pragma unroll
-                    for (int q = 0; q < kQ; ++q) {
-                        tq[q] = tn[q];
-                        yq[q] = yn[q];
-                    }
-                    load_batch(ts, y, beg, n, jb, tn, yn);
-                    jb += kQ;
-                    c = 0;
+                for (int q = 0; q + 1 < kQ; ++q) {
+                    tq[q] = tq[q + 1];
+                    yq[q] = yq[q + 1];
                 }
+                tq[kQ - 1] = (nxt < n) ? ts[beg + nxt] : INT_MAX;
+                yq[kQ - 1] = (nxt < n) ? to_f32<Tin>(y[beg + nxt]) : 0.f;
+                ++nxt;
+                m |= 1u << r;
             }
             if (valid) col[(int64_t)r * D] = from_f32<Tout>(cur);
         }
@@ -469,22 +453,18 @@ restore_bwd_bitmap(const T* __restrict__ dout, const int32_t* __restrict__ cu, c
     int open = -1;          // owned event whose interval is running
     float acc = 0.f;
     const T* col = dout + (u.b * L + u.t_beg) * (int64_t)D + dc;
-    // rows in batches of 32, the next batch's loads issued before the current
-    // one is summed
-    auto load_rows = [&](int t0, float (&v)[32]) {
+    for (int t0 = u.t_beg; t0 < L; t0 += 32) {
+        if (t0 >= u.t_end && !__any_sync(kFull, open >= 0)) break;
+        const uint32_t m0 = valid ? mcol[(int64_t)(t0 >> 5) * D] : 0u;
+        float v[32];
         if (t0 + 32 <= L) {
 #pragma unroll
-            for (int r = 0; r < 32; ++r) v[r] = to_f32<T>(col[(int64_t)(t0 - u.t_beg + r) * D]);
+            for (int r = 0; r < 32; ++r) v[r] = to_f32<T>(col[(int64_t)r * D]);
         } else {
 #pragma unroll
-            for (int r = 0; r < 32; ++r)
-                v[r] = (t0 + r < L) ? to_f32<T>(col[(int64_t)(t0 - u.t_beg + r) * D]) : 0.f;
+            for (int r = 0; r < 32; ++r) v[r] = (t0 + r < L) ? to_f32<T>(col[(int64_t)r * D]) : 0.f;
         }
-    };
-    float va[32], vb[32];
-    load_rows(u.t_beg, va);
-    auto sum_rows = [&](int t0, const float (&v)[32]) {
-        const uint32_t m0 = valid ? mcol[(int64_t)(t0 >> 5) * D] : 0u;
+        col += (int64_t)32 * D;
 #pragma unroll
         for (int r = 0; r < 32; ++r) {
             const bool hit = ((m0 >> r) & 1u) != 0u;
@@ -493,21 +473,6 @@ restore_bwd_bitmap(const T* __restrict__ dout, const int32_t* __restrict__ cu, c
             e += hit ? 1 : 0;
             acc = (hit ? 0.f : acc) + v[r];
         }
-    };
-    // (the batch after the current one is loaded whenever it exists: an
-    // interval may open in the current batch; at most one batch per unit is
-    // loaded and not needed)
-    for (int t0 = u.t_beg; t0 < L; t0 += 64) {
-        if (t0 >= u.t_end && !__any_sync(kFull, open >= 0)) break;
-        const bool more = t0 + 32 < L;
-        if (more) load_rows(t0 + 32, vb);
-        sum_rows(t0, va);
-        if (!more) break;
-        if (t0 + 32 >= u.t_end && !__any_sync(kFull, open >= 0)) break;
-        const bool more2 = t0 + 64 < L;
-        if (more2) load_rows(t0 + 64, va);
-        sum_rows(t0 + 32, vb);
-        if (!more2) break;
     }
     if (open >= 0) dy[open] = acc;              // the interval runs to L
 }

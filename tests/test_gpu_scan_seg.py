@@ -141,3 +141,30 @@ def test_seg_bench_shape_rows():
     inp, ch, t, k, cu, mx, u = _events(c)
     p = lambda n: inp[n].numpy()
     _run_and_check(u, k, cu, mx, p("dt_idle"), p("dt_active"), p("A"), p("W_B"), p("W_C"), D=p("D"))
+
+
+def test_seg_and_staged_agree_on_bursty_rows():
+    """Both kernel families on the c4 row layout with 50 % Markov spikes
+    (channels of very different lengths, some over 2048 events): every output
+    and gradient within the fp32 tolerance of each other."""
+    import bc_mamba_b200 as bcm
+    from helpers import assert_close
+
+    ops = bcm.load_ops()
+    c = CONFIGS["c4"].with_(B=32, D=64, L=4000, rho=0.5, spikes="markov", seed=25)
+    inp, ch, t, k, cu, mx, u = _events(c)
+    assert mx > 2048
+    dev = "cuda"
+    T_ = lambda x: torch.as_tensor(np.asarray(x)).to(dev).contiguous()
+    ps = [T_(inp[n].numpy()) for n in ["dt_idle", "dt_active", "A", "W_B", "W_C"]]
+    args = (T_(u), T_(k), T_(cu), mx, *ps)
+    dout = torch.randn(u.size, generator=torch.Generator().manual_seed(3)).to(dev)
+    res = {}
+    for mode in ("0", "2"):
+        os.environ["BCM_SCAN_SEG"] = mode
+        out, x, ck = ops.fwd_flat_ch_ckpt(*args, T_(inp["D"].numpy()), None, None, 0, True, None, None)
+        g = ops.bwd_flat_ch(*args, dout, x, T_(inp["D"].numpy()), None, None, None, 0, True, None, None, ck)
+        res[mode] = [out, x] + list(g)
+    names = ["out", "x", "du", "dA", "dW_B", "dW_C", "ddt_idle", "ddt_active", "dD"]
+    for n, a, b in zip(names, res["0"], res["2"]):
+        assert_close(a, b.cpu().numpy(), TOL_F32, n)
