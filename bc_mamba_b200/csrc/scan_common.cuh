@@ -42,12 +42,17 @@ struct ScanArgs {
     const float* dtab;     // staged kernels (nullable): decay tables computed once per call,
                            // [dim][padded dstate][kKT3 + 1], copied by each CTA instead of
                            // evaluating exp2 in double per CTA
+    int rank_major;        // staged kernels: CTA i walks row group i / dim of feature
+                           // i % dim (set with row_order: every feature's longest rows
+                           // are dispatched first), else feature-major
 };
 
 // Batch row of slot b of feature d in the staged kernels' walk.
 __device__ __forceinline__ int scan_row(const ScanArgs& a, int d, int b) {
     return a.row_order ? a.row_order[d * (a.n_channels / a.dim) + b] : b;
 }
+
+__device__ __forceinline__ bool rank_major(const ScanArgs& a) { return a.rank_major != 0; }
 
 // Decay factor exp2(clamp(delta*A2, -126, 126)) with the accurate exp2f
 // (as the reference): with long-memory states (a close to 1) a biased

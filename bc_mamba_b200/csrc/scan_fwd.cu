@@ -288,6 +288,7 @@ void scan_fill_args(const bcm_flat_ch_args* p, ScanArgs& a) {
     a.ckpt = nullptr;
     a.row_order = nullptr;
     a.dtab = nullptr;
+    a.rank_major = 0;
     if (p->ckpt != nullptr && (seg_selected(a) || v3_ckpt_bytes(a) > 0)) a.ckpt = p->ckpt;   // else ignored
 }
 

@@ -37,6 +37,11 @@ namespace bcm {
 
 namespace {
 
+int env_int(const char* name, int dflt) {
+    const char* e = getenv(name);
+    return e ? atoi(e) : dflt;
+}
+
 constexpr int kR3 = 32;          // events per channel per staged batch
 constexpr int kKT3 = 128;        // tabulated gaps 1..kKT3
 constexpr int kRows3 = kKT3 + 1; // row 0 = identity (padding slots)
@@ -224,8 +229,9 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
     int* s_n = s_beg + CPW;
 
     const int lane = threadIdx.x, grp = lane / LPC, q = lane % LPC;
-    const int d = blockIdx.x / bgroups;
-    const int b0 = (blockIdx.x % bgroups) * CPW;
+    // rank-major: the warps holding every feature's longest rows start first
+    const int d = rank_major(a) ? blockIdx.x % a.dim : blockIdx.x / bgroups;
+    const int b0 = (rank_major(a) ? blockIdx.x / a.dim : blockIdx.x % bgroups) * CPW;
     const int N = a.dstate;
     if (lane < CPW) {
         const int c = scan_row(a, d, b0 + lane) * a.dim + d;
@@ -599,8 +605,9 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = lane / LPC, q = lane % LPC;
-    const int d = blockIdx.x / blocks_per_d;
-    const int b0 = ((blockIdx.x % blocks_per_d) * nwarps + warp) * CPW;
+    // rank-major: the CTAs holding every feature's longest rows start first
+    const int d = rank_major(a) ? blockIdx.x % a.dim : blockIdx.x / blocks_per_d;
+    const int b0 = ((rank_major(a) ? blockIdx.x / a.dim : blockIdx.x % blocks_per_d) * nwarps + warp) * CPW;
     float* tab = sm4;
     float* wbase = sm4 + NP * kRows3 + warp * V::WARP_FLOATS;
     float* s_u = wbase;
@@ -807,8 +814,9 @@ bcm_status launch_fwd_v4(const ScanArgs& a, cudaStream_t st) {
     using V = V4<G, NP>;
     const int bn = a.n_channels / a.dim;
     const int groups = bn / V::CPW;          // warps per feature
+    const int wmax = std::min(v4_max_warps<G, NP>(), std::max(1, env_int("BCM_V4_WPB", 16)));
     int wpb = 1;
-    while (wpb * 2 <= v4_max_warps<G, NP>() && groups % (wpb * 2) == 0) wpb *= 2;
+    while (wpb * 2 <= wmax && groups % (wpb * 2) == 0) wpb *= 2;
     const int blocks_per_d = groups / wpb;
     const size_t smem = (size_t)(NP * kRows3 + wpb * V::WARP_FLOATS) * sizeof(float);
     if (smem > 48 * 1024) {
@@ -849,11 +857,6 @@ bcm_status launch_bwd_v3(const ScanArgs& a, cudaStream_t st) {
     dw_bwd_v3<T, G, LPC><<<a.dim * bgroups, 32, bwd_v3_smem<G, LPC>(), st>>>(a, bgroups);
     BCM_LAUNCH_CHECK();
     return BCM_OK;
-}
-
-int env_int(const char* name, int dflt) {
-    const char* e = getenv(name);
-    return e ? atoi(e) : dflt;
 }
 
 // States per lane of the split forward (BCM_V4_G = 1, 2 or 4 overrides the
@@ -964,6 +967,7 @@ bcm_status staged_prep_launch(ScanArgs& a, void* ws, cudaStream_t st) {
     BCM_LAUNCH_CHECK();
     a.row_order = order;
     a.dtab = tab;
+    a.rank_major = env_int("BCM_V3_RANK_MAJOR", 1) != 0;
     return BCM_OK;
 }
 
