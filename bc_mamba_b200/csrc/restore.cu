@@ -418,6 +418,103 @@ restore_fwd_sweep(const Tin* __restrict__ y, const int32_t* __restrict__ ts, con
     }
 }
 
+// ---- word sweep forward (bitmap first) ---------------------------------------------
+// With the event bitmap built first (event_bitmap_kernel), a warp unit
+// (b, 32 features, positions [t_beg, t_end), the units of the sweep layout)
+// needs no event times in its sweep.  Per 32-position word each lane reads
+// its mask word (one coalesced load per warp, two words ahead) and copies the
+// word's event values, consecutive in its channel's stream, into its column
+// of a shared-memory slot buffer by 4-byte cp.async one word ahead; row r of
+// the word then holds the value of event popc(mask & bits 0..r) - 1 of the
+// word, or the value held into the word when that count is 0: branch-free,
+// with every row one coalesced store of 32 features.  The unit still records
+// its lanes' first event indices for the backward.
+constexpr int kWU = 4;   // units (warps) per CTA, as the sweep layout's kFU
+
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int NG>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(NG) : "memory"); }
+
+template <typename Tin, typename Tout>
+__global__ void __launch_bounds__(kWU * 32)
+restore_fwd_words(const Tin* __restrict__ y, const int32_t* __restrict__ ts, const int32_t* __restrict__ cu,
+                  const uint32_t* __restrict__ bm, int D, int L, int nw, int part_len, int n_dblk, int n_parts,
+                  int64_t n_units, Tout* __restrict__ out, int32_t* __restrict__ e_start) {
+    __shared__ float s_val[kWU][2][32][32];   // [warp][buffer][slot][lane]
+    const int wi = threadIdx.x >> 5;
+    const int64_t unit = (int64_t)blockIdx.x * kWU + wi;
+    if (unit >= n_units) return;   // warp-uniform; the kernel has no block barrier
+    const int lane = threadIdx.x & 31;
+    const BUnit u = bunit(unit, n_dblk, n_parts, part_len, L);
+    const int d = u.d0 + lane;
+    const bool valid = d < D;
+    const int dc = valid ? d : D - 1;   // lanes past D address a real column and store nothing
+    int beg = 0, n = 0;
+    if (valid) {
+        const int64_t c = u.b * D + d;
+        beg = cu[c];
+        n = min(cu[c + 1] - beg, kCap);
+    }
+    const int p = (u.t_beg == 0 || n <= 0) ? 0 : lower_bound8(ts + beg, n, u.t_beg);
+    if (e_start != nullptr) e_start[unit * 32 + lane] = p;
+    float cur = (p > 0) ? to_f32<Tin>(y[beg + p - 1]) : 0.f;
+    int idx = beg + p;   // the next event (global index)
+    const uint32_t* mcol = bm + (u.b * nw + (u.t_beg >> 5)) * (int64_t)D + dc;
+    const int nwd = (u.t_end - u.t_beg + 31) >> 5;   // words of the unit
+    auto mask_at = [&](int w) -> uint32_t { return (valid && w < nwd) ? mcol[(int64_t)w * D] : 0u; };
+    // the values of a word's events (from global index first) into slot buffer buf
+    auto fetch = [&](uint32_t m, int first, int buf) {
+        const int nv = __popc(m);
+        float(*sv)[32] = s_val[wi][buf];
+        for (int k = 0; k < nv; ++k) {
+            if constexpr (sizeof(Tin) == 4) {
+                cp_async4(&sv[k][lane], y + first + k);
+            } else {
+                sv[k][lane] = to_f32<Tin>(y[first + k]);
+            }
+        }
+        cp_async_commit();
+    };
+    uint32_t m0 = mask_at(0), m1 = mask_at(1);
+    fetch(m0, idx, 0);
+    Tout* col = out + (u.b * L + u.t_beg) * (int64_t)D + dc;
+    for (int w = 0; w < nwd; ++w) {
+        const int buf = w & 1;
+        const uint32_t m2 = mask_at(w + 2);
+        const int nv0 = __popc(m0);
+        fetch(m1, idx + nv0, buf ^ 1);   // the next word's values, in flight during this word's rows
+        cp_async_wait<1>();
+        __syncwarp();
+        const float(*sv)[32] = s_val[wi][buf];
+        const int rows = min(32, u.t_end - (u.t_beg + 32 * w));
+        if (rows == 32) {
+#pragma unroll
+            for (int r = 0; r < 32; ++r) {
+                const int k = __popc(m0 & ((2u << r) - 1u));
+                const float v = k ? sv[k ? k - 1 : 0][lane] : cur;
+                if (valid) col[(int64_t)r * D] = from_f32<Tout>(v);
+            }
+        } else {
+            for (int r = 0; r < rows; ++r) {
+                const int k = __popc(m0 & ((2u << r) - 1u));
+                const float v = k ? sv[k ? k - 1 : 0][lane] : cur;
+                if (valid) col[(int64_t)r * D] = from_f32<Tout>(v);
+            }
+        }
+        cur = nv0 ? sv[nv0 ? nv0 - 1 : 0][lane] : cur;
+        idx += nv0;
+        col += (int64_t)32 * D;
+        __syncwarp();   // this buffer is refilled by the next word's fetch
+        m0 = m1;
+        m1 = m2;
+    }
+    cp_async_wait<0>();
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kBU * 32)
 restore_bwd_bitmap(const T* __restrict__ dout, const int32_t* __restrict__ cu, const uint32_t* __restrict__ bm,
@@ -534,12 +631,27 @@ static bcm_status restore_fwd_impl(const void* y_flat, bcm_dtype y_dtype, const 
     int32_t* e_start = bitmap ? reinterpret_cast<int32_t*>(reinterpret_cast<char*>(bitmap) +
                                                            bitmap_words_bytes(n_channels, seqlen))
                               : nullptr;
+    if (bitmap != nullptr && n_events > 0) {
+        // the bitmap first (every word written: zeros, then the words holding
+        // events), then the word sweep reads it instead of the event times
+        BCM_CUDA_TRY(cudaMemsetAsync(bitmap, 0, bitmap_words_bytes(n_channels, seqlen), stream));
+        event_bitmap_kernel<<<(unsigned)((n_channels + 7) / 8), 256, 0, stream>>>(
+            time_steps, cu_seqlens, n_channels, (int)dim, (int)seqlen, nw, bitmap);
+        BCM_LAUNCH_CHECK();
+    }
     auto launch = [&](auto tin, auto tout) -> bcm_status {
         using Tin = decltype(tin);
         using Tout = decltype(tout);
-        restore_fwd_sweep<Tin, Tout><<<(unsigned)((lay.n_units + kFU - 1) / kFU), kFU * 32, 0, stream>>>(
-            static_cast<const Tin*>(y_flat), time_steps, cu_seqlens, (int)dim, (int)seqlen, nw, lay.part_len,
-            lay.n_dblk, lay.n_parts, lay.n_units, static_cast<Tout*>(out), bitmap, e_start);
+        if (bitmap != nullptr && n_events > 0) {
+            static_assert(kWU == kFU, "the word sweep runs the sweep layout's units");
+            restore_fwd_words<Tin, Tout><<<(unsigned)((lay.n_units + kWU - 1) / kWU), kWU * 32, 0, stream>>>(
+                static_cast<const Tin*>(y_flat), time_steps, cu_seqlens, bitmap, (int)dim, (int)seqlen, nw,
+                lay.part_len, lay.n_dblk, lay.n_parts, lay.n_units, static_cast<Tout*>(out), e_start);
+        } else {
+            restore_fwd_sweep<Tin, Tout><<<(unsigned)((lay.n_units + kFU - 1) / kFU), kFU * 32, 0, stream>>>(
+                static_cast<const Tin*>(y_flat), time_steps, cu_seqlens, (int)dim, (int)seqlen, nw, lay.part_len,
+                lay.n_dblk, lay.n_parts, lay.n_units, static_cast<Tout*>(out), bitmap, e_start);
+        }
         BCM_LAUNCH_CHECK();
         return BCM_OK;
     };
