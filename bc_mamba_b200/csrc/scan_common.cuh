@@ -157,6 +157,9 @@ bcm_status v3_launch(const ScanArgs& a, bcm_dtype dtype, bool bwd, cudaStream_t 
 // checkpoint buffer size shared by their forward and backward (0 when either
 // does not apply, in which case ScanArgs::ckpt must be null).
 int v3_ckpt_np(int dstate);
+// Warps of the staged backward for these arguments (its lane groups hold
+// whole channels).
+int64_t v3_bwd_warps(const ScanArgs& a);
 size_t v3_ckpt_bytes(const ScanArgs& a);
 
 // Event-parallel kernels (scan_seg.cu): depthwise, no gate, dstate <= 64.

@@ -842,7 +842,14 @@ bool seg_selected(const ScanArgs& a) {
     const int mode = e ? atoi(e) : 1;
     if (mode == 0 || !seg_supported(a)) return false;
     if (mode >= 2) return true;
-    return !(v3_supported(a, false) && v3_supported(a, true));
+    if (!(v3_supported(a, false) && v3_supported(a, true))) return true;
+    // the staged kernels walk each channel's events in one warp lane group:
+    // with few batch rows per feature (a batch sharded over many ranks) they
+    // leave the SMs short of warps, and the event-parallel kernels, whose
+    // warps hold whole tiles of events, are faster (B200, the 4-block stack
+    // at 16 rows per feature: scan 0.88 ms per step against 1.10 ms; at 32
+    // rows 1.39 against 1.31)
+    return v3_bwd_warps(a) < 5 * sm_count();
 }
 
 size_t seg_table_bytes(const ScanArgs& a) {

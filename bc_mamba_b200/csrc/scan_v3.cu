@@ -895,6 +895,10 @@ bool v3_supported(const ScanArgs& a, bool bwd) {
 
 int v3_ckpt_np(int dstate) { return padded_states(dstate); }
 
+int64_t v3_bwd_warps(const ScanArgs& a) {
+    return (int64_t)a.n_channels / channels_per_warp(a.dstate, true);
+}
+
 size_t v3_ckpt_bytes(const ScanArgs& a) {
     if (a.bc_mode != BCM_BC_DEPTHWISE || a.n_events <= 0 || !v3_supported(a, false) || !v3_supported(a, true))
         return 0;

@@ -15,6 +15,20 @@ from bc_mamba_b200.workloads import CONFIGS
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def staged_only():
+    """The staged kernels at every size (by default small batches take the
+    event-parallel ones)."""
+    import os
+    old = os.environ.get("BCM_SCAN_SEG")
+    os.environ["BCM_SCAN_SEG"] = "0"
+    yield
+    if old is None:
+        os.environ.pop("BCM_SCAN_SEG", None)
+    else:
+        os.environ["BCM_SCAN_SEG"] = old
+
+
 @pytest.mark.parametrize("N", [1, 4, 7, 8, 9, 12, 16, 17, 24, 32, 33, 48, 64])
 def test_staged_dstates(N):
     c = CONFIGS["c0"].with_(B=16, D=8, N=N, L=300, rho=0.25, seed=40 + N)
