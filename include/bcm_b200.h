@@ -358,16 +358,20 @@ typedef struct bcm_flat_ch_args {
     /* scratch */
     void* workspace;
     size_t workspace_bytes;
-    /* nullable: state checkpoints (the normalised state entering every 8th
-     * event of a channel), bcm_flat_ch_ckpt_bytes(args) bytes.  The forward
-     * writes them, a backward given the same buffer reads them instead of
-     * re-running the forward recurrence; ignored when that size is 0. */
+    /* nullable: state checkpoints, bcm_flat_ch_ckpt_bytes(args) bytes: the
+     * normalised state entering every 8th event of a channel (staged
+     * kernels) or entering every 256-event tile of a warp's events
+     * (event-parallel kernels; which family runs depends on the shape and on
+     * BCM_SCAN_SEG, read on every call).  The forward writes them, a backward
+     * given the same buffer and settings reads them instead of re-running
+     * the forward recurrence; ignored when that size is 0. */
     float* ckpt;
 } bcm_flat_ch_args;
 
-/* Bytes of the checkpoint buffer for these arguments: nonzero for the
- * depthwise shapes the staged kernels run (dstate <= 64, the batch rows of
- * a feature filling whole warps), 0 where the buffer would not be used. */
+/* Bytes of the checkpoint buffer for these arguments: nonzero where the
+ * staged kernels (depthwise, dstate <= 64, each feature's batch rows in
+ * whole warps) or the event-parallel kernels (depthwise, no gate,
+ * dstate <= 64) run, 0 where the buffer would not be used. */
 BCM_API size_t bcm_flat_ch_ckpt_bytes(const bcm_flat_ch_args* args);
 BCM_API size_t bcm_flat_ch_fwd_workspace_bytes(const bcm_flat_ch_args* args);
 BCM_API size_t bcm_flat_ch_bwd_workspace_bytes(const bcm_flat_ch_args* args);
