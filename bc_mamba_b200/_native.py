@@ -47,6 +47,9 @@ ABI_SYMBOLS = (
     "bcm_restore_dense_bwd_bitmap",
     "bcm_restore_dense_fwd",
     "bcm_restore_dense_bwd",
+    "bcm_s6_fwd",
+    "bcm_s6_bwd_workspace_bytes",
+    "bcm_s6_bwd",
 )
 
 _ops = None

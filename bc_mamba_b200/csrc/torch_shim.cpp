@@ -822,11 +822,209 @@ std::vector<Tensor> selective_scan_bwd_flat_ch(
     return result;
 }
 
-std::vector<Tensor> dense_scan_unavailable(py::args, py::kwargs) {
-    TORCH_CHECK(false,
-                "selective_scan_cuda.fwd/bwd (dense Mamba scan) is not part of this build; "
-                "the event path uses fwd_flat_ch/bwd_flat_ch");
-    return {};
+// ------------------------------------------------------------- dense S6 ----
+// selective_scan_cuda.fwd / .bwd (reference csrc/selective_scan/selective_scan.cpp:
+// 403-497 and 499-669): same arguments, checks, messages and outputs, real
+// weights (complex A is rejected with a clear message).
+struct S6In {
+    bool varB, varC;
+    int64_t batch, dim, L, N, groups;
+    Tensor Bc, Cc;
+};
+
+S6In s6_check(const Tensor& u, const Tensor& delta, const Tensor& A, const Tensor& B, const Tensor& C,
+              const optional<Tensor>& D_, const optional<Tensor>& delta_bias_) {
+    auto input_type = u.scalar_type();
+    auto weight_type = A.scalar_type();
+    TORCH_CHECK(input_type == at::ScalarType::Float || input_type == at::ScalarType::Half ||
+                input_type == at::ScalarType::BFloat16);
+    TORCH_CHECK(weight_type == at::ScalarType::Float || weight_type == at::ScalarType::ComplexFloat);
+    TORCH_CHECK(weight_type == at::ScalarType::Float,
+                "selective_scan: complex weights are not supported by this build");
+    S6In s;
+    s.varB = B.dim() >= 3;
+    s.varC = C.dim() >= 3;
+    TORCH_CHECK(delta.scalar_type() == input_type);
+    TORCH_CHECK(B.scalar_type() == (!s.varB ? weight_type : input_type));
+    TORCH_CHECK(C.scalar_type() == (!s.varC ? weight_type : input_type));
+    TORCH_CHECK(u.is_cuda());
+    TORCH_CHECK(delta.is_cuda());
+    TORCH_CHECK(A.is_cuda());
+    TORCH_CHECK(B.is_cuda());
+    TORCH_CHECK(C.is_cuda());
+    TORCH_CHECK(u.stride(-1) == 1 || u.size(-1) == 1);
+    TORCH_CHECK(delta.stride(-1) == 1 || delta.size(-1) == 1);
+    TORCH_CHECK(u.dim() == 3, "u must have shape (batch, dim, seqlen)");
+    s.batch = u.size(0);
+    s.dim = u.size(1);
+    s.L = u.size(2);
+    s.N = A.size(1);
+    s.groups = s.varB ? B.size(1) : 1;
+    TORCH_CHECK(s.N <= 256, "selective_scan only supports state dimension <= 256");
+    TORCH_CHECK(delta.sizes() == u.sizes(), "delta must have shape (batch, dim, seqlen)");
+    TORCH_CHECK(A.dim() == 2 && A.size(0) == s.dim, "A must have shape (dim, dstate)");
+    auto check_bc = [&](const Tensor& X, bool var, const char* name) {
+        if (!var) {
+            TORCH_CHECK(X.dim() == 2 && X.size(0) == s.dim && X.size(1) == s.N, name,
+                        " must have shape (dim, dstate)");
+        } else {
+            TORCH_CHECK(X.dim() == 4 && X.size(0) == s.batch && X.size(1) == s.groups && X.size(2) == s.N &&
+                            X.size(3) == s.L,
+                        name, " must have shape (batch, n_groups, dstate, seqlen)");
+            TORCH_CHECK(X.stride(-1) == 1 || X.size(-1) == 1);
+        }
+    };
+    check_bc(B, s.varB, "B");
+    check_bc(C, s.varC, "C");
+    TORCH_CHECK(!(s.varB || s.varC) || s.dim % s.groups == 0, "dim must be a multiple of n_groups");
+    if (D_.has_value()) {
+        auto D = D_.value();
+        TORCH_CHECK(D.scalar_type() == at::ScalarType::Float);
+        TORCH_CHECK(D.is_cuda());
+        TORCH_CHECK(D.stride(-1) == 1 || D.size(-1) == 1);
+        TORCH_CHECK(D.dim() == 1 && D.size(0) == s.dim, "D must have shape (dim,)");
+    }
+    if (delta_bias_.has_value()) {
+        auto delta_bias = delta_bias_.value();
+        TORCH_CHECK(delta_bias.scalar_type() == at::ScalarType::Float);
+        TORCH_CHECK(delta_bias.is_cuda());
+        TORCH_CHECK(delta_bias.stride(-1) == 1 || delta_bias.size(-1) == 1);
+        TORCH_CHECK(delta_bias.dim() == 1 && delta_bias.size(0) == s.dim, "delta_bias must have shape (dim,)");
+    }
+    s.Bc = s.varB ? B.contiguous() : B;
+    s.Cc = s.varC ? C.contiguous() : C;
+    return s;
+}
+
+bcm_s6_args s6_args(const S6In& s, const Tensor& u, const Tensor& delta, const Tensor& A,
+                    const optional<Tensor>& D_, const optional<Tensor>& delta_bias_, bool delta_softplus) {
+    bcm_s6_args a{};
+    a.batch = s.batch; a.dim = s.dim; a.seqlen = s.L; a.dstate = s.N; a.n_groups = s.groups;
+    a.dtype = to_bcm(u.scalar_type(), "selective_scan");
+    a.is_variable_B = s.varB; a.is_variable_C = s.varC; a.delta_softplus = delta_softplus;
+    a.u = u.data_ptr(); a.u_stride_b = u.stride(0); a.u_stride_d = u.stride(1);
+    a.delta = delta.data_ptr(); a.delta_stride_b = delta.stride(0); a.delta_stride_d = delta.stride(1);
+    a.A = A.data_ptr<float>(); a.A_stride_d = A.stride(0); a.A_stride_n = A.stride(1);
+    a.B = s.Bc.data_ptr(); a.C = s.Cc.data_ptr();
+    if (!s.varB) { a.B_stride_d = s.Bc.stride(0); a.B_stride_n = s.Bc.stride(1); }
+    if (!s.varC) { a.C_stride_d = s.Cc.stride(0); a.C_stride_n = s.Cc.stride(1); }
+    a.D = D_.has_value() ? D_.value().data_ptr<float>() : nullptr;
+    a.delta_bias = delta_bias_.has_value() ? delta_bias_.value().data_ptr<float>() : nullptr;
+    return a;
+}
+
+std::vector<Tensor> selective_scan_fwd(const Tensor& u, const Tensor& delta, const Tensor& A, const Tensor& B,
+                                       const Tensor& C, const optional<Tensor>& D_, const optional<Tensor>& z_,
+                                       const optional<Tensor>& delta_bias_, bool delta_softplus) {
+    S6In s = s6_check(u, delta, A, B, C, D_, delta_bias_);
+    Tensor z, out_z;
+    const bool has_z = z_.has_value();
+    if (has_z) {
+        z = z_.value();
+        TORCH_CHECK(z.scalar_type() == u.scalar_type());
+        TORCH_CHECK(z.is_cuda());
+        TORCH_CHECK(z.stride(-1) == 1 || z.size(-1) == 1);
+        TORCH_CHECK(z.sizes() == u.sizes(), "z must have shape (batch, dim, seqlen)");
+        z = z.contiguous();
+        out_z = torch::empty(u.sizes(), z.options());
+    }
+    const int64_t n_chunks = (s.L + 2048 - 1) / 2048;
+    Tensor out = torch::empty(u.sizes(), delta.options());
+    Tensor x = torch::empty({s.batch, s.dim, n_chunks, s.N * 2}, u.options().dtype(A.scalar_type()));
+    c10::cuda::CUDAGuard device_guard(u.device());
+    bcm_s6_args a = s6_args(s, u, delta, A, D_, delta_bias_, delta_softplus);
+    a.z = has_z ? z.data_ptr() : nullptr;
+    a.out = out.data_ptr();
+    a.out_z = has_z ? out_z.data_ptr() : nullptr;
+    a.x = x.data_ptr<float>();
+    check_status(bcm_s6_fwd(&a, cur_stream()), "selective_scan_fwd");
+    std::vector<Tensor> result = {out, x};
+    if (has_z) result.push_back(out_z);
+    return result;
+}
+
+std::vector<Tensor> selective_scan_bwd(const Tensor& u, const Tensor& delta, const Tensor& A, const Tensor& B,
+                                       const Tensor& C, const optional<Tensor>& D_, const optional<Tensor>& z_,
+                                       const optional<Tensor>& delta_bias_, const Tensor& dout,
+                                       const optional<Tensor>& x_, const optional<Tensor>& out_,
+                                       optional<Tensor> dz_, bool delta_softplus, bool recompute_out_z) {
+    S6In s = s6_check(u, delta, A, B, C, D_, delta_bias_);
+    TORCH_CHECK(dout.scalar_type() == u.scalar_type());
+    TORCH_CHECK(dout.is_cuda());
+    TORCH_CHECK(dout.stride(-1) == 1 || dout.size(-1) == 1);
+    TORCH_CHECK(dout.sizes() == u.sizes(), "dout must have shape (batch, dim, seqlen)");
+    Tensor z, out, dz, out_z;
+    const bool has_z = z_.has_value();
+    if (has_z) {
+        z = z_.value();
+        TORCH_CHECK(z.scalar_type() == u.scalar_type());
+        TORCH_CHECK(z.is_cuda());
+        TORCH_CHECK(z.stride(-1) == 1 || z.size(-1) == 1);
+        TORCH_CHECK(z.sizes() == u.sizes(), "z must have shape (batch, dim, seqlen)");
+        TORCH_CHECK(out_.has_value());
+        out = out_.value();
+        TORCH_CHECK(out.scalar_type() == u.scalar_type());
+        TORCH_CHECK(out.is_cuda());
+        TORCH_CHECK(out.stride(-1) == 1 || out.size(-1) == 1);
+        TORCH_CHECK(out.sizes() == u.sizes(), "out must have shape (batch, dim, seqlen)");
+        z = z.contiguous();
+        out = out.contiguous();
+        if (dz_.has_value()) {
+            dz = dz_.value();
+            TORCH_CHECK(dz.scalar_type() == u.scalar_type());
+            TORCH_CHECK(dz.is_cuda());
+            TORCH_CHECK(dz.stride(-1) == 1 || dz.size(-1) == 1);
+            TORCH_CHECK(dz.sizes() == u.sizes(), "dz must have shape (batch, dim, seqlen)");
+            TORCH_CHECK(dz.is_contiguous(), "dz must be contiguous");
+        } else {
+            dz = torch::empty(u.sizes(), z.options());
+        }
+        if (recompute_out_z) out_z = torch::empty(u.sizes(), out.options());
+    }
+    const int64_t n_chunks = (s.L + 2048 - 1) / 2048;
+    if (n_chunks > 1) { TORCH_CHECK(x_.has_value()); }
+    if (x_.has_value()) {
+        auto x = x_.value();
+        TORCH_CHECK(x.scalar_type() == A.scalar_type());
+        TORCH_CHECK(x.is_cuda());
+        TORCH_CHECK(x.is_contiguous());
+        TORCH_CHECK(x.dim() == 4 && x.size(0) == s.batch && x.size(1) == s.dim && x.size(2) == n_chunks &&
+                        x.size(3) == 2 * s.N,
+                    "x must have shape (batch, dim, n_chunks, 2 * dstate)");
+    }
+    Tensor doutc = dout.contiguous();
+    Tensor du = torch::empty(u.sizes(), u.options());
+    Tensor ddelta = torch::empty(u.sizes(), delta.options());
+    Tensor dA = torch::zeros_like(A);
+    Tensor dB = !s.varB ? torch::zeros_like(B) : torch::zeros_like(B, B.options().dtype(torch::kFloat32));
+    Tensor dC = !s.varC ? torch::zeros_like(C) : torch::zeros_like(C, C.options().dtype(torch::kFloat32));
+    Tensor dD, ddelta_bias;
+    if (D_.has_value()) dD = torch::zeros_like(D_.value());
+    if (delta_bias_.has_value()) ddelta_bias = torch::zeros_like(delta_bias_.value());
+    TORCH_CHECK(dA.is_contiguous() && dB.is_contiguous() && dC.is_contiguous(),
+                "selective_scan_bwd: A, B and C must be contiguous");
+    c10::cuda::CUDAGuard device_guard(u.device());
+    bcm_s6_args a = s6_args(s, u, delta, A, D_, delta_bias_, delta_softplus);
+    a.z = has_z ? z.data_ptr() : nullptr;
+    a.dout = doutc.data_ptr();
+    a.out_fwd = has_z ? out.data_ptr() : nullptr;
+    a.du = du.data_ptr();
+    a.ddelta = ddelta.data_ptr();
+    a.dA = dA.data_ptr<float>();
+    a.dB = dB.data_ptr<float>();
+    a.dC = dC.data_ptr<float>();
+    a.dD = D_.has_value() ? dD.data_ptr<float>() : nullptr;
+    a.ddelta_bias = delta_bias_.has_value() ? ddelta_bias.data_ptr<float>() : nullptr;
+    a.dz = has_z ? dz.data_ptr() : nullptr;
+    a.out_z = (has_z && recompute_out_z) ? out_z.data_ptr() : nullptr;
+    Tensor ws = workspace((int64_t)bcm_s6_bwd_workspace_bytes(&a), u.device());
+    a.workspace = ws.data_ptr();
+    a.workspace_bytes = (size_t)ws.numel();
+    check_status(bcm_s6_bwd(&a, cur_stream()), "selective_scan_bwd");
+    std::vector<Tensor> result = {du, ddelta, dA, dB.to(B.dtype()), dC.to(C.dtype()), dD, ddelta_bias};
+    if (has_z) result.push_back(dz);
+    if (recompute_out_z) result.push_back(out_z);
+    return result;
 }
 
 // ---------------------------------------------------------------- restore ----
@@ -972,8 +1170,8 @@ Tensor restore_dense_bwd_bitmap(const Tensor& dout, const Tensor& time_steps, co
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.attr("abi_version") = bcm_abi_version();
     // selective_scan_cuda
-    m.def("fwd", &dense_scan_unavailable, "dense Mamba selective scan (not built)");
-    m.def("bwd", &dense_scan_unavailable, "dense Mamba selective scan (not built)");
+    m.def("fwd", &selective_scan_fwd, "dense selective scan forward");
+    m.def("bwd", &selective_scan_bwd, "dense selective scan backward");
     m.def("fwd_flat_ch", &selective_scan_fwd_flat_ch, py::arg("u_flat"), py::arg("k_flat"),
           py::arg("cu_seqlens"), py::arg("max_seqlen"), py::arg("dt_idle"), py::arg("dt_active"),
           py::arg("A"), py::arg("B"), py::arg("C"), py::arg("D") = py::none(),

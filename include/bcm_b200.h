@@ -468,6 +468,56 @@ BCM_API bcm_status bcm_event_decode_step(const void* x, const void* spikes, bcm_
                                  float* eta, int32_t* counters, float* held,
                                  void* y, cudaStream_t stream);
 
+/* -------------------------------------------------------------------------
+ * Dense selective scan (Mamba's S6) — replaces selective_scan_cuda.fwd / .bwd
+ * (reference csrc/selective_scan/selective_scan.cpp:403-669, kernels
+ * selective_scan_fwd_kernel.cuh:84-326 and selective_scan_bwd_kernel.cuh:
+ * 31-500), real weights.
+ *
+ * u, delta, z, out, out_z, dout, du, ddelta, dz [batch, dim, seqlen] in dtype
+ * (u and delta with the batch / dim strides below and unit position stride,
+ * the others contiguous); A [dim, dstate] fp32 (strides);
+ * B, C either fixed [dim, dstate] fp32 (strides) or variable
+ * [batch, n_groups, dstate, seqlen] in dtype (contiguous), channel d reading
+ * group d / (dim / n_groups); D, delta_bias [dim] fp32 or NULL.
+ * delta' = delta + delta_bias, then softplus (log1p(exp), identity above 20)
+ * when delta_softplus; h_s = exp2(clamp(delta'*A_s*log2(e), +-126)) * h_s +
+ * (B variable ? B_s : 1) * delta' * u; y = sum_s C'_s * h_s + D * u with
+ * C'_s = (C variable ? C_s : C_s) * (B fixed ? B_s : 1); out_z = y * silu(z).
+ * x [batch, dim, ceil(seqlen/2048), 2*dstate] fp32: after each 2048-position
+ * chunk, (product of the decays since position 0, h_s) per state.
+ * Backward: du, ddelta in dtype; dA [dim, dstate], dB / dC (fixed: [dim,
+ * dstate]; variable: [batch, n_groups, dstate, seqlen]), dD, ddelta_bias
+ * fp32, all ACCUMULATED into (the caller zeroes them); dz when z is given
+ * (needs `out`, the ungated forward output), out_z recomputed when non-NULL.
+ * The backward re-runs the recurrence from position 0 (x is not read) and
+ * needs bcm_s6_bwd_workspace_bytes of workspace.
+ * ------------------------------------------------------------------------- */
+typedef struct bcm_s6_args {
+    int64_t batch, dim, seqlen, dstate, n_groups;
+    bcm_dtype dtype;
+    int is_variable_B, is_variable_C, delta_softplus;
+    const void* u; int64_t u_stride_b, u_stride_d;
+    const void* delta; int64_t delta_stride_b, delta_stride_d;
+    const float* A; int64_t A_stride_d, A_stride_n;
+    const void* B; int64_t B_stride_d, B_stride_n;   /* strides: fixed B only */
+    const void* C; int64_t C_stride_d, C_stride_n;   /* strides: fixed C only */
+    const float* D;
+    const float* delta_bias;
+    const void* z;
+    /* forward outputs */
+    void* out; void* out_z; float* x;
+    /* backward */
+    const void* dout; const void* out_fwd;
+    void* du; void* ddelta; float* dA; float* dB; float* dC; float* dD; float* ddelta_bias;
+    void* dz;
+    void* workspace; size_t workspace_bytes;
+} bcm_s6_args;
+
+BCM_API bcm_status bcm_s6_fwd(const bcm_s6_args* args, cudaStream_t stream);
+BCM_API size_t bcm_s6_bwd_workspace_bytes(const bcm_s6_args* args);
+BCM_API bcm_status bcm_s6_bwd(const bcm_s6_args* args, cudaStream_t stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

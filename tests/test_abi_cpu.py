@@ -84,8 +84,19 @@ def test_dropin_module_names():
     assert hasattr(selective_scan_cuda, "fwd_flat_ch")
 
 
-def test_dense_scan_is_explicitly_unavailable():
+def test_dense_scan_entry_points_and_cpu_errors():
+    """selective_scan_cuda.fwd/bwd take the reference's arguments and check
+    them before any kernel runs (CPU tensors are rejected)."""
+    import torch
+
     import bc_mamba_b200
 
-    with pytest.raises(RuntimeError, match="not part of this build"):
-        bc_mamba_b200.load_ops().fwd()
+    ops = bc_mamba_b200.load_ops()
+    u = torch.zeros(1, 2, 4)
+    A = -torch.ones(2, 4)
+    with pytest.raises(RuntimeError):
+        ops.fwd(u, u, A, A, A, None, None, None, False)
+    with pytest.raises(RuntimeError, match="complex weights"):
+        ops.fwd(u, u, A.to(torch.complex64), A.to(torch.complex64), A.to(torch.complex64), None, None, None, False)
+    with pytest.raises(RuntimeError):
+        ops.bwd(u, u, A, A, A, None, None, None, u, None, None, None, False, False)
