@@ -244,14 +244,24 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
     const int nch = (n + kChunkX - 1) / kChunkX;
     const int nch_max = warp_max(nch);
 
-    float cc[G], ccA[G];
+    // states advance in fp32x2 pairs (state 2h in .x, 2h+1 in .y): the same
+    // fp32 operations, in the same order, as one state at a time
+    static_assert(G % 2 == 0, "state pairs");
+    constexpr int H = G / 2;
+    float2 cc[H], ccA[H];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const int s = q * G + g;
-        const bool o = s < N;
-        const float Ar = o ? a.A[d * a.A_sd + s * a.A_sn] : 0.f;
-        cc[g] = o ? a.B[d * N + s] * a.C[d * N + s] : 0.f;
-        ccA[g] = cc[g] * Ar;
+    for (int h = 0; h < H; ++h) {
+        float c2[2], a2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int s = q * G + 2 * h + e;
+            const bool o = s < N;
+            const float Ar = o ? a.A[d * a.A_sd + s * a.A_sn] : 0.f;
+            c2[e] = o ? a.B[d * N + s] * a.C[d * N + s] : 0.f;
+            a2[e] = c2[e] * Ar;
+        }
+        cc[h] = make_float2(c2[0], c2[1]);
+        ccA[h] = make_float2(a2[0], a2[1]);
     }
     const float dti = a.dt_idle[d], dta = a.dt_active[d];
     const float Dv = a.D ? a.D[d] : 0.f;
@@ -282,12 +292,15 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
         }
     };
 
-    float gam[G], anx[G], SA[G], SB[G], QE[G], tA[G], tB[G], tQ[G];
+    float2 gam[H], anx[H], SA[H], SB[H], QE[H];
+    float tA[G], tB[G], tQ[G];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        gam[g] = 0.f; anx[g] = 1.f;
-        tA[g] = tB[g] = tQ[g] = 0.f;
+    for (int h = 0; h < H; ++h) {
+        gam[h] = make_float2(0.f, 0.f);
+        anx[h] = make_float2(1.f, 1.f);
     }
+#pragma unroll
+    for (int g = 0; g < G; ++g) tA[g] = tB[g] = tQ[g] = 0.f;
     float t_ddi = 0.f, t_dda = 0.f, t_dD = 0.f;
 
     for (int c = nch_max - 1; c >= 0; --c) {
@@ -302,7 +315,7 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
         }
         __syncwarp();
 #pragma unroll
-        for (int g = 0; g < G; ++g) SA[g] = SB[g] = QE[g] = 0.f;
+        for (int h = 0; h < H; ++h) SA[h] = SB[h] = QE[h] = make_float2(0.f, 0.f);
         float c_ddi = 0.f, c_dda = 0.f, c_dD = 0.f;
         float* const ck = fwd_ck ? ck0 + (int64_t)(cs >> 3) * NP : ck0;
 
@@ -398,15 +411,16 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
 #pragma unroll 1
                     for (int t = kR3 / TB - 1; t >= 0; --t) {
                         const int i0 = t * TB;
-                        float et[G], e0[G];
+                        float2 et[H], e0[H];
 #pragma unroll
-                        for (int g = 0; g < G; ++g) et[g] = e0[g] = eN[g];
+                        for (int h = 0; h < H; ++h) et[h] = e0[h] = make_float2(eN[2 * h], eN[2 * h + 1]);
                         if (t > 0) {   // next (earlier) tile's checkpoint
                             const int jt = jb + i0 - TB;
                             ck_load<G>(ck + (int64_t)(jt / TB) * NP, jt < len, eN);
                         }
                         // forward recompute of the tile
-                        float eti[TB][G], te[TB], tg[TB], ta[TB];
+                        float2 eti[TB][H];
+                        float te[TB], tg[TB], ta[TB];
 #pragma unroll
                         for (int ii = 0; ii < TB; ++ii) {
                             const int i = i0 + ii;
@@ -417,15 +431,16 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
                             float dec[G];
                             decays(exact_c, kv, jb + i < len, dl, dec);
                             const float w = dl * uv * uv;
-                            float s0 = 0.f, s1 = 0.f;
+                            const float2 w2 = make_float2(w, w), q2 = make_float2(qv, qv);
+                            float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
-                            for (int g = 0; g < G; ++g) {
-                                et[g] = fmaf(dec[g], et[g], w);
-                                eti[ii][g] = et[g];
-                                if (g & 1) s1 = fmaf(cc[g], et[g], s1); else s0 = fmaf(cc[g], et[g], s0);
-                                QE[g] = fmaf(qv, et[g], QE[g]);
+                            for (int h = 0; h < H; ++h) {
+                                et[h] = __ffma2_rn(make_float2(dec[2 * h], dec[2 * h + 1]), et[h], w2);
+                                eti[ii][h] = et[h];
+                                s2 = __ffma2_rn(cc[h], et[h], s2);
+                                QE[h] = __ffma2_rn(q2, et[h], QE[h]);
                             }
-                            te[ii] = s0 + s1;
+                            te[ii] = s2.x + s2.y;
                         }
                         // reverse over the tile: per-lane partial sums
 #pragma unroll
@@ -438,27 +453,24 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
                             float dec[G];
                             decays(exact_c, kv, jb + i < len, dl, dec);
                             const float w = dl * uv * uv;
-                            float tg0 = 0.f, tg1 = 0.f, ta0 = 0.f, ta1 = 0.f;
+                            const float2 w2 = make_float2(w, w), q2 = make_float2(qv, qv), dl2 = make_float2(dl, dl);
+                            float2 tg2 = make_float2(0.f, 0.f), ta2 = make_float2(0.f, 0.f);
 #pragma unroll
-                            for (int g = 0; g < G; ++g) {
-                                gam[g] = fmaf(anx[g], gam[g], qv);
+                            for (int h = 0; h < H; ++h) {
+                                const float2 dc = make_float2(dec[2 * h], dec[2 * h + 1]);
+                                gam[h] = __ffma2_rn(anx[h], gam[h], q2);
                                 // gam * (eta_i - w_i), formed as gam * a_i * eta_{i-1}:
                                 // no cancellation when the state has decayed
-                                const float ep = (ii > 0) ? eti[ii > 0 ? ii - 1 : 0][g] : e0[g];
-                                const float pr = gam[g] * (dec[g] * ep);
-                                SB[g] = fmaf(gam[g], w, SB[g]);
-                                SA[g] = fmaf(pr, dl, SA[g]);
-                                if (g & 1) {
-                                    ta1 = fmaf(ccA[g], pr, ta1);
-                                    tg1 = fmaf(cc[g], gam[g], tg1);
-                                } else {
-                                    ta0 = fmaf(ccA[g], pr, ta0);
-                                    tg0 = fmaf(cc[g], gam[g], tg0);
-                                }
-                                anx[g] = dec[g];
+                                const float2 ep = (ii > 0) ? eti[ii > 0 ? ii - 1 : 0][h] : e0[h];
+                                const float2 pr = __fmul2_rn(gam[h], __fmul2_rn(dc, ep));
+                                SB[h] = __ffma2_rn(gam[h], w2, SB[h]);
+                                SA[h] = __ffma2_rn(pr, dl2, SA[h]);
+                                ta2 = __ffma2_rn(ccA[h], pr, ta2);
+                                tg2 = __ffma2_rn(cc[h], gam[h], tg2);
+                                anx[h] = dc;
                             }
-                            tg[ii] = tg0 + tg1;
-                            ta[ii] = ta0 + ta1;
+                            tg[ii] = tg2.x + tg2.y;
+                            ta[ii] = ta2.x + ta2.y;
                         }
                         group_transpose_sum<LPC, TB>(te, q);
                         group_transpose_sum<LPC, TB>(tg, q);
@@ -493,10 +505,13 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
             }
         }
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            tA[g] += SA[g];
-            tB[g] += SB[g];
-            tQ[g] += QE[g];
+        for (int h = 0; h < H; ++h) {
+            tA[2 * h] += SA[h].x;
+            tA[2 * h + 1] += SA[h].y;
+            tB[2 * h] += SB[h].x;
+            tB[2 * h + 1] += SB[h].y;
+            tQ[2 * h] += QE[h].x;
+            tQ[2 * h + 1] += QE[h].y;
         }
         t_ddi += c_ddi;
         t_dda += c_dda;
@@ -511,7 +526,7 @@ dw_bwd_v3(ScanArgs a, int bgroups) {
     for (int g = 0; g < G; ++g) {
         const int s = q * G + g;
         if (s < N) {
-            part[s] = cc[g] * tA[g];
+            part[s] = ((g & 1) ? cc[g / 2].y : cc[g / 2].x) * tA[g];
             part[NP + s] = a.C[d * N + s] * tB[g];
             part[2 * NP + s] = a.B[d * N + s] * tQ[g];
         }
