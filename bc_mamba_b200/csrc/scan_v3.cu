@@ -659,9 +659,12 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
         decaying = decaying && A2[g] <= 0.f;
     }
     // phase B needs cc of every state
-    float ccall[NP];
+    // as pairs (state 2h in .x, 2h+1 in .y) for the packed output sum
+    float2 ccall[NP / 2];
 #pragma unroll
-    for (int st = 0; st < NP; ++st) ccall[st] = st < N ? a.B[d * N + st] * a.C[d * N + st] : 0.f;
+    for (int h = 0; h < NP / 2; ++h)
+        ccall[h] = make_float2(2 * h < N ? a.B[d * N + 2 * h] * a.C[d * N + 2 * h] : 0.f,
+                               2 * h + 1 < N ? a.B[d * N + 2 * h + 1] * a.C[d * N + 2 * h + 1] : 0.f);
     const float dti = a.dt_idle[d], dta = a.dt_active[d];
     const float Dv = a.D ? a.D[d] : 0.f;
     decaying = decaying && dti >= 0.f && dta >= 0.f;
@@ -730,8 +733,18 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
                 tab_row4<G>(tab, __float_as_int(wr1.y), s0, dn);
                 const float w1 = wr1.x;
                 wr1 = s_wr[i2 * P + grp];
+                if constexpr (G % 2 == 0) {   // state pairs in packed fp32x2 FMAs
 #pragma unroll
-                for (int g = 0; g < G; ++g) eta[g] = fmaf(dec[g], eta[g], w0);
+                    for (int h = 0; h < G / 2; ++h) {
+                        const float2 r = __ffma2_rn(make_float2(dec[2 * h], dec[2 * h + 1]),
+                                                    make_float2(eta[2 * h], eta[2 * h + 1]), make_float2(w0, w0));
+                        eta[2 * h] = r.x;
+                        eta[2 * h + 1] = r.y;
+                    }
+                } else {
+#pragma unroll
+                    for (int g = 0; g < G; ++g) eta[g] = fmaf(dec[g], eta[g], w0);
+                }
                 sts_vec<G>(erow + i * EP, eta);
                 if (ckb != nullptr && (i & 7) == 7 && j0 + i + 1 < n)
                     sts_vec<G>(ckb + (int64_t)((j0 + i + 1) >> 3) * NP, eta);
@@ -798,16 +811,15 @@ dw_fwd_v4(ScanArgs a, int blocks_per_d) {
             const float* ev = s_eta + lane * EP;
 #pragma unroll 2
             for (int c = 0; c < CPW; ++c) {
-                float s4[4] = {0.f, 0.f, 0.f, 0.f};
+                // four running sums (states st%4 = 0..3) as two packed pairs
+                float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int st = 0; st < NP; st += 4) {
                     const float4 e4 = *reinterpret_cast<const float4*>(ev + c * NP + st);
-                    s4[0] = fmaf(ccall[st], e4.x, s4[0]);
-                    s4[1] = fmaf(ccall[st + 1], e4.y, s4[1]);
-                    s4[2] = fmaf(ccall[st + 2], e4.z, s4[2]);
-                    s4[3] = fmaf(ccall[st + 3], e4.w, s4[3]);
+                    s01 = __ffma2_rn(ccall[st / 2], make_float2(e4.x, e4.y), s01);
+                    s23 = __ffma2_rn(ccall[st / 2 + 1], make_float2(e4.z, e4.w), s23);
                 }
-                const float acc = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+                const float acc = (s01.x + s01.y) + (s23.x + s23.y);
                 const float uv = s_u[lane * P + c];
                 const float y = fmaf(Dv, uv, uv * acc);
                 if (j < s_n[c]) {
