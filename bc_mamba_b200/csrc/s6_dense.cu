@@ -52,11 +52,12 @@ __device__ __forceinline__ float s6_decay(float dl, float A2) {
 // Shared memory of one warp: per channel rows of delta', delta'*u, u, a
 // fourth row (forward: output; backward: gated dout) and a fifth (backward:
 // the softplus derivative), then the B and C tiles [CPW][N][kP6] when
-// variable.
+// variable and (backward) tiles of the same shape for their gradients.
 template <int CPW>
 __host__ __device__ constexpr int s6_rows_floats() { return 5 * CPW * kP6; }
-__host__ __device__ inline int s6_warp_floats(int cpw, int N, bool varB, bool varC) {
-    return (5 * cpw * kP6 + (varB ? cpw * N * kP6 : 0) + (varC ? cpw * N * kP6 : 0) + 3) / 4 * 4;
+__host__ __device__ inline int s6_warp_floats(int cpw, int N, bool varB, bool varC, bool bwd = false) {
+    const int tiles = (varB ? 1 : 0) + (varC ? 1 : 0);
+    return (5 * cpw * kP6 + (bwd ? 2 : 1) * tiles * cpw * N * kP6 + 3) / 4 * 4;
 }
 
 // Stage positions t0 .. t0+31 of the warp's channels (lane = position).
@@ -264,7 +265,7 @@ s6_bwd_kernel(S6 p) {
     const int lane = threadIdx.x & 31;
     const int64_t warp_id = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (warp_id * CPW >= (int64_t)p.batch * p.dim) return;   // warp-uniform; no block barrier below
-    float* sw = sm6 + (threadIdx.x >> 5) * s6_warp_floats(CPW, p.N, p.varB, p.varC);
+    float* sw = sm6 + (threadIdx.x >> 5) * s6_warp_floats(CPW, p.N, p.varB, p.varC, true);
     int64_t chb[CPW];
     int chd[CPW];
     s6_channels<CPW>(p, warp_id, chb, chd);
@@ -276,8 +277,11 @@ s6_bwd_kernel(S6 p) {
     const int64_t ch = b * p.dim + dd;
     const int n_tiles = (p.L + kTile6 - 1) / kTile6;
     float* ckc = p.ck + ch * (int64_t)n_tiles * NP + q * G;
-    const int grp = dd / p.hpg;
-    const int64_t bc_row0 = ((b * p.groups + grp) * (int64_t)p.N) * p.L;   // variable B/C [.., s, t]
+    // per-position gradients of variable B / C for the batch, [CPW][N][kP6]:
+    // summed over the channels of one (batch row, group) and added to global
+    // memory once per batch with position-coalesced atomics
+    float* s_gB = sw + 5 * CPW * kP6 + ((p.varB ? 1 : 0) + (p.varC ? 1 : 0)) * CPW * p.N * kP6;
+    float* s_gC = s_gB + (p.varB ? CPW * p.N * kP6 : 0);
 
     // Cx: fixed C (1 when variable), Bw: fixed B (1 when variable), Cf = Cx*Bw
     // (0 for padding states): the output weight without the variable C factor
@@ -371,14 +375,13 @@ s6_bwd_kernel(S6 p) {
                         aA[g] = fmaf(pr, dl, aA[g]);
                         g0 = fmaf(pr, A2[g], g0);                 // times ln 2 below
                         u0 = fmaf(dh[g], bv, u0);                 // times u (ddelta') and delta' (du)
-                        const bool sv = live_ch && s < p.N && t < p.L;
                         if (p.varB) {
-                            if (sv) atomicAdd(p.dB + bc_row0 + (int64_t)s * p.L + t, dh[g] * dlu);
+                            if (s < p.N) s_gB[(j * p.N + s) * kP6 + i] = dh[g] * dlu;
                         } else {
                             aB[g] = fmaf(dy * cv * Cx[g], ht, aB[g]);
                         }
                         if (p.varC) {
-                            if (sv) atomicAdd(p.dC + bc_row0 + (int64_t)s * p.L + t, dy * ht * Bw[g]);
+                            if (s < p.N) s_gC[(j * p.N + s) * kP6 + i] = dy * ht * Bw[g];
                         } else {
                             aC[g] = fmaf(dy * Bw[g], ht, aC[g]);
                         }
@@ -428,6 +431,31 @@ s6_bwd_kernel(S6 p) {
                     const int64_t e = (chb[jj] * p.dim + chd[jj]) * (int64_t)p.L + t;
                     static_cast<T*>(p.du)[e] = from_f32<T>(s_dl[jj * kP6 + lane]);
                     static_cast<T*>(p.ddelta)[e] = from_f32<T>(s_dlu[jj * kP6 + lane]);
+                }
+            }
+            // variable dB / dC: lane = position; the warp's channels of one
+            // (batch row, group) summed first, then one coalesced atomic row
+            // per state.  Every slot read here was written this batch: the
+            // positions of tiles past the sequence end are not read.
+            if ((p.varB || p.varC) && t < p.L) {
+                for (int s = 0; s < p.N; ++s) {
+                    float accB = 0.f, accC = 0.f;
+#pragma unroll
+                    for (int jj = 0; jj < CPW; ++jj) {
+                        if (chd[jj] < 0) break;
+                        if (p.varB) accB += s_gB[(jj * p.N + s) * kP6 + lane];
+                        if (p.varC) accC += s_gC[(jj * p.N + s) * kP6 + lane];
+                        const bool last = jj + 1 == CPW || chd[jj + 1 < CPW ? jj + 1 : jj] < 0 ||
+                                          chb[jj + 1 < CPW ? jj + 1 : jj] != chb[jj] ||
+                                          chd[jj + 1 < CPW ? jj + 1 : jj] / p.hpg != chd[jj] / p.hpg;
+                        if (last) {
+                            const int64_t row =
+                                ((chb[jj] * p.groups + chd[jj] / p.hpg) * (int64_t)p.N + s) * p.L + t;
+                            if (p.varB) atomicAdd(p.dB + row, accB);
+                            if (p.varC) atomicAdd(p.dC + row, accC);
+                            accB = accC = 0.f;
+                        }
+                    }
                 }
             }
         }
@@ -495,7 +523,7 @@ bcm_status s6_launch_t(const S6& p, bool bwd, cudaStream_t st) {
     const int64_t warps = ((int64_t)p.batch * p.dim + CPW - 1) / CPW;
     const int64_t blocks = (warps + wpb - 1) / wpb;
     BCM_REQUIRE(blocks < (1ll << 31), "selective_scan: too many channels");
-    const size_t smem = (size_t)wpb * s6_warp_floats(CPW, p.N, p.varB, p.varC) * sizeof(float);
+    const size_t smem = (size_t)wpb * s6_warp_floats(CPW, p.N, p.varB, p.varC, bwd) * sizeof(float);
     if (bwd) {
         bcm_status s = s6_smem_optin(s6_bwd_kernel<T, G, LPC>, smem);
         if (s != BCM_OK) return s;
