@@ -50,6 +50,8 @@ ABI_SYMBOLS = (
     "bcm_s6_fwd",
     "bcm_s6_bwd_workspace_bytes",
     "bcm_s6_bwd",
+    "bcm_event_params_fwd",
+    "bcm_event_params_bwd",
 )
 
 _ops = None

@@ -30,7 +30,7 @@ LIB = PKG / "libbcm_b200.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CU_SOURCES = ["abi.cu", "extract.cu", "restore.cu", "scan_fwd.cu", "scan_bwd.cu", "scan_dw.cu", "scan_v3.cu", "scan_seg.cu",
-              "conv_events.cu", "decode.cu", "s6_dense.cu"]
+              "conv_events.cu", "decode.cu", "s6_dense.cu", "param_prep.cu"]
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
     "--expt-relaxed-constexpr", "-I", str(INCLUDE), "-I", str(CSRC),

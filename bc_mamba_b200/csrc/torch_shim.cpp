@@ -1165,6 +1165,69 @@ Tensor restore_dense_bwd_bitmap(const Tensor& dout, const Tensor& time_steps, co
     return dy;
 }
 
+// ------------------------------------------------------- block parameters ----
+// (the messages name the expected shape symbolically: an int64_t value in a
+// TORCH_CHECK message crashed the process with this torch build)
+static void check_param(const Tensor& t, const char* name, int64_t n0, int64_t n1, const char* shape) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32 && t.is_contiguous(), "event_params: ", name,
+                " must be a contiguous float32 CUDA tensor");
+    if (n1 < 0) {
+        TORCH_CHECK(t.dim() == 1 && t.size(0) == n0, "event_params: ", name, " must have shape ", shape);
+    } else {
+        TORCH_CHECK(t.dim() == 2 && t.size(0) == n0 && t.size(1) == n1, "event_params: ", name,
+                    " must have shape ", shape);
+    }
+}
+
+std::vector<Tensor> event_params_fwd(const Tensor& A_log, const Tensor& W_BC, const Tensor& a0, const Tensor& a1,
+                                     double eps) {
+    TORCH_CHECK(A_log.dim() == 2, "event_params: A_log must be 2-D (dim, dstate)");
+    const int64_t dim = A_log.size(0), N = A_log.size(1);
+    check_param(A_log, "A_log", dim, N, "(dim, dstate)");
+    check_param(W_BC, "W_BC", dim, 2 * N, "(dim, 2*dstate)");
+    check_param(a0, "a0", dim, -1, "(dim)");
+    check_param(a1, "a1", dim, -1, "(dim)");
+    c10::cuda::CUDAGuard guard(A_log.device());
+    auto A = torch::empty_like(A_log), W_B = torch::empty_like(A_log), W_C = torch::empty_like(A_log);
+    auto dt_idle = torch::empty_like(a0), dt_active = torch::empty_like(a1);
+    check_status(bcm_event_params_fwd(A_log.data_ptr<float>(), W_BC.data_ptr<float>(), a0.data_ptr<float>(),
+                                      a1.data_ptr<float>(), dim, N, (float)eps, A.data_ptr<float>(),
+                                      W_B.data_ptr<float>(), W_C.data_ptr<float>(), dt_idle.data_ptr<float>(),
+                                      dt_active.data_ptr<float>(), cur_stream()),
+                 "event_params_fwd");
+    return {A, W_B, W_C, dt_idle, dt_active};
+}
+
+// gradients given as None are zero
+std::vector<Tensor> event_params_bwd(const Tensor& A, const Tensor& a0, const Tensor& a1, const optional<Tensor>& dA,
+                                     const optional<Tensor>& dW_B, const optional<Tensor>& dW_C,
+                                     const optional<Tensor>& ddt_idle, const optional<Tensor>& ddt_active) {
+    TORCH_CHECK(A.dim() == 2, "event_params: A must be 2-D (dim, dstate)");
+    const int64_t dim = A.size(0), N = A.size(1);
+    check_param(A, "A", dim, N, "(dim, dstate)");
+    check_param(a0, "a0", dim, -1, "(dim)");
+    check_param(a1, "a1", dim, -1, "(dim)");
+    auto ptr = [&](const optional<Tensor>& t, const char* name, int64_t n1, const char* shape) -> const float* {
+        if (!t.has_value()) return nullptr;
+        check_param(*t, name, dim, n1, shape);
+        return t->data_ptr<float>();
+    };
+    const float* pdA = ptr(dA, "dA", N, "(dim, dstate)");
+    const float* pdB = ptr(dW_B, "dW_B", N, "(dim, dstate)");
+    const float* pdC = ptr(dW_C, "dW_C", N, "(dim, dstate)");
+    const float* pdi = ptr(ddt_idle, "ddt_idle", -1, "(dim)");
+    const float* pda = ptr(ddt_active, "ddt_active", -1, "(dim)");
+    c10::cuda::CUDAGuard guard(A.device());
+    auto dA_log = torch::empty_like(A);
+    auto dW_BC = torch::empty({dim, 2 * N}, A.options());
+    auto da0 = torch::empty_like(a0), da1 = torch::empty_like(a1);
+    check_status(bcm_event_params_bwd(A.data_ptr<float>(), a0.data_ptr<float>(), a1.data_ptr<float>(), pdA, pdB, pdC,
+                                      pdi, pda, dim, N, dA_log.data_ptr<float>(), dW_BC.data_ptr<float>(),
+                                      da0.data_ptr<float>(), da1.data_ptr<float>(), cur_stream()),
+                 "event_params_bwd");
+    return {dA_log, dW_BC, da0, da1};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -1243,4 +1306,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"), py::arg("bitmap") = true,
           "Backward of restore_dense_fwd; returns dy_flat (float32).  bitmap=False runs the "
           "windowed kernel (no workspace) instead of the event-bitmap one (same result up to fp32 rounding)");
+    // block parameter transforms (no reference binding: PyTorch ops in Mamba.forward)
+    m.def("event_params_fwd", &event_params_fwd, py::arg("A_log"), py::arg("W_BC"), py::arg("a0"), py::arg("a1"),
+          py::arg("eps"),
+          "-> [A = -exp(A_log), W_B, W_C (the halves of W_BC), softplus(a0) + eps, softplus(a1) + eps]");
+    m.def("event_params_bwd", &event_params_bwd, py::arg("A"), py::arg("a0"), py::arg("a1"), py::arg("dA"),
+          py::arg("dW_B"), py::arg("dW_C"), py::arg("ddt_idle"), py::arg("ddt_active"),
+          "backward of event_params_fwd (None gradients are zero) -> [dA_log, dW_BC, da0, da1]");
 }

@@ -191,6 +191,34 @@ def restore_dense_fn(y_flat, time_steps_i32, cu_seqlens, dim: int, seqlen: int):
     return RestoreDenseFn.apply(y_flat, time_steps_i32, cu_seqlens, dim, seqlen)
 
 
+class EventParamsFn(torch.autograd.Function):
+    """An event block's parameter transforms in one launch each way
+    (spike_mamba/e_model.py:463 A = -exp(A_log); :475-476 W_B, W_C = the
+    halves of W_BC; :210-230 dt_idle / dt_active = softplus(a0 / a1) + eps):
+    the same values and gradients as those PyTorch ops, with one kernel and
+    one autograd node instead of eight of each."""
+
+    @staticmethod
+    def forward(ctx, A_log, W_BC, a0, a1, eps: float):
+        A, W_B, W_C, dt_idle, dt_active = load_ops().event_params_fwd(A_log, W_BC, a0, a1, float(eps))
+        ctx.save_for_backward(A, a0, a1)
+        ctx.set_materialize_grads(False)   # an output without a gradient reaches the kernel as NULL
+        return A, W_B, W_C, dt_idle, dt_active
+
+    @staticmethod
+    def backward(ctx, dA, dW_B, dW_C, ddt_idle, ddt_active):
+        A, a0, a1 = ctx.saved_tensors
+        c = lambda t: None if t is None else t.contiguous()
+        dA_log, dW_BC, da0, da1 = load_ops().event_params_bwd(A, a0, a1, c(dA), c(dW_B), c(dW_C), c(ddt_idle),
+                                                              c(ddt_active))
+        return dA_log, dW_BC, da0, da1, None
+
+
+def event_params(A_log, W_BC, a0, a1, eps: float = 1e-6):
+    """(A, W_B, W_C, dt_idle, dt_active) of one event block's parameters."""
+    return EventParamsFn.apply(A_log, W_BC, a0, a1, eps)
+
+
 class GatherEventsFn(torch.autograd.Function):
     """u_flat[e] = x_conv[b, d, t] at (channel_ids[e] = b*D + d, time_steps[e])."""
 

@@ -177,11 +177,16 @@ class EventStack:
         the path's (events, max_seqlen))."""
         p = self.params[l]
         N = self.cfg.N
-        A = -torch.exp(p.A_log)
-        W_B = p.W_BC[:, :N].contiguous()
-        W_C = p.W_BC[:, N:].contiguous()
-        dt_idle = F.softplus(p.a0) + 1e-6
-        dt_active = F.softplus(p.a1) + 1e-6
+        if p.A_log.is_cuda and p.A_log.dtype == torch.float32:
+            from .interface import event_params
+
+            A, W_B, W_C, dt_idle, dt_active = event_params(p.A_log, p.W_BC, p.a0, p.a1, 1e-6)
+        else:   # the float64 CPU restatement the tests run
+            A = -torch.exp(p.A_log)
+            W_B = p.W_BC[:, :N].contiguous()
+            W_C = p.W_BC[:, N:].contiguous()
+            dt_idle = F.softplus(p.a0) + 1e-6
+            dt_active = F.softplus(p.a1) + 1e-6
         y_dense, events = self.path(s, x_conv, 0.0, self.cfg.expand, dt_idle, dt_active, A, W_B, W_C, p.D)
         return _Proj.apply(y_dense, p.W_out, offset, self.proj_tf32), events
 

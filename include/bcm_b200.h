@@ -518,6 +518,28 @@ BCM_API bcm_status bcm_s6_fwd(const bcm_s6_args* args, cudaStream_t stream);
 BCM_API size_t bcm_s6_bwd_workspace_bytes(const bcm_s6_args* args);
 BCM_API bcm_status bcm_s6_bwd(const bcm_s6_args* args, cudaStream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * Event-block parameter transforms.  No reference binding: the reference
+ * computes them with PyTorch ops in Mamba.forward (spike_mamba/e_model.py:463
+ * A = -exp(A_log); :475-476 W_B / W_C = the halves of W_BC; :210-230
+ * TwoLevelDelta dt_idle / dt_active = softplus(a0 / a1) + eps), eight small
+ * kernels per direction; here one launch each way.
+ * A_log, A, W_B, W_C, dA, dW_B, dW_C [dim, dstate]; W_BC, dW_BC [dim,
+ * 2*dstate]; a0, a1, dt_*, da0, da1 [dim]; all fp32, contiguous.
+ * softplus: x above 20 passes through (torch.nn.functional.softplus).
+ * Backward: the gradient pointers dA, dW_B, dW_C, ddt_idle, ddt_active may
+ * each be NULL (a zero gradient); every output is written, not accumulated.
+ * ------------------------------------------------------------------------- */
+BCM_API bcm_status bcm_event_params_fwd(const float* A_log, const float* W_BC, const float* a0,
+                                        const float* a1, int64_t dim, int64_t dstate, float eps,
+                                        float* A, float* W_B, float* W_C, float* dt_idle,
+                                        float* dt_active, cudaStream_t stream);
+BCM_API bcm_status bcm_event_params_bwd(const float* A, const float* a0, const float* a1,
+                                        const float* dA, const float* dW_B, const float* dW_C,
+                                        const float* ddt_idle, const float* ddt_active, int64_t dim,
+                                        int64_t dstate, float* dA_log, float* dW_BC, float* da0,
+                                        float* da1, cudaStream_t stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -100,3 +100,18 @@ def test_dense_scan_entry_points_and_cpu_errors():
         ops.fwd(u, u, A.to(torch.complex64), A.to(torch.complex64), A.to(torch.complex64), None, None, None, False)
     with pytest.raises(RuntimeError):
         ops.bwd(u, u, A, A, A, None, None, None, u, None, None, None, False, False)
+
+
+def test_event_params_entry_points_and_cpu_errors():
+    """The fused block-parameter transforms are exported and reject CPU
+    tensors before any kernel runs."""
+    import torch
+
+    import bc_mamba_b200
+
+    ops = bc_mamba_b200.load_ops()
+    A_log, W_BC, a = torch.zeros(4, 8), torch.zeros(4, 16), torch.zeros(4)
+    with pytest.raises(RuntimeError, match="A_log must be a contiguous float32 CUDA tensor"):
+        ops.event_params_fwd(A_log, W_BC, a, a, 1e-6)
+    with pytest.raises(RuntimeError, match="A must be a contiguous float32 CUDA tensor"):
+        ops.event_params_bwd(A_log, a, a, None, None, None, None, None)
