@@ -6,6 +6,8 @@ reference's Python layer so callers switch without edits:
 * ``RestoreDenseFn`` / ``restore_dense_fn``  (spike_mamba/e_model.py:123-161)
 * ``GatherEventsFn`` / ``gather_events``       (spike_mamba/e_model.py:167-193)
 * ``extract_events_1d``                        (spike_mamba/e_model.py:361-409)
+* ``EventParamsFn`` / ``event_params``          (the parameter transforms of
+  Mamba.forward, spike_mamba/e_model.py:210-230, 463, 475-476, in one kernel)
 
 All device work goes through the native shim (``bc_mamba_b200._native``);
 there is no Python or CPU fallback.  ``install_shim()`` puts the drop-in

@@ -131,6 +131,25 @@ STAGE_OPS = {
 # 1, restore fwd 1, restore bwd 1, scan bwd 2, gather bwd 1 (row writer)
 KERNELS_PER_BLOCK = 9
 
+
+def stack_kernels_per_block(cfg, rows: int, sm_count: int) -> int:
+    """Kernels of ours one block of the stack launches per step (forward and
+    backward), from the launch list of the bench workload: parameter
+    transforms 1 + 1, extraction 3, restore forward 2 (event bitmap, word
+    sweep), restore backward 1, gather backward 1, and the scan: staged
+    dispatch 3 forward (decay table, row order, scan) + 4 backward (the same
+    and the partial-sum reduction), event-parallel dispatch 2 + 3 (no row
+    order).  The event-parallel kernels run where the staged backward would
+    have fewer than 5 warps per SM (dstate 16: 8 channels per warp)."""
+    mode = os.environ.get("BCM_SCAN_SEG", "1")   # the library's dispatch override (0 never, 2 always)
+    if mode == "0":
+        seg = False
+    elif mode == "1":
+        seg = rows * cfg.D // 8 < 5 * sm_count
+    else:
+        seg = True
+    return 9 + (5 if seg else 7)
+
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per stage and
 # block from one ncu capture, summed over the stage's kernels (summaries in
 # profiles/, one per workload).  Writes that stay in the 126 MB L2 when a
@@ -412,7 +431,8 @@ def run_stack(args, cfg, rank, world, local, dev):
         "per_op_ms": per_op,
         "per_op_frac_hbm": per_frac,
         "clocks": clk,
-        "gpu_launches": KERNELS_PER_BLOCK * cfg.blocks * args.steps,
+        "gpu_launches": cfg.blocks * args.steps * stack_kernels_per_block(
+            cfg, b1 - b0, torch.cuda.get_device_properties(dev).multi_processor_count),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
