@@ -40,6 +40,7 @@ ABI_SYMBOLS = (
     "bcm_event_decode_step",
     "bcm_extract_expand_fill",
     "bcm_extract_expanded",
+    "bcm_extract_expanded_ft",
     "bcm_gather_events_bwd_rows",
     "bcm_restore_workspace_bytes",
     "bcm_restore_bitmap_bytes",

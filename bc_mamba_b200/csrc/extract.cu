@@ -73,8 +73,8 @@ constexpr int kBldWords = 2;
 template <typename T>
 __global__ void __launch_bounds__(kCountWarps * 32)
 threshold_mask_bld_kernel(const T* __restrict__ x, int L, int Dm, int n_words, int n_dblk, int n_wparts,
-                          int64_t n_units, float thr, uint32_t* __restrict__ mask,
-                          int32_t* __restrict__ counts) {
+                          int64_t n_units, float thr, const float* __restrict__ thr_feature,
+                          uint32_t* __restrict__ mask, int32_t* __restrict__ counts) {
     const int64_t unit = (int64_t)blockIdx.x * kCountWarps + (threadIdx.x >> 5);
     if (unit >= n_units) return;
     const int lane = lane_id();
@@ -84,6 +84,8 @@ threshold_mask_bld_kernel(const T* __restrict__ x, int L, int Dm, int n_words, i
     const int64_t b = rest / n_dblk;
     const int d = dblk * 32 + lane;
     const bool valid = d < Dm;
+    // one threshold for every feature, or feature d's own
+    const float th = (thr_feature != nullptr && valid) ? thr_feature[d] : thr;
     const T* col = x + b * L * (int64_t)Dm + d;
     uint32_t* mrow = mask + (b * Dm + d) * (int64_t)n_words;
     const int w_beg = wpart * kBldWords;
@@ -98,7 +100,7 @@ threshold_mask_bld_kernel(const T* __restrict__ x, int L, int Dm, int n_words, i
         }
         uint32_t word = 0u;
 #pragma unroll
-        for (int r = 0; r < 32; ++r) word |= (v[r] > thr ? 1u : 0u) << r;   // NaN > thr is false
+        for (int r = 0; r < 32; ++r) word |= (v[r] > th ? 1u : 0u) << r;   // NaN > th is false
         if (valid) {
             mrow[w] = word;
             cnt += __popc(word);
@@ -612,7 +614,8 @@ static bcm_status count_base_impl(const void* base_input, bcm_dtype dtype, int64
 
 template <typename Hook>
 static bcm_status count_bld_impl(const void* input_bld, bcm_dtype dtype, int64_t batch, int64_t seqlen,
-                                 int64_t d_model, float threshold, int32_t* counts, int32_t* cu_seqlens,
+                                 int64_t d_model, float threshold, const float* thr_feature,
+                                 int32_t* counts, int32_t* cu_seqlens,
                                  int32_t* max_seqlen, void* workspace, size_t workspace_bytes,
                                  int64_t* n_events_host, int32_t* max_seqlen_host, cudaStream_t stream,
                                  Hook&& before_sync) {
@@ -649,7 +652,7 @@ static bcm_status count_bld_impl(const void* input_bld, bcm_dtype dtype, int64_t
             using T = decltype(tag);
             threshold_mask_bld_kernel<T><<<(unsigned)grid, kCountWarps * 32, 0, stream>>>(
                 static_cast<const T*>(input_bld), L, (int)d_model, n_words, n_dblk, n_wparts, n_units, threshold,
-                static_cast<uint32_t*>(workspace), counts);
+                thr_feature, static_cast<uint32_t*>(workspace), counts);
             BCM_LAUNCH_CHECK();
             return BCM_OK;
         });
@@ -680,8 +683,8 @@ extern "C" bcm_status bcm_extract_base_count_bld(const void* input_bld, bcm_dtyp
                                                  int64_t* n_events_host, int32_t* max_seqlen_host,
                                                  cudaStream_t stream) {
     clear_error();
-    return count_bld_impl(input_bld, dtype, batch, seqlen, d_model, threshold, counts, cu_seqlens, max_seqlen,
-                          workspace, workspace_bytes, n_events_host, max_seqlen_host, stream, no_hook);
+    return count_bld_impl(input_bld, dtype, batch, seqlen, d_model, threshold, nullptr, counts, cu_seqlens,
+                          max_seqlen, workspace, workspace_bytes, n_events_host, max_seqlen_host, stream, no_hook);
 }
 
 extern "C" bcm_status bcm_extract_base_fill(int64_t n_base_channels, int64_t seqlen,
@@ -756,15 +759,13 @@ extern "C" bcm_status bcm_extract_expand_fill(int64_t n_base_channels, int64_t s
                               cu_seqlens, x, x_dtype, x_flat, INT64_MAX, stream);
 }
 
-extern "C" bcm_status bcm_extract_expanded(const void* input, bcm_dtype dtype, int32_t input_layout,
-                                           int64_t batch, int64_t d_model, int64_t seqlen, float threshold,
-                                           int64_t expand, int32_t* counts, int32_t* base_cu_seqlens,
-                                           int32_t* max_seqlen, void* workspace, size_t workspace_bytes,
-                                           int64_t capacity, int32_t* ch_ids, int32_t* t_steps, int32_t* k_flat,
-                                           int32_t* cu_seqlens, const void* x, bcm_dtype x_dtype, void* x_flat,
-                                           int64_t* n_events_host, int32_t* max_seqlen_host,
-                                           cudaStream_t stream) {
-    clear_error();
+static bcm_status extract_expanded_impl(const void* input, bcm_dtype dtype, int32_t input_layout, int64_t batch,
+                                        int64_t d_model, int64_t seqlen, float threshold, const float* thr_feature,
+                                        int64_t expand, int32_t* counts, int32_t* base_cu_seqlens,
+                                        int32_t* max_seqlen, void* workspace, size_t workspace_bytes,
+                                        int64_t capacity, int32_t* ch_ids, int32_t* t_steps, int32_t* k_flat,
+                                        int32_t* cu_seqlens, const void* x, bcm_dtype x_dtype, void* x_flat,
+                                        int64_t* n_events_host, int32_t* max_seqlen_host, cudaStream_t stream) {
     BCM_REQUIRE(input_layout == 0 || input_layout == 1, "extract_expanded: input_layout must be 0 or 1");
     BCM_REQUIRE(batch >= 0 && d_model >= 0 && seqlen >= 0 && capacity >= 0, "extract_expanded: negative size");
     BCM_REQUIRE(expand >= 1 && batch * d_model * expand < (1ll << 31), "extract_expanded: bad expand");
@@ -789,8 +790,39 @@ extern "C" bcm_status bcm_extract_expanded(const void* input, bcm_dtype dtype, i
     if (input_layout == 0)
         return count_base_impl(input, dtype, NCb, seqlen, threshold, counts, base_cu_seqlens, max_seqlen, workspace,
                                workspace_bytes, n_events_host, max_seqlen_host, stream, fill);
-    return count_bld_impl(input, dtype, batch, seqlen, d_model, threshold, counts, base_cu_seqlens, max_seqlen,
-                          workspace, workspace_bytes, n_events_host, max_seqlen_host, stream, fill);
+    return count_bld_impl(input, dtype, batch, seqlen, d_model, threshold, thr_feature, counts, base_cu_seqlens,
+                          max_seqlen, workspace, workspace_bytes, n_events_host, max_seqlen_host, stream, fill);
+}
+
+extern "C" bcm_status bcm_extract_expanded(const void* input, bcm_dtype dtype, int32_t input_layout,
+                                           int64_t batch, int64_t d_model, int64_t seqlen, float threshold,
+                                           int64_t expand, int32_t* counts, int32_t* base_cu_seqlens,
+                                           int32_t* max_seqlen, void* workspace, size_t workspace_bytes,
+                                           int64_t capacity, int32_t* ch_ids, int32_t* t_steps, int32_t* k_flat,
+                                           int32_t* cu_seqlens, const void* x, bcm_dtype x_dtype, void* x_flat,
+                                           int64_t* n_events_host, int32_t* max_seqlen_host,
+                                           cudaStream_t stream) {
+    clear_error();
+    return extract_expanded_impl(input, dtype, input_layout, batch, d_model, seqlen, threshold, nullptr, expand,
+                                 counts, base_cu_seqlens, max_seqlen, workspace, workspace_bytes, capacity, ch_ids,
+                                 t_steps, k_flat, cu_seqlens, x, x_dtype, x_flat, n_events_host, max_seqlen_host,
+                                 stream);
+}
+
+extern "C" bcm_status bcm_extract_expanded_ft(const void* input_bld, bcm_dtype dtype, int64_t batch,
+                                              int64_t d_model, int64_t seqlen, const float* feature_thresholds,
+                                              int64_t expand, int32_t* counts, int32_t* base_cu_seqlens,
+                                              int32_t* max_seqlen, void* workspace, size_t workspace_bytes,
+                                              int64_t capacity, int32_t* ch_ids, int32_t* t_steps,
+                                              int32_t* k_flat, int32_t* cu_seqlens, const void* x,
+                                              bcm_dtype x_dtype, void* x_flat, int64_t* n_events_host,
+                                              int32_t* max_seqlen_host, cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(feature_thresholds != nullptr, "extract_expanded_ft: null feature thresholds");
+    return extract_expanded_impl(input_bld, dtype, 1, batch, d_model, seqlen, 0.f, feature_thresholds, expand,
+                                 counts, base_cu_seqlens, max_seqlen, workspace, workspace_bytes, capacity, ch_ids,
+                                 t_steps, k_flat, cu_seqlens, x, x_dtype, x_flat, n_events_host, max_seqlen_host,
+                                 stream);
 }
 
 extern "C" bcm_status bcm_expand_base_events(const int32_t* base_ch_ids,

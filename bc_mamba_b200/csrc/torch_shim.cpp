@@ -234,7 +234,8 @@ static int64_t async_fill_bytes() {
 }
 
 std::tuple<std::vector<Tensor>, int64_t> extract_expanded_events(Tensor x, double threshold, int64_t expand,
-                                                                  bool bld, const optional<Tensor>& x_conv) {
+                                                                  bool bld, const optional<Tensor>& x_conv,
+                                                                  const optional<Tensor>& feature_thresholds) {
     const char* fn = "extract_expanded_events";
     TORCH_CHECK(expand >= 1, fn, ": expand must be >= 1");
     TORCH_CHECK(x.is_cuda() && x.is_contiguous() && x.dim() == 3, fn, ": x must be a contiguous 3-D CUDA tensor");
@@ -248,6 +249,15 @@ std::tuple<std::vector<Tensor>, int64_t> extract_expanded_events(Tensor x, doubl
         TORCH_CHECK(v.size(0) == B && v.size(1) == d_model * expand && v.size(2) == L, fn,
                     ": x_conv must be (B, d_model*expand, L)");
         xc = &v;
+    }
+    const float* thr_ft = nullptr;
+    if (feature_thresholds.has_value() && feature_thresholds->defined()) {
+        const Tensor& t = *feature_thresholds;
+        TORCH_CHECK(bld, fn, ": feature_thresholds need the (B, L, d_model) layout (bld=True)");
+        TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32 && t.is_contiguous() && t.dim() == 1 &&
+                        t.size(0) == d_model && t.device() == x.device(),
+                    fn, ": feature_thresholds must be a contiguous float32 (d_model) tensor on x's device");
+        thr_ft = t.data_ptr<float>();
     }
     const bcm_dtype dt = to_bcm(x.scalar_type(), fn);
     const int64_t NCb = B * d_model;
@@ -271,16 +281,25 @@ std::tuple<std::vector<Tensor>, int64_t> extract_expanded_events(Tensor x, doubl
     const bool fill_now = cap > 0;
     int64_t E = 0;
     int32_t mh = 0;
-    check_status(bcm_extract_expanded(x.data_ptr(), dt, bld ? 1 : 0, B, d_model, L, (float)threshold, expand,
-                                      counts.data_ptr<int32_t>(), base_cu.data_ptr<int32_t>(), mx.data_ptr<int32_t>(),
-                                      ws.data_ptr(), ws.numel(), cap,
-                                      fill_now ? ch_c.data_ptr<int32_t>() : nullptr,
-                                      fill_now ? ts_c.data_ptr<int32_t>() : nullptr,
-                                      fill_now ? kf_c.data_ptr<int32_t>() : nullptr, cu_x.data_ptr<int32_t>(),
-                                      (fill_now && xc) ? xc->data_ptr() : nullptr,
-                                      xc ? to_bcm(xc->scalar_type(), fn) : BCM_F32,
-                                      (fill_now && xc) ? x_c.data_ptr() : nullptr, &E, &mh, cur_stream()),
-                 fn);
+    int32_t* o_ch = fill_now ? ch_c.data_ptr<int32_t>() : nullptr;
+    int32_t* o_ts = fill_now ? ts_c.data_ptr<int32_t>() : nullptr;
+    int32_t* o_kf = fill_now ? kf_c.data_ptr<int32_t>() : nullptr;
+    const void* g_x = (fill_now && xc) ? xc->data_ptr() : nullptr;
+    const bcm_dtype g_dt = xc ? to_bcm(xc->scalar_type(), fn) : BCM_F32;
+    void* g_out = (fill_now && xc) ? x_c.data_ptr() : nullptr;
+    if (thr_ft) {
+        check_status(bcm_extract_expanded_ft(x.data_ptr(), dt, B, d_model, L, thr_ft, expand,
+                                             counts.data_ptr<int32_t>(), base_cu.data_ptr<int32_t>(),
+                                             mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), cap, o_ch, o_ts, o_kf,
+                                             cu_x.data_ptr<int32_t>(), g_x, g_dt, g_out, &E, &mh, cur_stream()),
+                     fn);
+    } else {
+        check_status(bcm_extract_expanded(x.data_ptr(), dt, bld ? 1 : 0, B, d_model, L, (float)threshold, expand,
+                                          counts.data_ptr<int32_t>(), base_cu.data_ptr<int32_t>(),
+                                          mx.data_ptr<int32_t>(), ws.data_ptr(), ws.numel(), cap, o_ch, o_ts, o_kf,
+                                          cu_x.data_ptr<int32_t>(), g_x, g_dt, g_out, &E, &mh, cur_stream()),
+                     fn);
+    }
     const int64_t n = E * expand;
     TORCH_CHECK(n < (1ll << 31), fn, ": expanded events exceed int32");
     record_events(key, n);
@@ -1268,9 +1287,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "extract_base_events (bld: from the (B, L, d_model) layout) -> (6 outputs, max count as a host int)");
     m.def("extract_expanded_events", &extract_expanded_events, py::arg("x"), py::arg("threshold"),
           py::arg("expand"), py::arg("bld") = false, py::arg("x_conv") = py::none(),
+          py::arg("feature_thresholds") = py::none(),
           "extract_base_events then expand_base_events in one fill pass -> ((ch, t, k, cu, max[, x_flat]), "
           "max count as a host int); bld: from the (B, L, d_model) layout; x_conv (B, d_model*expand, L): "
-          "also gather_events_fwd of it at the stream (x_flat)");
+          "also gather_events_fwd of it at the stream (x_flat); feature_thresholds (d_model) float32 with bld: "
+          "feature j fires above feature_thresholds[j] instead of threshold");
     m.def("extract_base_events_bld", &extract_base_events_bld_fwd, py::arg("x"), py::arg("threshold"),
           "extract_base_events from the (B, L, d_model) layout: same 6 outputs, no transposed copy");
     m.def("conv_events_fwd", &conv_events_fwd, py::arg("x"), py::arg("weight"), py::arg("bias"),

@@ -294,12 +294,14 @@ class ExtractGatherFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x_conv, spikes, threshold, expand, bld, max_out):
         x_c = x_conv.contiguous()
+        # threshold: one float, or a tensor with one threshold per feature
+        ft = threshold if isinstance(threshold, torch.Tensor) else None
         with cuda_stage("routing_index_extraction"):
             # the maximum count arrives on the host with the event total (one
             # synchronisation); expansion copies counts, so it is max_seqlen
             # of the expanded stream too
             (ch, ts, kf, cu, _mx, x_flat), max_seqlen = load_ops().extract_expanded_events(
-                spikes, threshold, expand, bld=bld, x_conv=x_c)
+                spikes, 0.0 if ft is not None else threshold, expand, bld=bld, x_conv=x_c, feature_thresholds=ft)
         max_out.append(int(max_seqlen))
         ctx.save_for_backward(ts, cu)
         ctx.shape = x_c.shape
@@ -339,9 +341,12 @@ def extract_events_base(base_input, x_conv, threshold: float, expand: int):
     return ch, ts, kf, cu, mx[0], x_flat
 
 
-def extract_events_1d(hidden_states, x_conv, threshold: float, expand: int):
+def extract_events_1d(hidden_states, x_conv, threshold, expand: int):
     """Threshold (B, L, d_model) spikes into the expanded event stream and
     gather x_conv (B, D, L) at the events, like Mamba.extract_events_1d.
+    `threshold` is a float as in the reference, or a contiguous float32
+    (d_model,) tensor on the spikes' device: feature j fires above
+    threshold[j].
 
     Returns (channel_ids, time_steps, k_flat, cu_seqlens, max_seqlen, x_conv_flat).
     """
@@ -350,8 +355,8 @@ def extract_events_1d(hidden_states, x_conv, threshold: float, expand: int):
     # and the gather of x_conv in one fill pass, the maximum count back with
     # the event total (one synchronisation, no .item())
     mx = []
-    x_flat, ch, ts, kf, cu = ExtractGatherFn.apply(x_conv, hidden_states.contiguous(), float(threshold),
-                                                   int(expand), True, mx)
+    thr = threshold if isinstance(threshold, torch.Tensor) else float(threshold)
+    x_flat, ch, ts, kf, cu = ExtractGatherFn.apply(x_conv, hidden_states.contiguous(), thr, int(expand), True, mx)
     return ch, ts, kf, cu, mx[0], x_flat
 
 

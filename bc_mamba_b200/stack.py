@@ -22,14 +22,16 @@ calibrated once on the workload's data (``calibrate_thresholds``): every
 feature fires at rate rho (the reference regularises each layer's rate
 towards a target, lra_impl.py SequenceClassifierBase target_rate) and the
 spike pattern comes from the layer's own membrane.  (The reference's spike
-head STE(sigmoid(prob_head(LN v)) >= theta) does not control density.)  The
-stack carries the membrane relative to the next block's thresholds,
-s_l = v_l - theta_l, so extraction compares s_l > 0 with the reference's
-scalar-threshold API and the offsets ride in out_proj's epilogue:
-s_{l+1} = leak*s_l + (y_l W_out^T + c_l), c_l = leak*theta_l - theta_{l+1}
-(theta after the last block = 0, so the stack's output is v itself).  The
-conv feeding the gather (in_proj, causal conv1d, SiLU; e_model.py:428-451) is
-outside the path: each block's x_conv (B, D, L) is an input of the step.
+head STE(sigmoid(prob_head(LN v)) >= theta) does not control density.)  With
+n blocks the stack carries the membrane scaled as z_l = leak^(n-l) * v_l, so
+the leak disappears from the chain: z_{l+1} = z_l + leak^(n-1-l) * y_l W_out^T
+is one GEMM that adds into z in place (cuBLAS beta = 1, alpha = the scale),
+z_n = v_n is the stack's output, and the backward passes z's gradient
+through every block without an elementwise kernel.  Block l extracts where
+z_l > leak^(n-l) * theta_l, feature by feature (extraction's per-feature
+threshold form; leak > 0).  The conv feeding the gather (in_proj, causal
+conv1d, SiLU; e_model.py:428-451) is outside the path: each block's x_conv
+(B, D, L) is an input of the step.
 
 Inputs are generated per GLOBAL batch row from that row's own seed, so a rank
 holding rows [b0, b1) of the global batch sees exactly the rows a single GPU
@@ -52,9 +54,10 @@ def _inv_softplus(y: torch.Tensor) -> torch.Tensor:
     return torch.log(torch.expm1(y))
 
 
-def event_path(v, x_conv, threshold: float, expand: int, dt_idle, dt_active, A, W_B, W_C, D):
+def event_path(v, x_conv, threshold, expand: int, dt_idle, dt_active, A, W_B, W_C, D):
     """The event hot path of one block on the GPU: extraction of v (B, L,
-    d_model) at `threshold` with the gather of x_conv (B, D, L) -> depthwise
+    d_model) at `threshold` (a float, or a (d_model,) tensor with one
+    threshold per feature) with the gather of x_conv (B, D, L) -> depthwise
     scan -> ZOH restore.  Returns (y_dense (B, L, D), (events, max_seqlen))."""
     from . import interface as itf
 
@@ -66,30 +69,36 @@ def event_path(v, x_conv, threshold: float, expand: int, dt_idle, dt_active, A, 
     return itf.restore_dense_fn(y, ts, cu, dim, L), (int(ch.numel()), int(mx))
 
 
-class _Proj(torch.autograd.Function):
-    """out_proj: y (B, L, D) @ W_out^T + c -> (B, L, d_model) with a constant
-    per-feature offset c (no gradient), optionally with TF32 tensor-core GEMMs
-    in forward and backward."""
+class _ProjAccum(torch.autograd.Function):
+    """out_proj added into the carried membrane in place:
+    z += alpha * (y (B, L, D) @ W_out^T), one GEMM whose epilogue reads and
+    writes z (cuBLAS beta = 1), optionally with TF32 tensor cores.  The
+    backward passes z's gradient through unchanged and folds alpha into the
+    small operands: dY = g @ (alpha * W_out), dW_out = alpha * g^T y."""
 
     @staticmethod
-    def forward(ctx, y, w, c, tf32: bool):
+    def forward(ctx, z, y, w, alpha: float, tf32: bool):
         from .interface import cuda_stage
 
         ctx.save_for_backward(y, w)
+        ctx.alpha = alpha
         ctx.tf32 = tf32
         with cuda_stage("out_projection"), _tf32(tf32 and y.is_cuda):
-            return F.linear(y, w, c)
+            z.view(-1, z.shape[-1]).addmm_(y.reshape(-1, y.shape[-1]), w.t(), alpha=alpha)
+        ctx.mark_dirty(z)
+        return z
 
     @staticmethod
     def backward(ctx, g):
         from .interface import cuda_stage
 
         y, w = ctx.saved_tensors
+        a = ctx.alpha
         with cuda_stage("out_projection_backward"), _tf32(ctx.tf32 and y.is_cuda):
-            dy = g @ w if ctx.needs_input_grad[0] else None
-            dw = _weight_grad(g.reshape(-1, g.shape[-1]), y.reshape(-1, y.shape[-1])) \
-                if ctx.needs_input_grad[1] else None
-        return dy, dw, None, None
+            dy = g @ (w * a) if ctx.needs_input_grad[1] else None
+            dw = _weight_grad(g.reshape(-1, g.shape[-1]), y.reshape(-1, y.shape[-1])).mul_(a) \
+                if ctx.needs_input_grad[2] else None
+        return g, dy, dw, None, None
 
 
 def _weight_grad(g2: torch.Tensor, y2: torch.Tensor) -> torch.Tensor:
@@ -142,6 +151,8 @@ class EventStack:
 
     def __init__(self, cfg: Config, device, seed: int = 0, leak: float = 0.95,
                  path: Callable = event_path, dtype=torch.float32, proj_tf32: bool = False):
+        if not leak > 0:
+            raise ValueError("EventStack: leak must be positive (the membrane is carried scaled by its powers)")
         self.cfg = cfg
         self.leak = leak
         self.path = path
@@ -150,6 +161,7 @@ class EventStack:
         self.proj_tf32 = proj_tf32
         g = torch.Generator().manual_seed(seed * 7919 + 17)
         D, N, dm = cfg.D, cfg.N, cfg.d_model
+        self._thr_cache = None
         self.params: List[StackParams] = []
         for _ in range(cfg.blocks):
             # value distributions of the benchmark configs (A = -(1..N);
@@ -171,10 +183,15 @@ class EventStack:
     def all_params(self) -> List[torch.Tensor]:
         return [t for p in self.params for t in p.tensors()]
 
-    def block(self, l: int, s: torch.Tensor, x_conv: torch.Tensor, offset=None):
-        """Block l on its membrane relative to its thresholds, s (B, L,
-        d_model) (a feature fires where s > 0): returns (y W_out^T + offset,
-        the path's (events, max_seqlen))."""
+    def z_scale(self, l: int) -> float:
+        """z_l = z_scale(l) * v_l: the carried membrane before block l."""
+        return self.leak ** (self.cfg.blocks - l)
+
+    def block(self, l: int, z: torch.Tensor, x_conv: torch.Tensor, threshold):
+        """Block l on the carried membrane z_l (B, L, d_model), in place:
+        extraction where z_l exceeds `threshold` (per feature, on z's scale),
+        the event path, and z_{l+1} = z_l + leak^(n-1-l) * y W_out^T.
+        Returns (z_{l+1} (the same tensor), the path's (events, max_seqlen))."""
         p = self.params[l]
         N = self.cfg.N
         if p.A_log.is_cuda and p.A_log.dtype == torch.float32:
@@ -187,25 +204,31 @@ class EventStack:
             W_C = p.W_BC[:, N:].contiguous()
             dt_idle = F.softplus(p.a0) + 1e-6
             dt_active = F.softplus(p.a1) + 1e-6
-        y_dense, events = self.path(s, x_conv, 0.0, self.cfg.expand, dt_idle, dt_active, A, W_B, W_C, p.D)
-        return _Proj.apply(y_dense, p.W_out, offset, self.proj_tf32), events
+        y_dense, events = self.path(z, x_conv, threshold, self.cfg.expand, dt_idle, dt_active, A, W_B, W_C, p.D)
+        alpha = self.z_scale(l + 1)
+        return _ProjAccum.apply(z, y_dense, p.W_out, alpha, self.proj_tf32), events
 
-    def offsets(self, thetas: Sequence[torch.Tensor]) -> List[torch.Tensor]:
-        """c_l = leak*theta_l - theta_{l+1} (theta after the last block = 0)."""
-        n = self.cfg.blocks
-        return [(self.leak * thetas[l] - (thetas[l + 1] if l + 1 < n else 0.0)).contiguous() for l in range(n)]
+    def z_thresholds(self, thetas: Sequence[torch.Tensor]) -> List[torch.Tensor]:
+        """Block l's per-feature thresholds on z's scale, z_scale(l) *
+        thetas[l]; kept while the same threshold tensors come back unchanged."""
+        c = self._thr_cache
+        if c is not None and len(c[0]) == len(thetas) and all(
+                a is b and a._version == ver for a, b, ver in zip(c[0], thetas, c[1])):
+            return c[2]
+        tz = [(thetas[l] * self.z_scale(l)).contiguous() for l in range(self.cfg.blocks)]
+        self._thr_cache = (list(thetas), [t._version for t in thetas], tz)
+        return tz
 
     def forward(self, v0: torch.Tensor, x_convs: Sequence[torch.Tensor], thetas: Sequence[torch.Tensor]):
         """Membrane after the stack and (events, max_seqlen) of every block;
-        thetas[l] (d_model,) are block l's firing thresholds."""
-        c = self.offsets(thetas)
-        s = v0 - thetas[0]
+        thetas[l] (d_model,) are block l's firing thresholds on v_l."""
+        tz = self.z_thresholds(thetas)
+        z = v0 * self.z_scale(0)     # a fresh tensor: the blocks add into it in place
         events = []
         for l in range(self.cfg.blocks):
-            dv, e = self.block(l, s, x_convs[l], c[l])
-            s = torch.add(dv, s, alpha=self.leak)
+            z, e = self.block(l, z, x_convs[l], tz[l])
             events.append(e)
-        return s, events
+        return z, events
 
 
 # ------------------------------------------------------------------ data ----
@@ -272,12 +295,13 @@ def calibrate_thresholds(stack: EventStack, v0: torch.Tensor, x_convs: Sequence[
                          rho: Optional[float] = None, group=None, gather: bool = True) -> List[torch.Tensor]:
     """theta_l[j] = the (1 - rho) quantile of feature j of block l's input
     membrane, block by block (each block's membrane depends on the
-    thresholds before it)."""
+    thresholds before it).  The quantile is taken on the carried membrane
+    z_l (a positive multiple of v_l) and returned on v's scale."""
     rho = stack.cfg.rho if rho is None else rho
-    v = v0
+    z = v0 * stack.z_scale(0)
     th = []
     for l in range(stack.cfg.blocks):
-        th.append(feature_quantiles(v, 1.0 - rho, group, gather))
-        dv, _ = stack.block(l, (v - th[-1]).contiguous(), x_convs[l])
-        v = stack.leak * v + dv
+        tz = feature_quantiles(z, 1.0 - rho, group, gather).contiguous()
+        th.append(tz / stack.z_scale(l))
+        z, _ = stack.block(l, z, x_convs[l], tz)
     return th

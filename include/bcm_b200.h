@@ -171,6 +171,24 @@ BCM_API bcm_status bcm_extract_expanded(const void* input, bcm_dtype dtype,
                                   int64_t* n_events_host, int32_t* max_seqlen_host,
                                   cudaStream_t stream);
 
+/* bcm_extract_expanded on the (B, L, d_model) layout with a threshold per
+ * feature: input[b, t, j] fires when float(input[b, t, j]) >
+ * feature_thresholds[j] (device, d_model floats).  No reference binding
+ * (the reference thresholds with one scalar); a stack of event blocks that
+ * carries its membrane without per-feature offsets extracts with it. */
+BCM_API bcm_status bcm_extract_expanded_ft(const void* input_bld, bcm_dtype dtype,
+                                  int64_t batch, int64_t d_model, int64_t seqlen,
+                                  const float* feature_thresholds, int64_t expand,
+                                  int32_t* counts, int32_t* base_cu_seqlens,
+                                  int32_t* max_seqlen,
+                                  void* workspace, size_t workspace_bytes,
+                                  int64_t capacity, int32_t* ch_ids,
+                                  int32_t* t_steps, int32_t* k_flat,
+                                  int32_t* cu_seqlens,
+                                  const void* x, bcm_dtype x_dtype, void* x_flat,
+                                  int64_t* n_events_host, int32_t* max_seqlen_host,
+                                  cudaStream_t stream);
+
 /* ------------------------------------------------------------------------- *
  * Event gather of x[NC, L] at (channel_ids, time_steps) and its transpose.
  * Replaces extract_events_cuda.gather_events_fwd / gather_events_bwd

@@ -27,11 +27,14 @@ def _k_flat(ch: np.ndarray, t: np.ndarray) -> np.ndarray:
     return k
 
 
-def extract_base_events(base_input: np.ndarray, threshold: float):
-    """base_input (B, d_model, L) -> (ch, t, k, cu[NCb+1], counts[NCb], max)."""
+def extract_base_events(base_input: np.ndarray, threshold):
+    """base_input (B, d_model, L) -> (ch, t, k, cu[NCb+1], counts[NCb], max).
+    `threshold`: a scalar (the reference's API), or d_model values, one per
+    feature (the per-feature form of bcm_extract_expanded_ft)."""
     B, dm, L = base_input.shape
     x = np.asarray(base_input, dtype=np.float32).reshape(B * dm, L)
-    mask = x > np.float32(threshold)
+    thr = np.asarray(threshold, dtype=np.float32)
+    mask = x > (thr if thr.ndim == 0 else np.tile(thr.reshape(dm), B)[:, None])
     counts = mask.sum(axis=1).astype(I32)
     cu = np.zeros(B * dm + 1, dtype=I32)
     np.cumsum(counts, out=cu[1:])

@@ -20,7 +20,8 @@ class OracleEventPath(torch.autograd.Function):
         B, L, dm = v.shape
         dim = x_conv.shape[1]
         base = v.detach().transpose(1, 2).contiguous().numpy()           # (B, d_model, L)
-        bch, bt, bk, bcu, _, _ = ev.extract_base_events(base, threshold)
+        thr = threshold.detach().cpu().numpy() if isinstance(threshold, torch.Tensor) else threshold
+        bch, bt, bk, bcu, _, _ = ev.extract_base_events(base, thr)
         ch, t, k, cu, mx = ev.expand_base_events(bch, bt, bk, bcu, B, dm, expand)
         uf = ev.gather_events_fwd(x_conv.detach().numpy(), ch, t)
         p = [x.detach().double().numpy() for x in (dt_idle, dt_active, A, W_B, W_C, D)]

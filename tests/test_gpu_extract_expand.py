@@ -122,3 +122,44 @@ def test_capacity_paths(cap_bytes, monkeypatch):
         assert torch.equal(a, b)
     assert mx == int(ref[4].reshape(-1)[0].item())
     assert torch.equal(got[5], ops.gather_events_fwd(xc, ref[0], ref[1])[0])
+
+
+@pytest.mark.parametrize("B,dm,L", [(1, 1, 1), (2, 5, 31), (3, 33, 300), (4, 96, 1000), (2, 128, 4000)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_feature_thresholds(B, dm, L, dtype):
+    """The per-feature form (bcm_extract_expanded_ft): feature j fires above
+    thr[j]; bit-exact against the oracle's per-feature extraction, with the
+    fused gather of x_conv; one value in every threshold repeats an input
+    value exactly (strict compare)."""
+    ops = load_ops()
+    g = torch.Generator().manual_seed(B * 7 + dm + L)
+    x = torch.randn(B, L, dm, generator=g).to(dtype)
+    thr = (0.8 * torch.randn(dm, generator=g)).float()
+    thr[0] = x[0, 0, 0].float()
+    x_bdl = x.transpose(1, 2).contiguous()
+    for expand in (1, 2):
+        xc = torch.randn(B, dm * expand, L, generator=g).to(dev)
+        got, mx = ops.extract_expanded_events(x.to(dev), 0.0, expand, bld=True, x_conv=xc,
+                                              feature_thresholds=thr.to(dev))
+        bch, bt, bk, bcu, _, _ = ev.extract_base_events(x_bdl.float().numpy(), thr.numpy())
+        ref = ev.expand_base_events(bch, bt, bk, bcu, B, dm, expand)
+        for a, r, n in zip(got[:4], ref[:4], NAMES):
+            assert_exact(a, r, n)
+        assert mx == int(np.asarray(ref[4]).reshape(-1)[0])
+        if got[0].numel():
+            assert torch.equal(got[5], ops.gather_events_fwd(xc, got[0], got[1])[0])
+    # a threshold per feature equal to one scalar gives the scalar extraction
+    same, _ = ops.extract_expanded_events(x.to(dev), 0.3, 2, bld=True,
+                                          feature_thresholds=torch.full((dm,), 0.3, device=dev))
+    scal, _ = ops.extract_expanded_events(x.to(dev), 0.3, 2, bld=True)
+    for a, b in zip(same, scal):
+        assert torch.equal(a.reshape(-1), b.reshape(-1))
+
+
+def test_feature_thresholds_errors():
+    ops = load_ops()
+    x = torch.randn(2, 10, 4, device=dev)
+    with pytest.raises(RuntimeError, match="need the"):
+        ops.extract_expanded_events(x, 0.0, 1, bld=False, feature_thresholds=torch.zeros(4, device=dev))
+    with pytest.raises(RuntimeError, match="feature_thresholds must be"):
+        ops.extract_expanded_events(x, 0.0, 1, bld=True, feature_thresholds=torch.zeros(5, device=dev))

@@ -2,7 +2,8 @@
 float64 oracle path: the 4-block stack on the B200 (CUDA event path, fp32,
 fp32 out_proj) and the same stack on the CPU with the oracle path, same
 parameters and thresholds.  Each CPU block extracts its events from the
-membrane the GPU block saw (extraction is not differentiable in it), so both
+membrane the GPU block saw, at the per-feature thresholds the GPU block used
+(extraction is not differentiable in either), so both
 sides run on identical event streams and differ only by rounding; the final
 membrane, every parameter gradient and every x_conv gradient agree within the
 fp32 tolerance.  Event counts and densities are checked exactly against the
@@ -32,9 +33,10 @@ def test_stack_matches_oracle(spikes, rho):
     inp = stk.stack_inputs(cfg, range(cfg.B), dev)
     seen = []
 
-    def gpu_path(v, *a):
-        seen.append(v.detach().double().cpu())
-        return stk.event_path(v, *a)
+    def gpu_path(v, x_conv, threshold, *a):
+        # the carried membrane and the thresholds this block extracts at
+        seen.append((v.detach().double().cpu(), threshold.detach().cpu()))
+        return stk.event_path(v, x_conv, threshold, *a)
 
     gpu = stk.EventStack(cfg, dev, seed=cfg.seed, path=gpu_path)
     thr = stk.calibrate_thresholds(gpu, inp["v0"], inp["x_conv"])
@@ -46,8 +48,9 @@ def test_stack_matches_oracle(spikes, rho):
 
     it = iter(range(cfg.blocks))
 
-    def cpu_path(v_cpu, *a):
-        return oracle_path(seen[next(it)], *a)
+    def cpu_path(v_cpu, x_conv, threshold, *a):
+        v_gpu, thr_gpu = seen[next(it)]
+        return oracle_path(v_gpu, x_conv, thr_gpu, *a)
 
     cpu = stk.EventStack(cfg, "cpu", seed=cfg.seed, path=cpu_path, dtype=torch.float64)
     xs_c = [x.detach().double().cpu().requires_grad_(True) for x in inp["x_conv"]]
