@@ -118,3 +118,27 @@ def test_multichunk_x_layout():
     out2, x2, _ = sc.scan_fwd(u[:2048], k[:2048], np.array([0, 2048], np.int32), 2048, [0.001], [0.001], A,
                               [[1.0, 0.5]], [[1.0, 1.0]], is_depthwise_bc=True)
     np.testing.assert_allclose(x[0, 0], x2[0, 0], rtol=1e-12)
+
+
+def test_oracle_per_feature_thresholds():
+    """The oracle's per-feature extraction: feature j fires strictly above
+    thr[j]; equal thresholds give the scalar extraction."""
+    import numpy as np
+
+    from oracle import events as ev
+
+    rng = np.random.default_rng(3)
+    B, dm, L = 3, 7, 50
+    x = rng.standard_normal((B, dm, L)).astype(np.float32)
+    thr = rng.standard_normal(dm).astype(np.float32)
+    thr[2] = x[1, 2, 5]                       # a value equal to its threshold does not fire
+    ch, t, k, cu, counts, mx = ev.extract_base_events(x, thr)
+    mask = x.reshape(B * dm, L) > np.tile(thr, B)[:, None]
+    rows, cols = np.nonzero(mask)
+    assert np.array_equal(ch, rows) and np.array_equal(t, cols)
+    assert np.array_equal(counts, mask.sum(1))
+    assert not mask[1 * dm + 2, 5]
+    same = ev.extract_base_events(x, np.full(dm, 0.25, np.float32))
+    scal = ev.extract_base_events(x, 0.25)
+    for a, b in zip(same, scal):
+        assert np.array_equal(np.asarray(a), np.asarray(b))
