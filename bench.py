@@ -126,29 +126,30 @@ STAGE_OPS = {
     "dense_restoration_forward": "restore_fwd", "restore_backward": "restore_bwd",
     "sparse_scan_backward": "scan_bwd", "gather_scatter_backward": "gather_bwd",
 }
-# kernels each block launches (all ours): extract 3 (threshold + count,
-# count scan, fill of the expanded stream with the gather of x_conv), scan fwd
-# 1, restore fwd 1, restore bwd 1, scan bwd 2, gather bwd 1 (row writer)
-KERNELS_PER_BLOCK = 9
-
-
-def stack_kernels_per_block(cfg, rows: int, sm_count: int) -> int:
-    """Kernels of ours one block of the stack launches per step (forward and
-    backward), from the launch list of the bench workload: parameter
-    transforms 1 + 1, extraction 3, restore forward 2 (event bitmap, word
-    sweep), restore backward 1, gather backward 1, and the scan: staged
-    dispatch 3 forward (decay table, row order, scan) + 4 backward (the same
-    and the partial-sum reduction), event-parallel dispatch 2 + 3 (no row
-    order).  The event-parallel kernels run where the staged backward would
-    have fewer than 5 warps per SM (dstate 16: 8 channels per warp)."""
+def kernels_per_block(cfg, rows: int, sm_count: int, stack: bool) -> int:
+    """Kernels of ours one block launches per step (forward and backward),
+    from the launch list of the bench workload: extraction 3 (threshold +
+    count, count scan, fill of the expanded stream with the gather of
+    x_conv), restore forward 2 (event bitmap, word sweep), restore backward 1,
+    gather backward 1 (row writer), in the stack also the parameter
+    transforms 1 + 1, and the scan: staged dispatch 3 forward (decay table,
+    row order, scan) + 4 backward (the same and the partial-sum reduction),
+    event-parallel dispatch 2 + 3 (no row order).  The event-parallel kernels
+    run where the staged ones do not divide the rows of a feature into whole
+    warps, or where the staged backward would have fewer than 5 warps per SM
+    (the library's dispatch rule, dstate <= 64)."""
+    NP = 8 if cfg.N <= 8 else 16 if cfg.N <= 16 else 32 if cfg.N <= 32 else 64
+    cpw_bwd = 128 // NP if NP <= 16 else 256 // NP      # channels per warp, staged backward
+    cpw_fwd = 64 // NP                                  # and forward
+    staged_ok = rows % cpw_bwd == 0 and rows % cpw_fwd == 0
     mode = os.environ.get("BCM_SCAN_SEG", "1")   # the library's dispatch override (0 never, 2 always)
     if mode == "0":
         seg = False
     elif mode == "1":
-        seg = rows * cfg.D // 8 < 5 * sm_count
+        seg = not staged_ok or rows * cfg.D // cpw_bwd < 5 * sm_count
     else:
         seg = True
-    return 9 + (5 if seg else 7)
+    return 7 + (2 if stack else 0) + (5 if seg else 7)
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per stage and
 # block from one ncu capture, summed over the stage's kernels (summaries in
@@ -431,8 +432,8 @@ def run_stack(args, cfg, rank, world, local, dev):
         "per_op_ms": per_op,
         "per_op_frac_hbm": per_frac,
         "clocks": clk,
-        "gpu_launches": cfg.blocks * args.steps * stack_kernels_per_block(
-            cfg, b1 - b0, torch.cuda.get_device_properties(dev).multi_processor_count),
+        "gpu_launches": cfg.blocks * args.steps * kernels_per_block(
+            cfg, b1 - b0, torch.cuda.get_device_properties(dev).multi_processor_count, stack=True),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
@@ -526,7 +527,8 @@ def run_block(args, cfg, rank, world, local, dev):
         "per_op_ms": per_op,
         "per_op_frac_hbm": per_frac,
         "clocks": clk,
-        "gpu_launches": KERNELS_PER_BLOCK * args.steps,
+        "gpu_launches": args.steps * kernels_per_block(
+            cfg, cfg.B, torch.cuda.get_device_properties(dev).multi_processor_count, stack=False),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
