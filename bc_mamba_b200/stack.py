@@ -223,7 +223,7 @@ class EventStack:
         """Membrane after the stack and (events, max_seqlen) of every block;
         thetas[l] (d_model,) are block l's firing thresholds on v_l."""
         tz = self.z_thresholds(thetas)
-        z = v0 * self.z_scale(0)     # a fresh tensor: the blocks add into it in place
+        z = (v0 * self.z_scale(0)).contiguous()     # a fresh tensor: the blocks add into it in place
         events = []
         for l in range(self.cfg.blocks):
             z, e = self.block(l, z, x_convs[l], tz[l])
@@ -298,7 +298,7 @@ def calibrate_thresholds(stack: EventStack, v0: torch.Tensor, x_convs: Sequence[
     thresholds before it).  The quantile is taken on the carried membrane
     z_l (a positive multiple of v_l) and returned on v's scale."""
     rho = stack.cfg.rho if rho is None else rho
-    z = v0 * stack.z_scale(0)
+    z = (v0 * stack.z_scale(0)).contiguous()
     th = []
     for l in range(stack.cfg.blocks):
         tz = feature_quantiles(z, 1.0 - rho, group, gather).contiguous()

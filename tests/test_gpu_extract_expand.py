@@ -124,6 +124,24 @@ def test_capacity_paths(cap_bytes, monkeypatch):
     assert torch.equal(got[5], ops.gather_events_fwd(xc, ref[0], ref[1])[0])
 
 
+def test_capacity_pins_little_more_than_the_stream():
+    """The outputs are views of the fill's capacity buffers.  The capacity
+    follows the largest of the last totals of the same input shape (x 1.25,
+    + 4096 events), so no call's outputs keep much more storage alive than
+    they hold (the first call of a shape fills exact-size outputs)."""
+    ops = load_ops()
+    g = torch.Generator().manual_seed(77)
+    B, dm, L, expand = 3, 40, 777, 2              # a shape no other test uses
+    xc = torch.randn(B, dm * expand, L, generator=g).to(dev)
+    for _ in range(4):
+        v = torch.randn(B, L, dm, generator=g).to(dev)
+        got, _mx = ops.extract_expanded_events(v, 0.5, expand, bld=True, x_conv=xc)
+        n = got[0].numel()
+        limit = int(1.25 * 1.05 * n) + 4096       # draws at one density differ by well under 5 %
+        for t in (got[0], got[1], got[2], got[5]):
+            assert t.untyped_storage().nbytes() <= 4 * limit, (t.untyped_storage().nbytes(), n)
+
+
 @pytest.mark.parametrize("B,dm,L", [(1, 1, 1), (2, 5, 31), (3, 33, 300), (4, 96, 1000), (2, 128, 4000)])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_feature_thresholds(B, dm, L, dtype):
