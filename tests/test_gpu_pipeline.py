@@ -1,6 +1,7 @@
 """GPU parity of the whole hot path through the autograd boundary
-(extract -> expand -> gather -> scan -> restore, then backward), plus
-full-size (configs c1/c2) checks through size-independent properties:
+(extract -> expand -> gather -> scan -> restore, then backward) at c0 in
+full and at c1 size on a channel subset, plus full-size (configs c1/c2)
+checks of the separate entry points through size-independent properties:
 bit-exact streams, per-channel independence of the scan (a random channel
 subset against the oracle), linearity of the backward in dout."""
 import numpy as np
@@ -114,3 +115,42 @@ def test_full_size_properties(cfg_name):
                          None, None, 0, True)
     for a, b, n in zip(g[1:], g2[1:], ["dA", "dWB", "dWC", "ddti", "ddta", "dD"]):
         assert_close(b, 2.0 * a.float().cpu().numpy(), 1e-5, "linearity " + n)
+
+
+def test_pipeline_c1_composed():
+    """The bench's composed autograd path at configs[1] size (fused
+    extraction + expansion + gather, checkpointed scan, bitmap restore, row
+    gather backward) against the oracle: streams and gathered inputs
+    bit-exact, the dense output exactly the restore of the scan output, the
+    scan output and the gradient of the dense input on a random channel
+    subset within the fp32 tolerance."""
+    cfg = CONFIGS["c1"]
+    inp = make_inputs(cfg, device=dev)
+    (ch, ts, kf, cu, mx, u_flat, y, dense), du, _grads = _pipeline(cfg, inp)
+    cpu = make_inputs(cfg)
+    bch, bt, bk, bcu, _, _ = ev.extract_base_events(cpu["v"].numpy(), cpu["threshold"])
+    rch, rt, rk, rcu, rmx = ev.expand_base_events(bch, bt, bk, bcu, cfg.B, cfg.d_model, cfg.expand)
+    for a, b, n in [(ch, rch, "ch"), (ts, rt, "t"), (kf, rk, "k"), (cu, rcu, "cu")]:
+        assert_exact(a, b, n)
+    assert mx == int(np.asarray(rmx).reshape(-1)[0])
+    uf = ev.gather_events_fwd(cpu["u"].numpy(), rch, rt)
+    assert_exact(u_flat, uf, "u_flat")
+    y_np = y.detach().float().cpu().numpy()
+    assert_exact(dense, rs.restore_dense_fwd(y_np, rt, rcu, cfg.D, cfg.L), "dense = restore(y)")
+    # the scan on a channel subset, and the backward of the whole path there
+    rng = np.random.default_rng(1)
+    NC = cfg.B * cfg.D
+    chans = np.sort(rng.choice(NC, 96, replace=False))
+    idx, cu2 = _subset(rcu, chans)
+    d_of = chans % cfg.D
+    p = {n: cpu[n].numpy()[d_of] for n in ["dt_idle", "dt_active", "A", "W_B", "W_C", "D"]}
+    o_ref, _x, _ = sc.scan_fwd(uf[idx], rk[idx], cu2, int(np.asarray(rmx).reshape(-1)[0]), p["dt_idle"],
+                               p["dt_active"], p["A"], p["W_B"], p["W_C"], D=p["D"], is_depthwise_bc=True)
+    assert_close(y_np[idx], o_ref, TOL_F32, "y subset")
+    dy = rs.restore_dense_bwd(cpu["dout"].numpy(), rt, rcu, cfg.D, cfg.L)
+    g = sc.scan_bwd(uf[idx], rk[idx], cu2, int(np.asarray(rmx).reshape(-1)[0]), p["dt_idle"], p["dt_active"],
+                    p["A"], p["W_B"], p["W_C"], np.asarray(dy)[idx], D=p["D"], is_depthwise_bc=True)
+    local = np.repeat(np.arange(len(chans), dtype=np.int32), np.diff(cu2))
+    dx_ref = ev.gather_events_bwd(g[0], local, rt[idx], len(chans), cfg.L)
+    assert_close(du.reshape(NC, cfg.L)[torch.as_tensor(chans, device=dev)], np.asarray(dx_ref).reshape(len(chans), cfg.L),
+                 TOL_F32, "du subset")
