@@ -45,6 +45,7 @@ ABI_SYMBOLS = (
     "bcm_restore_workspace_bytes",
     "bcm_restore_bitmap_bytes",
     "bcm_restore_dense_fwd_bitmap",
+    "bcm_restore_dense_fwd_mask",
     "bcm_restore_dense_bwd_bitmap",
     "bcm_restore_dense_fwd",
     "bcm_restore_dense_bwd",

@@ -467,8 +467,11 @@ restore_fwd_words(const Tin* __restrict__ y, const int32_t* __restrict__ ts, con
     const int nwd = (u.t_end - u.t_beg + 31) >> 5;   // words of the unit
     auto mask_at = [&](int w) -> uint32_t { return (valid && w < nwd) ? mcol[(int64_t)w * D] : 0u; };
     // the values of a word's events (from global index first) into slot buffer buf
+    // (a bitmap with more bits than the channel has events, e.g. an
+    // extraction mask passed with another stream, reads no further than the
+    // channel's last event)
     auto fetch = [&](uint32_t m, int first, int buf) {
-        const int nv = __popc(m);
+        const int nv = min(__popc(m), beg + n - first);
         float(*sv)[32] = s_val[wi][buf];
         for (int k = 0; k < nv; ++k) {
             if constexpr (sizeof(Tin) == 4) {
@@ -606,6 +609,36 @@ static SweepLayout sweep_layout(int64_t B, int64_t D, int64_t L) {
     return s;
 }
 
+// The event bitmap from the extraction's threshold mask ([B*Dm, nw] words,
+// base channel b*Dm + j): logical channel b*D + d (D = Dm*expand) holds the
+// events of base feature j = d / expand, so its word w is mask word w of base
+// channel b*Dm + j.  A 32 x 32 tile per CTA through shared memory: the reads
+// run along w, the writes along d; every bitmap word is written.
+__global__ void __launch_bounds__(256)
+mask_bitmap_kernel(const uint32_t* __restrict__ mask, int Dm, int expand, int nw, int n_jblk, int n_wblk,
+                   uint32_t* __restrict__ bm) {
+    __shared__ uint32_t tile[32][33];
+    const int64_t blk = blockIdx.x;
+    const int wb = (int)(blk % n_wblk);
+    const int64_t rest = blk / n_wblk;
+    const int jb = (int)(rest % n_jblk);
+    const int64_t b = rest / n_jblk;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    for (int r = ty; r < 32; r += 8) {
+        const int j = jb * 32 + r, w = wb * 32 + tx;
+        tile[r][tx] = (j < Dm && w < nw) ? mask[(b * Dm + j) * (int64_t)nw + w] : 0u;
+    }
+    __syncthreads();
+    const int64_t D = (int64_t)Dm * expand;
+    const int n_j = min(32, Dm - jb * 32);
+    for (int r = ty; r < 32; r += 8) {
+        const int w = wb * 32 + r;
+        if (w >= nw) continue;
+        uint32_t* row = bm + (b * nw + w) * D + (int64_t)jb * 32 * expand;
+        for (int i = tx; i < n_j * expand; i += 32) row[i] = tile[i / expand][r];
+    }
+}
+
 static size_t bitmap_words_bytes(int64_t n_channels, int64_t seqlen) {
     return (size_t)n_channels * (size_t)((seqlen + 31) / 32) * sizeof(uint32_t);
 }
@@ -613,7 +646,8 @@ static size_t bitmap_words_bytes(int64_t n_channels, int64_t seqlen) {
 static bcm_status restore_fwd_impl(const void* y_flat, bcm_dtype y_dtype, const int32_t* time_steps,
                                    const int32_t* cu_seqlens, int64_t n_events, int64_t n_channels,
                                    int64_t dim, int64_t seqlen, void* out, bcm_dtype out_dtype,
-                                   uint32_t* bitmap, cudaStream_t stream) {
+                                   uint32_t* bitmap, const uint32_t* base_mask, int64_t expand,
+                                   cudaStream_t stream) {
     BCM_REQUIRE(dtype_ok(y_dtype) && dtype_ok(out_dtype), "restore_dense_fwd: unsupported dtype");
     BCM_REQUIRE(y_dtype == BCM_F32 || y_dtype == out_dtype,
                 "restore_dense_fwd: 16-bit input only supports the same output dtype");
@@ -631,7 +665,16 @@ static bcm_status restore_fwd_impl(const void* y_flat, bcm_dtype y_dtype, const 
     int32_t* e_start = bitmap ? reinterpret_cast<int32_t*>(reinterpret_cast<char*>(bitmap) +
                                                            bitmap_words_bytes(n_channels, seqlen))
                               : nullptr;
-    if (bitmap != nullptr && n_events > 0) {
+    if (bitmap != nullptr && n_events > 0 && base_mask != nullptr) {
+        // the bitmap transposed from the extraction's mask (every word written)
+        const int Dm = (int)(dim / expand);
+        const int n_jblk = (Dm + 31) / 32, n_wblk = (nw + 31) / 32;
+        const int64_t grid = B * n_jblk * n_wblk;
+        BCM_REQUIRE(grid < (1ll << 31), "restore_dense_fwd_mask: too many tiles");
+        mask_bitmap_kernel<<<(unsigned)grid, 256, 0, stream>>>(base_mask, Dm, (int)expand, nw, n_jblk, n_wblk,
+                                                               bitmap);
+        BCM_LAUNCH_CHECK();
+    } else if (bitmap != nullptr && n_events > 0) {
         // the bitmap first (every word written: zeros, then the words holding
         // events), then the word sweep reads it instead of the event times
         BCM_CUDA_TRY(cudaMemsetAsync(bitmap, 0, bitmap_words_bytes(n_channels, seqlen), stream));
@@ -671,7 +714,7 @@ extern "C" bcm_status bcm_restore_dense_fwd(const void* y_flat, bcm_dtype y_dtyp
                                             cudaStream_t stream) {
     clear_error();
     return restore_fwd_impl(y_flat, y_dtype, time_steps, cu_seqlens, n_events, n_channels, dim, seqlen,
-                            out, out_dtype, nullptr, stream);
+                            out, out_dtype, nullptr, nullptr, 1, stream);
 }
 
 extern "C" bcm_status bcm_restore_dense_fwd_bitmap(const void* y_flat, bcm_dtype y_dtype,
@@ -682,7 +725,24 @@ extern "C" bcm_status bcm_restore_dense_fwd_bitmap(const void* y_flat, bcm_dtype
     clear_error();
     BCM_REQUIRE(event_bitmap, "restore_dense_fwd_bitmap: null event_bitmap");
     return restore_fwd_impl(y_flat, y_dtype, time_steps, cu_seqlens, n_events, n_channels, dim, seqlen,
-                            out, out_dtype, event_bitmap, stream);
+                            out, out_dtype, event_bitmap, nullptr, 1, stream);
+}
+
+extern "C" bcm_status bcm_restore_dense_fwd_mask(const void* y_flat, bcm_dtype y_dtype,
+                                                 const int32_t* time_steps, const int32_t* cu_seqlens,
+                                                 int64_t n_events, int64_t n_channels, int64_t dim,
+                                                 int64_t seqlen, void* out, bcm_dtype out_dtype,
+                                                 const uint32_t* base_mask, int64_t expand,
+                                                 uint32_t* event_bitmap, cudaStream_t stream) {
+    clear_error();
+    BCM_REQUIRE(event_bitmap && base_mask, "restore_dense_fwd_mask: null event_bitmap or base_mask");
+    BCM_REQUIRE(expand >= 1 && dim % expand == 0, "restore_dense_fwd_mask: dim must be a multiple of expand");
+    // the bitmap built from events marks at most kCap events per channel;
+    // the mask holds them all, so the two agree only while no channel can
+    // have more
+    BCM_REQUIRE(seqlen <= kCap, "restore_dense_fwd_mask: seqlen above %d (use the event bitmap)", kCap);
+    return restore_fwd_impl(y_flat, y_dtype, time_steps, cu_seqlens, n_events, n_channels, dim, seqlen,
+                            out, out_dtype, event_bitmap, base_mask, expand, stream);
 }
 
 extern "C" size_t bcm_restore_bitmap_bytes(int64_t n_channels, int64_t dim, int64_t seqlen) {

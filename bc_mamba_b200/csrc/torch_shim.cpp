@@ -20,6 +20,7 @@
 #include <cstdlib>
 #include <map>
 #include <mutex>
+#include <string>
 #include <tuple>
 #include <vector>
 
@@ -33,9 +34,13 @@ namespace {
 using at::Tensor;
 using c10::optional;
 
+// Error messages carry no integers formatted by TORCH_CHECK itself: with this
+// torch build an integer in its message crashed the process instead of
+// raising, so numbers go in as text.
 void check_status(bcm_status st, const char* what) {
     if (st != BCM_OK) {
-        TORCH_CHECK(false, what, ": ", bcm_last_error(), " (status ", (int)st, ")");
+        const std::string code = std::to_string((int)st);
+        TORCH_CHECK(false, what, ": ", bcm_last_error(), " (status ", code, ")");
     }
 }
 
@@ -235,7 +240,8 @@ static int64_t async_fill_bytes() {
 
 std::tuple<std::vector<Tensor>, int64_t> extract_expanded_events(Tensor x, double threshold, int64_t expand,
                                                                   bool bld, const optional<Tensor>& x_conv,
-                                                                  const optional<Tensor>& feature_thresholds) {
+                                                                  const optional<Tensor>& feature_thresholds,
+                                                                  bool keep_mask) {
     const char* fn = "extract_expanded_events";
     TORCH_CHECK(expand >= 1, fn, ": expand must be >= 1");
     TORCH_CHECK(x.is_cuda() && x.is_contiguous() && x.dim() == 3, fn, ": x must be a contiguous 3-D CUDA tensor");
@@ -325,6 +331,7 @@ std::tuple<std::vector<Tensor>, int64_t> extract_expanded_events(Tensor x, doubl
     Tensor mo = (E == 0) ? torch::zeros({1}, opt_i) : mx;
     std::vector<Tensor> r = {ch, ts, kf, cu_x, mo};
     if (xc) r.push_back(x_flat);
+    if (keep_mask) r.push_back(ws);   // its first words: the threshold mask [B*d_model][ceil(L/32)]
     return {r, (int64_t)mh};
 }
 
@@ -1051,7 +1058,7 @@ std::vector<Tensor> selective_scan_bwd(const Tensor& u, const Tensor& delta, con
 // per-unit start indices, one flat int32 buffer for restore_dense_bwd_bitmap
 Tensor restore_fwd_impl(const Tensor& y_flat, const Tensor& time_steps, const Tensor& cu_seqlens,
                         int64_t dim, int64_t seqlen, const optional<at::ScalarType> out_dtype_opt,
-                        Tensor* bitmap) {
+                        Tensor* bitmap, const Tensor* base_mask = nullptr, int64_t expand = 1) {
     auto input_type = y_flat.scalar_type();
     TORCH_CHECK(input_type == at::ScalarType::Float || input_type == at::ScalarType::Half ||
                     input_type == at::ScalarType::BFloat16,
@@ -1088,6 +1095,23 @@ Tensor restore_fwd_impl(const Tensor& y_flat, const Tensor& time_steps, const Te
         const int64_t words = (int64_t)bcm_restore_bitmap_bytes(NC, dim, seqlen) / 4;
         TORCH_CHECK(words > 0, "restore_dense_fwd_bitmap: bad sizes");
         *bitmap = torch::empty({words}, y_flat.options().dtype(at::ScalarType::Int));
+        if (base_mask != nullptr) {
+            const Tensor& m = *base_mask;
+            TORCH_CHECK(expand >= 1 && dim % expand == 0, "restore_dense_fwd_bitmap: dim must be a multiple of expand");
+            TORCH_CHECK(m.is_cuda() && m.is_contiguous() && m.device() == y_flat.device() &&
+                            m.nbytes() >= (size_t)(NC / expand) * (size_t)((seqlen + 31) / 32) * 4,
+                        "restore_dense_fwd_bitmap: base_mask must be the mask buffer extract_expanded_events "
+                        "returned (keep_mask=True) for this stream");
+            check_status(bcm_restore_dense_fwd_mask(y_flat.data_ptr(), to_bcm(input_type, "restore_dense_fwd"),
+                                                    time_steps.data_ptr<int32_t>(), cu_seqlens.data_ptr<int32_t>(),
+                                                    E, NC, dim, seqlen, out.data_ptr(),
+                                                    to_bcm(out_type, "restore_dense_fwd"),
+                                                    reinterpret_cast<const uint32_t*>(m.data_ptr()), expand,
+                                                    reinterpret_cast<uint32_t*>(bitmap->data_ptr<int32_t>()),
+                                                    cur_stream()),
+                         "restore_dense_fwd_mask");
+            return out;
+        }
         check_status(bcm_restore_dense_fwd_bitmap(y_flat.data_ptr(), to_bcm(input_type, "restore_dense_fwd"),
                                                   time_steps.data_ptr<int32_t>(), cu_seqlens.data_ptr<int32_t>(),
                                                   E, NC, dim, seqlen, out.data_ptr(),
@@ -1112,9 +1136,11 @@ Tensor restore_dense_fwd(const Tensor& y_flat, const Tensor& time_steps, const T
 
 std::vector<Tensor> restore_dense_fwd_bitmap(const Tensor& y_flat, const Tensor& time_steps,
                                              const Tensor& cu_seqlens, int64_t dim, int64_t seqlen,
-                                             const optional<at::ScalarType> out_dtype_opt) {
+                                             const optional<at::ScalarType> out_dtype_opt,
+                                             const optional<Tensor>& base_mask, int64_t expand) {
     Tensor bitmap;
-    Tensor out = restore_fwd_impl(y_flat, time_steps, cu_seqlens, dim, seqlen, out_dtype_opt, &bitmap);
+    const Tensor* m = (base_mask.has_value() && base_mask->defined()) ? &*base_mask : nullptr;
+    Tensor out = restore_fwd_impl(y_flat, time_steps, cu_seqlens, dim, seqlen, out_dtype_opt, &bitmap, m, expand);
     return {out, bitmap};
 }
 
@@ -1185,8 +1211,7 @@ Tensor restore_dense_bwd_bitmap(const Tensor& dout, const Tensor& time_steps, co
 }
 
 // ------------------------------------------------------- block parameters ----
-// (the messages name the expected shape symbolically: an int64_t value in a
-// TORCH_CHECK message crashed the process with this torch build)
+// (the messages name the expected shape symbolically, see check_status)
 static void check_param(const Tensor& t, const char* name, int64_t n0, int64_t n1, const char* shape) {
     TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32 && t.is_contiguous(), "event_params: ", name,
                 " must be a contiguous float32 CUDA tensor");
@@ -1287,11 +1312,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "extract_base_events (bld: from the (B, L, d_model) layout) -> (6 outputs, max count as a host int)");
     m.def("extract_expanded_events", &extract_expanded_events, py::arg("x"), py::arg("threshold"),
           py::arg("expand"), py::arg("bld") = false, py::arg("x_conv") = py::none(),
-          py::arg("feature_thresholds") = py::none(),
+          py::arg("feature_thresholds") = py::none(), py::arg("keep_mask") = false,
           "extract_base_events then expand_base_events in one fill pass -> ((ch, t, k, cu, max[, x_flat]), "
           "max count as a host int); bld: from the (B, L, d_model) layout; x_conv (B, d_model*expand, L): "
           "also gather_events_fwd of it at the stream (x_flat); feature_thresholds (d_model) float32 with bld: "
-          "feature j fires above feature_thresholds[j] instead of threshold");
+          "feature j fires above feature_thresholds[j] instead of threshold; keep_mask: the buffer holding the "
+          "threshold mask is appended last (for restore_dense_fwd_bitmap(base_mask=))");
     m.def("extract_base_events_bld", &extract_base_events_bld_fwd, py::arg("x"), py::arg("threshold"),
           "extract_base_events from the (B, L, d_model) layout: same 6 outputs, no transposed copy");
     m.def("conv_events_fwd", &conv_events_fwd, py::arg("x"), py::arg("weight"), py::arg("bias"),
@@ -1318,8 +1344,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "One token of the event path for every channel (state updated in place) -> y (B, D)");
     m.def("restore_dense_fwd_bitmap", &restore_dense_fwd_bitmap, py::arg("y_flat"), py::arg("time_steps"),
           py::arg("cu_seqlens"), py::arg("dim"), py::arg("seqlen"), py::arg("out_dtype") = py::none(),
+          py::arg("base_mask") = py::none(), py::arg("expand") = 1,
           "restore_dense_fwd that also returns the event bitmap (the first B*ceil(L/32)*dim int32 words, "
-          "layout [B, ceil(L/32), dim]) and the sweep's start indices, consumed by restore_dense_bwd_bitmap");
+          "layout [B, ceil(L/32), dim]) and the sweep's start indices, consumed by restore_dense_bwd_bitmap; "
+          "base_mask (the mask buffer of extract_expanded_events(keep_mask=True) for this stream, dim = "
+          "d_model*expand, seqlen <= 4095): the bitmap is transposed from it instead of built from the events");
     m.def("restore_dense_bwd_bitmap", &restore_dense_bwd_bitmap, py::arg("dout"), py::arg("time_steps"),
           py::arg("cu_seqlens"), py::arg("bitmap"), py::arg("dim"), py::arg("seqlen"),
           "Backward of restore_dense_fwd from the forward's event bitmap; returns dy_flat (float32)");

@@ -170,11 +170,14 @@ class RestoreDenseFn(torch.autograd.Function):
     """Zero-order-hold restore: (E,) event values -> (B, L, D) dense."""
 
     @staticmethod
-    def forward(ctx, y_flat, time_steps_i32, cu_seqlens, dim: int, seqlen: int):
+    def forward(ctx, y_flat, time_steps_i32, cu_seqlens, dim: int, seqlen: int, base_mask=None, expand: int = 1):
         # the forward also writes the event bitmap (one bit per channel and
-        # position) that the backward sweeps instead of the event times
+        # position) that the backward sweeps instead of the event times;
+        # base_mask: the extraction's threshold mask of this stream, which the
+        # bitmap is transposed from instead
         with cuda_stage("dense_restoration_forward"):
-            out, bitmap = load_ops().restore_dense_fwd_bitmap(y_flat, time_steps_i32, cu_seqlens, dim, seqlen)
+            out, bitmap = load_ops().restore_dense_fwd_bitmap(y_flat, time_steps_i32, cu_seqlens, dim, seqlen,
+                                                              base_mask=base_mask, expand=expand)
         ctx.save_for_backward(time_steps_i32, cu_seqlens, bitmap)
         ctx.dim = dim
         ctx.seqlen = seqlen
@@ -186,11 +189,18 @@ class RestoreDenseFn(torch.autograd.Function):
         with cuda_stage("restore_backward"):
             dy = load_ops().restore_dense_bwd_bitmap(dout.contiguous(), time_steps_i32, cu_seqlens, bitmap,
                                                      ctx.dim, ctx.seqlen)
-        return dy, None, None, None, None
+        return dy, None, None, None, None, None, None
 
 
-def restore_dense_fn(y_flat, time_steps_i32, cu_seqlens, dim: int, seqlen: int):
-    return RestoreDenseFn.apply(y_flat, time_steps_i32, cu_seqlens, dim, seqlen)
+# the bitmap of the restore holds at most this many events per channel; up to
+# it the extraction's mask gives the same bitmap
+MASK_RESTORE_MAX_SEQLEN = 4095
+
+
+def restore_dense_fn(y_flat, time_steps_i32, cu_seqlens, dim: int, seqlen: int, base_mask=None, expand: int = 1):
+    """base_mask (optional): the mask buffer extract_events_1d(...,
+    return_mask=True) returned for this stream (seqlen <= 4095)."""
+    return RestoreDenseFn.apply(y_flat, time_steps_i32, cu_seqlens, dim, seqlen, base_mask, int(expand))
 
 
 class EventParamsFn(torch.autograd.Function):
@@ -292,7 +302,7 @@ class ExtractGatherFn(torch.autograd.Function):
     gather backward from the stream's rows."""
 
     @staticmethod
-    def forward(ctx, x_conv, spikes, threshold, expand, bld, max_out):
+    def forward(ctx, x_conv, spikes, threshold, expand, bld, max_out, keep_mask):
         x_c = x_conv.contiguous()
         # threshold: one float, or a tensor with one threshold per feature
         ft = threshold if isinstance(threshold, torch.Tensor) else None
@@ -300,24 +310,27 @@ class ExtractGatherFn(torch.autograd.Function):
             # the maximum count arrives on the host with the event total (one
             # synchronisation); expansion copies counts, so it is max_seqlen
             # of the expanded stream too
-            (ch, ts, kf, cu, _mx, x_flat), max_seqlen = load_ops().extract_expanded_events(
-                spikes, 0.0 if ft is not None else threshold, expand, bld=bld, x_conv=x_c, feature_thresholds=ft)
+            res, max_seqlen = load_ops().extract_expanded_events(
+                spikes, 0.0 if ft is not None else threshold, expand, bld=bld, x_conv=x_c, feature_thresholds=ft,
+                keep_mask=keep_mask)
+        ch, ts, kf, cu, _mx, x_flat = res[:6]
         max_out.append(int(max_seqlen))
         ctx.save_for_backward(ts, cu)
         ctx.shape = x_c.shape
-        ctx.mark_non_differentiable(ch, ts, kf, cu)
+        ctx.mark_non_differentiable(ch, ts, kf, cu, *res[6:])
         ctx.set_materialize_grads(False)
-        return x_flat, ch, ts, kf, cu
+        # keep_mask: also the buffer holding the threshold mask (restore_dense_fn's base_mask)
+        return (x_flat, ch, ts, kf, cu, res[6]) if keep_mask else (x_flat, ch, ts, kf, cu)
 
     @staticmethod
     def backward(ctx, grad_x, *_):
         if grad_x is None:
-            return (None,) * 6
+            return (None,) * 7
         ts, cu = ctx.saved_tensors
         B, D, L = ctx.shape
         with cuda_stage("gather_scatter_backward"):
             dx = load_ops().gather_events_bwd_rows(grad_x.contiguous(), ts, cu, B * D, L)
-        return dx.view(B, D, L), None, None, None, None, None
+        return dx.view(B, D, L), None, None, None, None, None, None
 
 
 def gather_events(x_conv, channel_ids_i32, time_steps_i32, cu_seqlens=None):
@@ -337,18 +350,20 @@ def extract_events_base(base_input, x_conv, threshold: float, expand: int):
     # base stream is never written)
     mx = []
     x_flat, ch, ts, kf, cu = ExtractGatherFn.apply(x_conv, base_input.contiguous(), float(threshold), int(expand),
-                                                   False, mx)
+                                                   False, mx, False)
     return ch, ts, kf, cu, mx[0], x_flat
 
 
-def extract_events_1d(hidden_states, x_conv, threshold, expand: int):
+def extract_events_1d(hidden_states, x_conv, threshold, expand: int, return_mask: bool = False):
     """Threshold (B, L, d_model) spikes into the expanded event stream and
     gather x_conv (B, D, L) at the events, like Mamba.extract_events_1d.
     `threshold` is a float as in the reference, or a contiguous float32
     (d_model,) tensor on the spikes' device: feature j fires above
     threshold[j].
 
-    Returns (channel_ids, time_steps, k_flat, cu_seqlens, max_seqlen, x_conv_flat).
+    Returns (channel_ids, time_steps, k_flat, cu_seqlens, max_seqlen, x_conv_flat), and with
+    return_mask=True also the buffer holding the threshold mask (for
+    restore_dense_fn's base_mask).
     """
     # straight from the (B, L, d_model) layout (the reference first makes a
     # transposed (B, d_model, L) copy, e_model.py:376); extraction, expansion
@@ -356,7 +371,10 @@ def extract_events_1d(hidden_states, x_conv, threshold, expand: int):
     # the event total (one synchronisation, no .item())
     mx = []
     thr = threshold if isinstance(threshold, torch.Tensor) else float(threshold)
-    x_flat, ch, ts, kf, cu = ExtractGatherFn.apply(x_conv, hidden_states.contiguous(), thr, int(expand), True, mx)
+    outs = ExtractGatherFn.apply(x_conv, hidden_states.contiguous(), thr, int(expand), True, mx, bool(return_mask))
+    x_flat, ch, ts, kf, cu = outs[:5]
+    if return_mask:
+        return ch, ts, kf, cu, mx[0], x_flat, outs[5]
     return ch, ts, kf, cu, mx[0], x_flat
 
 

@@ -63,10 +63,14 @@ def event_path(v, x_conv, threshold, expand: int, dt_idle, dt_active, A, W_B, W_
 
     B, L, _ = v.shape
     dim = x_conv.shape[1]
-    ch, ts, kf, cu, mx, u_flat = itf.extract_events_1d(v, x_conv, threshold, expand)
+    # up to 4095 positions the restore's event bitmap is the extraction's
+    # threshold mask transposed (no pass over the event times)
+    use_mask = L <= itf.MASK_RESTORE_MAX_SEQLEN
+    ch, ts, kf, cu, mx, u_flat, *mask = itf.extract_events_1d(v, x_conv, threshold, expand, return_mask=use_mask)
     y, _x = itf.selective_scan_flat_ch_fn(u_flat, kf, cu, mx, dt_idle, dt_active, A, W_B, W_C, D, None,
                                           is_depthwise_bc=True)
-    return itf.restore_dense_fn(y, ts, cu, dim, L), (int(ch.numel()), int(mx))
+    dense = itf.restore_dense_fn(y, ts, cu, dim, L, mask[0] if use_mask else None, expand)
+    return dense, (int(ch.numel()), int(mx))
 
 
 class _ProjAccum(torch.autograd.Function):

@@ -431,6 +431,22 @@ BCM_API bcm_status bcm_restore_dense_fwd_bitmap(const void* y_flat, bcm_dtype y_
                                  int64_t dim, int64_t seqlen,
                                  void* out, bcm_dtype out_dtype,
                                  uint32_t* event_bitmap, cudaStream_t stream);
+/* bcm_restore_dense_fwd_bitmap for a stream that bcm_extract_expanded[_ft]
+ * produced: the event bitmap is transposed from that call's threshold mask
+ * (the first words of its workspace, [B*d_model][ceil(seqlen/32)]) instead of
+ * being built from the event times; dim = d_model*expand.  base_mask must be
+ * the mask of the extraction that produced time_steps / cu_seqlens (a
+ * mismatch gives wrong values, not out-of-range reads).  seqlen <= 4095, the
+ * per-channel event limit of the bitmap; the same outputs as
+ * bcm_restore_dense_fwd_bitmap.  No reference binding. */
+BCM_API bcm_status bcm_restore_dense_fwd_mask(const void* y_flat, bcm_dtype y_dtype,
+                                 const int32_t* time_steps,
+                                 const int32_t* cu_seqlens,
+                                 int64_t n_events, int64_t n_channels,
+                                 int64_t dim, int64_t seqlen,
+                                 void* out, bcm_dtype out_dtype,
+                                 const uint32_t* base_mask, int64_t expand,
+                                 uint32_t* event_bitmap, cudaStream_t stream);
 BCM_API bcm_status bcm_restore_dense_bwd_bitmap(const void* dout, bcm_dtype dtype,
                                  const int32_t* time_steps,
                                  const int32_t* cu_seqlens,

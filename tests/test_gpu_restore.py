@@ -125,3 +125,39 @@ def test_restore_more_shapes(dim, L, rho, seed):
     t, cu = _random_stream(NC=2 * dim, L=L, rho=rho, seed=seed)
     _check(t, cu, dim, L)
     _check(t, cu, dim, L, torch.bfloat16, None, seed=seed)
+
+
+@pytest.mark.parametrize("B,dm,L,expand,thr", [(1, 1, 1, 1, 0.0), (2, 5, 31, 2, 0.3), (3, 40, 777, 2, 0.5),
+                                                (4, 96, 1000, 3, -0.5), (2, 128, 4000, 2, 1.28),
+                                                (2, 33, 4095, 2, 0.0)])
+def test_restore_from_extraction_mask(B, dm, L, expand, thr):
+    """restore_dense_fwd_bitmap(base_mask=) transposes the extraction's
+    threshold mask into the event bitmap: the same dense output, bitmap
+    buffer (words and sweep start indices) and backward as the bitmap built
+    from the event times; ragged shapes, dense and empty streams."""
+    ops = load_ops()
+    g = torch.Generator().manual_seed(B * 31 + dm + L)
+    x = torch.randn(B, L, dm, generator=g).to(dev)
+    res, _mx = ops.extract_expanded_events(x, thr, expand, bld=True, keep_mask=True)
+    ch, ts, kf, cu = res[:4]
+    mask = res[5]
+    D = dm * expand
+    y = torch.randn(ch.numel(), generator=g).to(dev)
+    out_e, bm_e = ops.restore_dense_fwd_bitmap(y, ts, cu, D, L)
+    out_m, bm_m = ops.restore_dense_fwd_bitmap(y, ts, cu, D, L, base_mask=mask, expand=expand)
+    assert torch.equal(out_m, out_e)
+    assert torch.equal(bm_m, bm_e)
+    dout = torch.randn(B, L, D, generator=g).to(dev)
+    assert torch.equal(ops.restore_dense_bwd_bitmap(dout, ts, cu, bm_m, D, L),
+                       ops.restore_dense_bwd_bitmap(dout, ts, cu, bm_e, D, L))
+
+
+def test_restore_from_extraction_mask_limits():
+    ops = load_ops()
+    x = torch.randn(1, 4096, 4, device=dev)
+    res, _mx = ops.extract_expanded_events(x, 0.0, 2, bld=True, keep_mask=True)
+    y = torch.randn(res[0].numel(), device=dev)
+    with pytest.raises(RuntimeError, match="seqlen above"):
+        ops.restore_dense_fwd_bitmap(y, res[1], res[3], 8, 4096, base_mask=res[5], expand=2)
+    with pytest.raises(RuntimeError, match="multiple of expand"):
+        ops.restore_dense_fwd_bitmap(y, res[1], res[3], 8, 4096, base_mask=res[5], expand=3)
