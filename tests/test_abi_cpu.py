@@ -115,3 +115,41 @@ def test_event_params_entry_points_and_cpu_errors():
         ops.event_params_fwd(A_log, W_BC, a, a, 1e-6)
     with pytest.raises(RuntimeError, match="A must be a contiguous float32 CUDA tensor"):
         ops.event_params_bwd(A_log, a, a, None, None, None, None, None)
+
+
+def test_argument_errors_without_gpu():
+    """The entry points added beside the reference's reject bad arguments
+    before any CUDA call: BCM_ERR_INVALID_ARGUMENT (1) and the reason in
+    bcm_last_error()."""
+    import ctypes
+
+    import bc_mamba_b200
+
+    lib = bc_mamba_b200.load_library()
+    lib.bcm_last_error.restype = ctypes.c_char_p
+    P, I, E = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+
+    f = lib.bcm_event_params_fwd
+    f.restype = E
+    f.argtypes = [P, P, P, P, I, I, ctypes.c_float] + [P] * 6
+    assert f(None, None, None, None, 0, 16, 1e-6, *([None] * 6)) == 1
+    assert b"event_params_fwd: bad sizes" in lib.bcm_last_error()
+
+    f = lib.bcm_event_params_bwd
+    f.restype = E
+    f.argtypes = [P] * 8 + [I, I] + [P] * 5
+    assert f(*([None] * 8), 4, 16, *([None] * 5)) == 1
+    assert b"event_params_bwd: null pointer" in lib.bcm_last_error()
+
+    f = lib.bcm_restore_dense_fwd_mask
+    f.restype = E
+    f.argtypes = [P, E, P, P, I, I, I, I, P, E, P, I, P, P]
+    assert f(None, 0, None, None, 10, 8, 8, 100, None, 0, None, 2, None, None) == 1
+    assert b"null event_bitmap or base_mask" in lib.bcm_last_error()
+
+    f = lib.bcm_extract_expanded_ft
+    f.restype = E
+    f.argtypes = [P, E, I, I, I, P, I, P, P, P, P, ctypes.c_size_t, I, P, P, P, P, P, E, P, P, P, P]
+    assert f(None, 0, 1, 4, 8, None, 2, None, None, None, None, 0, 0, None, None, None, None, None, 0,
+             None, None, None, None) == 1
+    assert b"null feature thresholds" in lib.bcm_last_error()
