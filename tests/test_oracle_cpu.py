@@ -142,3 +142,30 @@ def test_oracle_per_feature_thresholds():
     scal = ev.extract_base_events(x, 0.25)
     for a, b in zip(same, scal):
         assert np.array_equal(np.asarray(a), np.asarray(b))
+
+
+def test_restore_bitmap_is_the_extraction_mask_transposed():
+    """For a stream fresh from extraction and expansion, the restore's event
+    bitmap [B, ceil(L/32), D] is the threshold mask [B, d_model, ceil(L/32)]
+    transposed, logical channel b*D + d taking base feature d // expand's
+    words (what bcm_restore_dense_fwd_mask builds it from, up to 4095
+    positions)."""
+    import numpy as np
+
+    from oracle import events as ev
+    from oracle import restore as rs
+
+    rng = np.random.default_rng(4)
+    for B, dm, L, expand, thr in [(2, 5, 70, 3, 0.3), (1, 33, 64, 2, -0.2), (3, 4, 1, 1, 0.0)]:
+        x = rng.standard_normal((B, dm, L)).astype(np.float32)
+        bch, bt, bk, bcu, _, _ = ev.extract_base_events(x, thr)
+        ch, t, k, cu, mx = ev.expand_base_events(bch, bt, bk, bcu, B, dm, expand)
+        D = dm * expand
+        bm = rs.event_bitmap(t, cu, D, L)
+        nw = (L + 31) // 32
+        bits = np.zeros((B, dm, nw * 32), dtype=bool)
+        bits[:, :, :L] = x > np.float32(thr)
+        words = (bits.reshape(B, dm, nw, 32).astype(np.uint64) << np.arange(32, dtype=np.uint64)).sum(-1)
+        mask = words.astype(np.uint32)                               # [B, d_model, nw]
+        from_mask = np.repeat(mask.transpose(0, 2, 1), expand, axis=2)   # [B, nw, D]
+        assert np.array_equal(bm, from_mask)
